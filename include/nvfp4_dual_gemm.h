@@ -1,0 +1,156 @@
+/*
+ * nvfp4_dual_gemm.h — C ABI of the B200 (sm_100a) NVFP4 dual GEMM
+ *
+ *     C[m, n] = fp16( silu(sum_k A[m,k] * B1[n,k]) * (sum_k A[m,k] * B2[n,k]) )
+ *
+ * A, B1, B2 are NVFP4: e2m1 codes packed two per byte along K (element 2i in
+ * the low nibble, 2i+1 in the high nibble), K-major, with one fp8-e4m3 scale
+ * per 16 consecutive K elements.  The scales are passed in the tcgen05
+ * "blocked" layout: rows are grouped in blocks of 128 and K/16 scale columns
+ * in groups of 4; each (128-row, 4-column) block is one 512-byte atom, atoms
+ * ordered row-block major, and inside an atom the scale of (row r, column c)
+ * sits at byte (r % 32) * 16 + ((r % 128) / 32) * 4 + (c % 4).  This is the
+ * layout the reference kernel reads (nvfp4_dual_gemm.cu:226-243: atom index
+ * rowblock * (K/64) + kblock64, 512 bytes per atom).
+ *
+ * Buffer sizes the caller provides (L = 1):
+ *   A    : M * K/2 bytes        row m at A  + m * K/2
+ *   B1,B2: N * K/2 bytes        row n at B1 + n * K/2
+ *   SFA  : ceil(M/128) * (K/64) * 512 bytes   (blocked, rows padded to 128)
+ *   SFB1, SFB2: ceil(N/128) * (K/64) * 512 bytes
+ *   C    : M * N fp16, row-major (row m at C + m * N)
+ *
+ * Preconditions (checked, an error code is returned otherwise):
+ *   M >= 0, N >= 0, K >= 0; N % 64 == 0; K % 256 == 0; L == 1;
+ *   A, B1, B2, SFA, SFB1, SFB2, C 16-byte aligned.
+ * M needs no alignment: rows past M are read as zeros and never written.
+ *
+ * All pointers are device pointers owned by the caller.  `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  No entry
+ * point calls exit(); failures return a non-zero status and the message is
+ * available from nvfp4_dual_gemm_last_error() (thread-local).
+ */
+#ifndef NVFP4_DUAL_GEMM_H_
+#define NVFP4_DUAL_GEMM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define NVFP4DG_API __attribute__((visibility("default")))
+#else
+#define NVFP4DG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define NVFP4DG_OK 0
+#define NVFP4DG_ERR_INVALID 1     /* bad shape / null pointer / L != 1      */
+#define NVFP4DG_ERR_ALIGN 2       /* pointer not 16-byte aligned            */
+#define NVFP4DG_ERR_WORKSPACE 3   /* workspace missing or too small         */
+#define NVFP4DG_ERR_CUDA 4        /* CUDA runtime / driver call failed      */
+#define NVFP4DG_ERR_DEVICE 5      /* a kernel reported a bounded-wait timeout */
+#define NVFP4DG_ERR_UNSUPPORTED 6 /* device is not sm_100 or entry missing  */
+
+/* `flags` bits for nvfp4_dual_gemm_run / _run_ws (0 = automatic choice).    */
+#define NVFP4DG_FLAG_GRID_MASK 0xFFFu  /* bits 0-11: force the persistent grid */
+#define NVFP4DG_FLAG_BN64 (1u << 12)   /* force 64-column tiles per GEMM        */
+#define NVFP4DG_FLAG_BN128 (1u << 13)  /* force 128-column tiles per GEMM       */
+#define NVFP4DG_FLAG_NO_STREAMK (1u << 14) /* whole tiles only (no K split)     */
+#define NVFP4DG_FLAG_SYNC_CHECK (1u << 15) /* synchronize and read the device
+                                              error word after the launch       */
+#define NVFP4DG_FLAG_SPLIT_MMA (1u << 16) /* BN=128: two N=128 MMAs per K step
+                                             instead of one N=256 MMA           */
+
+/*
+ * Run the dual GEMM on `stream` using a workspace the library keeps per
+ * (device, stream); it is allocated (cudaMalloc) on the first call that needs
+ * it and reused afterwards.
+ *
+ * Replaces the reference's torch-extension entry
+ *   torch::Tensor cuda_nvfp4_dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C)
+ *   (nvfp4_dual_gemm.cu:381-446, declared submission.py:17-20),
+ * which derives M = A.size(0), N = B1.size(0), K = 2 * A.size(1) and launches
+ * on the legacy default stream.  Unlike the reference, shapes are not limited
+ * to a fixed table, and invalid shapes fail instead of returning C untouched
+ * (nvfp4_dual_gemm.cu:443-444).
+ */
+NVFP4DG_API int nvfp4_dual_gemm_run(const void* A, const void* B1, const void* B2,
+                        const void* SFA, const void* SFB1, const void* SFB2,
+                        void* C, int M, int N, int K, int L, unsigned flags,
+                        void* stream);
+
+/*
+ * Bytes of workspace nvfp4_dual_gemm_run_ws needs for this problem and flags
+ * on the current device (0 when the chosen schedule splits no tile along K).
+ * Has no counterpart in the reference, whose kernel never splits K.
+ */
+NVFP4DG_API size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
+                                      unsigned flags);
+
+/*
+ * Same as nvfp4_dual_gemm_run with a caller-owned workspace of at least
+ * nvfp4_dual_gemm_workspace_size() bytes (256-byte aligned).  The workspace
+ * must be zero-filled before its first use; every successful call leaves it
+ * ready for the next one.  Calls that overlap on the GPU must not share a
+ * workspace.  Same reference interface as nvfp4_dual_gemm_run.
+ */
+NVFP4DG_API int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void* B2,
+                           const void* SFA, const void* SFB1, const void* SFB2,
+                           void* C, int M, int N, int K, int L, unsigned flags,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/*
+ * Quantise fp32 rows to NVFP4 on the GPU: X is [rows, K] fp32 row-major;
+ * writes codes [rows, K/2] (low nibble = even element), the plain scales
+ * [rows, K/16] and the blocked scales (ceil(rows/128) * (K/64) * 512 bytes;
+ * padding rows are written as zero).  Scale = e4m3(amax/6), round to nearest
+ * even, saturating at 448; codes = e2m1(x / scale), round to nearest even,
+ * saturating at 6; a block whose scale rounds to 0 gets all-zero codes.
+ * `sf_plain` may be NULL.  K % 64 == 0.
+ * Produces the `data` tuple fields the reference's harness supplies
+ * (submission.py:1154: a/b1/b2, sfa/sfb1/sfb2 and the *_blocked copies).
+ */
+NVFP4DG_API int nvfp4_quantize(const float* X, int rows, int K, void* codes,
+                   void* sf_plain, void* sf_blocked, void* stream);
+
+/*
+ * Read and clear the device error word of `device` (synchronizes that
+ * device).  *word_out = 0 when no kernel reported a timeout; otherwise bits
+ * identify the role whose bounded wait expired.  Returns a status code.
+ */
+NVFP4DG_API int nvfp4_dual_gemm_device_status(int device, unsigned* word_out);
+
+/*
+ * Describe the schedule the library would use: writes the tile width per
+ * GEMM, persistent grid size, whole-tile count and the number of tiles split
+ * along K.  Host-only; usable without a GPU when `num_sms` > 0.
+ */
+NVFP4DG_API int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
+                         int* bn_out, int* grid_out, int* dp_tiles_out,
+                         int* sk_tiles_out);
+
+/*
+ * Enumerate the work of CTA `cta` under the plan for (M, N, K, flags,
+ * num_sms): writes up to `cap` records of 4 ints (tile, kb_begin, kb_end,
+ * slot; slot = -1 for a whole tile) and returns the record count, or -1 on
+ * error.  Host-only mirror of the device scheduler, for tests and tooling.
+ */
+NVFP4DG_API int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, int num_sms,
+                              int cta, int* records, int cap);
+
+/* Thread-local message describing the last failure ("" if none). */
+NVFP4DG_API const char* nvfp4_dual_gemm_last_error(void);
+
+/* ABI version: major * 100 + minor. */
+NVFP4DG_API int nvfp4_dual_gemm_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_DUAL_GEMM_H_ */

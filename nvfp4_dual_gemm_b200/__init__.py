@@ -1,0 +1,26 @@
+"""B200-native (sm_100a) NVFP4 dual GEMM: C = silu(A B1^T) * (A B2^T).
+
+Drop-in for the reference's ``custom_kernel(data)`` path; the compute runs in
+the in-tree CUDA library ``libnvfp4dg.so`` behind the C ABI declared in
+``include/nvfp4_dual_gemm.h``.
+"""
+from .api import (  # noqa: F401
+    cuda_nvfp4_dual_gemm,
+    custom_kernel,
+    dual_gemm,
+    generate_input,
+    plan,
+    plan_work,
+    quantize_nvfp4,
+    workspace_size,
+)
+from ._lib import (  # noqa: F401
+    FLAG_BN64,
+    FLAG_BN128,
+    FLAG_NO_STREAMK,
+    FLAG_SPLIT_MMA,
+    FLAG_SYNC_CHECK,
+    NativeLibraryError,
+)
+
+__version__ = "1.0.0"

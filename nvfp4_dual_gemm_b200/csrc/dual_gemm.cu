@@ -1,0 +1,985 @@
+// dual_gemm.cu — B200 (sm_100a) NVFP4 dual GEMM  C = silu(A B1^T) * (A B2^T)
+//
+// One persistent, warp-specialised kernel per tile width BN (64 or 128
+// columns of each GEMM), 192 threads per CTA, one CTA per SM:
+//   warp 4    TMA producer: per 256-wide K block streams the A tile
+//             (128 x 128 B), the B1 and B2 tiles (BN x 128 B each, stacked so
+//             that together they form one 2*BN-row operand) and the three
+//             2 KiB block-scale runs through a ring of shared-memory stages;
+//   warp 5    TMEM owner and MMA issuer: copies the scales of each stage into
+//             a per-stage TMEM region (tcgen05.cp) and issues
+//             tcgen05.mma kind::mxf4nvf4 block_scale into one TMEM
+//             accumulator of 2*BN fp32 columns (d1 | d2).  With BN = 128 a
+//             single N = 256 MMA per K step computes both GEMMs from one read
+//             of the A tile; with BN = 64 two N = 64 MMAs share it;
+//   warps 0-3 epilogue: tcgen05.ld of d1 and d2, silu(d1) * d2 in fp32,
+//             fp16 row stores; for tiles split along K the fp32 partials go
+//             through the workspace and the last segment to arrive finishes.
+// The reference kernel is non-persistent with one tile per CTA
+// (nvfp4_dual_gemm.cu:77-317); the scheduling here is in schedule.h.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "nvfp4_dual_gemm.h"
+#include "schedule.h"
+#include "sm100_ptx.cuh"
+
+namespace nvfp4dg {
+
+constexpr int kBM = 128;            // tile rows (TMEM lanes)
+constexpr int kRowBytes = 128;      // one stage = 256 fp4 of K = 128 bytes/row
+constexpr int kSfAtomBytes = 512;   // 128 rows x 4 scales
+constexpr int kSfRunBytes = 2048;   // 4 atoms = the scales of 256 K elements
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kSfTmemBase = 256;    // scale regions follow the accumulator
+constexpr int kSfTmemPerStage = 48; // SFA 4 x 4 cols, SFB 4 x (4 + 4) cols
+
+// Device error word bits (role whose bounded wait expired).
+constexpr unsigned kErrProducer = 1u << 0;
+constexpr unsigned kErrMma = 1u << 1;
+constexpr unsigned kErrEpilogue = 1u << 2;
+constexpr unsigned kErrDrain = 1u << 3;
+
+template <int BN>
+struct Cfg {
+  static constexpr int kStages = (BN == 128) ? 4 : 5;
+  static constexpr int kABytes = kBM * kRowBytes;
+  static constexpr int kBBytes = BN * kRowBytes;
+  static constexpr int kStageBytes = kABytes + 2 * kBBytes + 3 * kSfRunBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-B aligned");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kSfTmemBase + kStages * kSfTmemPerStage <= kTmemCols,
+                "TMEM budget");
+  static_assert(2 * BN <= kSfTmemBase, "accumulator must fit below scales");
+};
+
+struct KParams {
+  Plan plan;
+  int M, N, K;
+  const uint8_t* sfa;
+  const uint8_t* sfb1;
+  const uint8_t* sfb2;
+  __half* C;
+  float* partials;
+  int* counters;
+  unsigned* err;
+};
+
+__device__ unsigned g_err_word;
+
+__device__ __forceinline__ void epi_bar() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ float silu_mul(float x, float y) {
+  return __fdividef(x, 1.0f + __expf(-x)) * y;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// 32 outputs of one row -> 64 contiguous bytes of C.
+__device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
+                                            const float (&y)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 v;
+    v.x = pack_half2(silu_mul(x[8 * q + 0], y[8 * q + 0]),
+                     silu_mul(x[8 * q + 1], y[8 * q + 1]));
+    v.y = pack_half2(silu_mul(x[8 * q + 2], y[8 * q + 2]),
+                     silu_mul(x[8 * q + 3], y[8 * q + 3]));
+    v.z = pack_half2(silu_mul(x[8 * q + 4], y[8 * q + 4]),
+                     silu_mul(x[8 * q + 5], y[8 * q + 5]));
+    v.w = pack_half2(silu_mul(x[8 * q + 6], y[8 * q + 6]),
+                     silu_mul(x[8 * q + 7], y[8 * q + 7]));
+    d[q] = v;
+  }
+}
+
+__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    __stcg(d + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
+                              v[4 * q + 3]));
+}
+
+__device__ __forceinline__ void add_f32x32(float (&v)[32], const float* src) {
+  const float4* s = reinterpret_cast<const float4*>(src);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 t = __ldcg(s + q);
+    v[4 * q] += t.x;
+    v[4 * q + 1] += t.y;
+    v[4 * q + 2] += t.z;
+    v[4 * q + 3] += t.w;
+  }
+}
+
+// FUSE (BN = 128 only): one N = 256 MMA per K step over the stacked B1|B2
+// operand, reading the 8 TMEM scale columns of B1's and B2's atoms side by
+// side.  Without FUSE: two MMAs with N = BN per K step; the first keeps the A
+// tile in the collector and the second reuses it.
+template <int BN, bool FUSE>
+__global__ void __launch_bounds__(kThreads, 1)
+    dual_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB1,
+                     const __grid_constant__ CUtensorMap tmB2,
+                     const KParams p) {
+  using Cf = Cfg<BN>;
+  constexpr int S = Cf::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t acc_full_bar;
+  __shared__ __align__(8) uint64_t acc_empty_bar;
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int finisher_sh;
+
+  // Operand tiles use the 128-byte swizzle, whose pattern repeats every
+  // 1024 bytes: align the ring to 1024 in the shared window.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const Plan& plan = p.plan;
+
+  if (warp == 4 && lane == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&acc_full_bar, 1);
+    mbar_init(&acc_empty_bar, 128);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB1);
+    prefetch_tmap(&tmB2);
+  }
+  if (warp == 5) {
+    tmem_alloc(&tmem_base_sh, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int kblk64 = p.K / 64;  // scale atoms per 128-row block
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      WorkIter it;
+      work_begin(plan, blockIdx.x, it);
+      Work w;
+      while (ok && work_next(plan, it, w)) {
+        const int m_tile = w.tile % plan.m_tiles;
+        const int n_tile = w.tile / plan.m_tiles;
+        const int row_a = m_tile * kBM;
+        const int row_b = n_tile * BN;
+        const uint8_t* sfa = p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
+        const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
+        const uint8_t* sfb1 = p.sfb1 + sfb_off;
+        const uint8_t* sfb2 = p.sfb2 + sfb_off;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + stage * Cf::kStageBytes;
+          uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
+          mbar_arrive_expect_tx(&full_bar[stage], Cf::kStageBytes);
+          tma_load_2d(st, &tmA, &full_bar[stage], kb * kRowBytes, row_a, pol_a);
+          tma_load_2d(st + Cf::kABytes, &tmB1, &full_bar[stage],
+                      kb * kRowBytes, row_b, pol_b);
+          tma_load_2d(st + Cf::kABytes + Cf::kBBytes, &tmB2, &full_bar[stage],
+                      kb * kRowBytes, row_b, pol_b);
+          bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
+                    &full_bar[stage], pol_a);
+          bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
+                    kSfRunBytes, &full_bar[stage], pol_b);
+          bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
+                    kSfRunBytes, &full_bar[stage], pol_b);
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave with copies in flight: wait (bounded) until the last
+      // load issued into each stage has landed.
+      for (int s = 0; s < S; ++s) {
+        if (issued > s) {
+          const long long fill = (issued - 1 - s) / S;
+          mbar_wait(&full_bar[s], static_cast<uint32_t>(fill & 1), p.err,
+                    kErrDrain, /*bail_on_err=*/false);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdesc =
+          FUSE ? idesc_nvf4(128, 2 * BN) : idesc_nvf4(128, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      WorkIter it;
+      work_begin(plan, blockIdx.x, it);
+      Work w;
+      while (ok && work_next(plan, it, w)) {
+        const int n_tile = w.tile / plan.m_tiles;
+        // BN = 64: the tile is one half of a 128-row scale atom; its scales
+        // sit in atom columns 0-1 (upper half: 2-3) of the copied block.
+        const uint32_t sfb_half = (BN == 64) ? (uint32_t)(n_tile & 1) * 2u : 0u;
+        if (!mbar_wait(&acc_empty_bar, acc_phase ^ 1u, p.err, kErrMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
+          const uint32_t b_addr = a_addr + Cf::kABytes;
+          const uint32_t sf_addr = b_addr + 2 * Cf::kBBytes;
+          const uint32_t sf_t = tmem + kSfTmemBase + stage * kSfTmemPerStage;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t sfa_t = sf_t + 4 * j;
+            const uint32_t sfb_t = sf_t + 16 + 8 * j;
+            tc_cp_32x128b_x4(sfa_t, smem_desc(sf_addr + j * kSfAtomBytes, 128,
+                                              128, SmemLayout::kNone));
+            tc_cp_32x128b_x4(sfb_t,
+                             smem_desc(sf_addr + kSfRunBytes + j * kSfAtomBytes,
+                                       128, 128, SmemLayout::kNone));
+            tc_cp_32x128b_x4(
+                sfb_t + 4, smem_desc(sf_addr + 2 * kSfRunBytes + j * kSfAtomBytes,
+                                     128, 128, SmemLayout::kNone));
+            const uint32_t accum = (kb > w.kb0 || j > 0) ? 1u : 0u;
+            const uint64_t a_desc = smem_desc(a_addr + 32 * j, 16, 1024,
+                                              SmemLayout::kSwizzle128B);
+            if constexpr (FUSE) {
+              const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
+                                                SmemLayout::kSwizzle128B);
+              tc_mma_nvf4(tmem, a_desc, b_desc, kIdesc, sfa_t, sfb_t, accum);
+            } else {
+              const uint64_t b1_desc = smem_desc(b_addr + 32 * j, 16, 1024,
+                                                 SmemLayout::kSwizzle128B);
+              const uint64_t b2_desc =
+                  smem_desc(b_addr + Cf::kBBytes + 32 * j, 16, 1024,
+                            SmemLayout::kSwizzle128B);
+              tc_mma_nvf4<kCollFill>(tmem, a_desc, b1_desc, kIdesc, sfa_t,
+                                     sfb_t + sfb_half, accum);
+              tc_mma_nvf4<kCollLastUse>(tmem + BN, a_desc, b2_desc, kIdesc,
+                                        sfa_t, sfb_t + 4 + sfb_half, accum);
+            }
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full_bar);
+        acc_phase ^= 1u;
+      }
+      // No MMA or scale copy may still be running when TMEM is released.
+      tc_commit(&drain_bar);
+      mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int row = threadIdx.x;  // TMEM lane == tile row
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    uint32_t acc_phase = 0;
+    WorkIter it;
+    work_begin(plan, blockIdx.x, it);
+    Work w;
+    while (work_next(plan, it, w)) {
+      const bool got = mbar_wait(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int m_tile = w.tile % plan.m_tiles;
+      const int n_tile = w.tile / plan.m_tiles;
+      const int grow = m_tile * kBM + row;
+      const bool row_ok = grow < p.M;
+      __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+      if (w.slot < 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32], y[32];
+          __syncwarp();
+          tc_ld_32cols(t_row + 32 * c, x);
+          tc_ld_32cols(t_row + BN + 32 * c, y);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&acc_empty_bar);
+          }
+          if (row_ok) store_row32(crow + 32 * c, x, y);
+        }
+      } else {
+        float* mine = p.partials + (size_t)w.slot * partial_slot_floats(plan) +
+                      (size_t)row * 2 * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32], y[32];
+          __syncwarp();
+          tc_ld_32cols(t_row + 32 * c, x);
+          tc_ld_32cols(t_row + BN + 32 * c, y);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&acc_empty_bar);
+          }
+          store_f32x32(mine + 32 * c, x);
+          store_f32x32(mine + BN + 32 * c, y);
+        }
+        __threadfence();
+        epi_bar();
+        const long long ts = w.tile - plan.dp_tiles;
+        int b_first, b_last;
+        sk_tile_owners(plan, ts, &b_first, &b_last);
+        if (threadIdx.x == 0) {
+          const int old = atomicAdd(&p.counters[ts], 1);
+          const int last = (old == b_last - b_first) ? 1 : 0;
+          if (last) p.counters[ts] = 0;  // ready for the next launch
+          finisher_sh = last;
+        }
+        epi_bar();
+        if (finisher_sh) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float x[32], y[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              x[i] = 0.f;
+              y[i] = 0.f;
+            }
+            for (int b = b_first; b <= b_last; ++b) {
+              const float* src = p.partials +
+                                 (size_t)sk_slot(plan, b, ts) *
+                                     partial_slot_floats(plan) +
+                                 (size_t)row * 2 * BN;
+              add_f32x32(x, src + 32 * c);
+              add_f32x32(y, src + BN + 32 * c);
+            }
+            if (row_ok) store_row32(crow + 32 * c, x, y);
+          }
+        }
+      }
+      acc_phase ^= 1u;
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ===========================================================================
+// NVFP4 quantiser (fp32 rows -> e2m1 codes + e4m3 block scales)
+// ===========================================================================
+// Eight fp32 values -> four bytes of e2m1 pairs (round to nearest even,
+// saturating at +-6).  cvt...e2m1x2 puts its first source operand in the high
+// nibble, so the odd element goes first and element 2i lands in the low nibble.
+__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 q2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 q3, %8, %7;\n\t"
+      "mov.b32 %0, {q0, q1, q2, q3};\n\t}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]),
+        "f"(v[6]), "f"(v[7]));
+  return r;
+}
+
+__global__ void quantize_kernel(const float* __restrict__ X, int rows, int K,
+                                uint8_t* __restrict__ codes,
+                                uint8_t* __restrict__ sf_plain,
+                                uint8_t* __restrict__ sf_blocked) {
+  const int kb16 = K / 16;
+  const long long nblk = static_cast<long long>(rows) * kb16;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nblk;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / kb16);
+    const int j = static_cast<int>(i - (long long)r * kb16);
+    const float4* src =
+        reinterpret_cast<const float4*>(X + (size_t)r * K + (size_t)j * 16);
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 t = src[q];
+      v[4 * q] = t.x;
+      v[4 * q + 1] = t.y;
+      v[4 * q + 2] = t.z;
+      v[4 * q + 3] = t.w;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) amax = fmaxf(amax, fabsf(v[q]));
+    const __nv_fp8_storage_t sb =
+        __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+    const __half_raw hr = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
+    const float sd = __half2float(__half(hr));
+    uint32_t w0 = 0, w1 = 0;
+    if (sd > 0.f) {
+      float q[16];
+#pragma unroll
+      for (int t = 0; t < 16; ++t) q[t] = v[t] / sd;
+      w0 = e2m1x8(q);
+      w1 = e2m1x8(q + 8);
+    }
+    *reinterpret_cast<uint2*>(codes + (size_t)r * (K / 2) + (size_t)j * 8) =
+        make_uint2(w0, w1);
+    if (sf_plain) sf_plain[(size_t)r * kb16 + j] = sb;
+    const size_t atom = (size_t)(r / 128) * (K / 64) + (j / 4);
+    sf_blocked[atom * kSfAtomBytes + (r % 32) * 16 + ((r % 128) / 32) * 4 +
+               (j % 4)] = sb;
+  }
+}
+
+}  // namespace nvfp4dg
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+namespace {
+
+using namespace nvfp4dg;
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(NVFP4DG_ERR_CUDA,
+              std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
+                                   void*, const cuuint64_t*, const cuuint64_t*,
+                                   const cuuint32_t*, const cuuint32_t*,
+                                   CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+std::mutex g_mu;
+EncodeTiledFn g_encode = nullptr;
+
+struct DevInfo {
+  bool init = false;
+  int sms = 0;
+  int major = 0;
+  int minor = 0;
+  bool attr64 = false;
+  bool attr128 = false;
+  bool attr128f = false;
+  unsigned* err = nullptr;
+};
+std::map<int, DevInfo> g_dev;
+
+struct MapKey {
+  const void* ptr;
+  long long rows;
+  long long row_bytes;
+  int box_rows;
+  int dev;
+  bool operator<(const MapKey& o) const {
+    if (ptr != o.ptr) return ptr < o.ptr;
+    if (rows != o.rows) return rows < o.rows;
+    if (row_bytes != o.row_bytes) return row_bytes < o.row_bytes;
+    if (box_rows != o.box_rows) return box_rows < o.box_rows;
+    return dev < o.dev;
+  }
+};
+std::map<MapKey, CUtensorMap> g_maps;
+
+struct WsEntry {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, void*>, WsEntry> g_ws;
+
+int get_encode() {
+  if (g_encode) return NVFP4DG_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn,
+                                          cudaEnableDefault, &q);
+  if (e != cudaSuccess || fn == nullptr || q != cudaDriverEntryPointSuccess)
+    return fail(NVFP4DG_ERR_CUDA, "cuTensorMapEncodeTiled not available");
+  g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  return NVFP4DG_OK;
+}
+
+int device_info(int dev, DevInfo** out) {
+  DevInfo& d = g_dev[dev];
+  if (!d.init) {
+    cudaError_t e;
+    if ((e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount,
+                                    dev)) != cudaSuccess)
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (d.major != 10)
+      return fail(NVFP4DG_ERR_UNSUPPORTED,
+                  "device is not sm_100 (compute capability " +
+                      std::to_string(d.major) + "." + std::to_string(d.minor) +
+                      ")");
+    void* ptr = nullptr;
+    if ((e = cudaGetSymbolAddress(&ptr, g_err_word)) != cudaSuccess)
+      return cuda_fail(e, "cudaGetSymbolAddress(error word)");
+    d.err = static_cast<unsigned*>(ptr);
+    d.init = true;
+  }
+  *out = &d;
+  return NVFP4DG_OK;
+}
+
+int tensor_map(const void* ptr, long long rows, long long row_bytes,
+               int box_rows, int dev, CUtensorMap* out) {
+  MapKey key{ptr, rows, row_bytes, box_rows, dev};
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return NVFP4DG_OK;
+  }
+  int rc = get_encode();
+  if (rc) return rc;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes),
+                              static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytes),
+                             static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4DG_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) +
+                    ")");
+  if (g_maps.size() > 256) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return NVFP4DG_OK;
+}
+
+// ---------------------------------------------------------------- planning
+// Cost model (cycles of the busiest CTA) used to choose the tile width and
+// whether to split tiles along K.  Per 256-wide K block an SM issues 4 K
+// steps; the FP4 tensor pipe retires an M=128 x N=256 x K=64 MMA in ~128
+// cycles, so BN = 128 costs ~512 cycles per block and BN = 64 (two N = 64
+// MMAs) ~256.  A split tile costs its partial round trip through L2 at
+// ~64 B/cycle per SM.
+Plan plan_for(int M, int N, int K, int bn, int grid_cap, bool streamk) {
+  Plan p{};
+  p.bn = bn;
+  p.m_tiles = (M + kBM - 1) / kBM;
+  p.n_tiles = N / bn;
+  p.kblocks = K / 256;
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  const int T = p.num_tiles;
+  if (!streamk || T % grid_cap == 0) {
+    p.grid = std::min(T, grid_cap);
+    p.dp_tiles = T;
+    p.sk_iters = 0;
+    return p;
+  }
+  const int waves = T / grid_cap;
+  p.dp_tiles = waves >= 2 ? (waves - 1) * grid_cap : 0;
+  const long long sk_total = (long long)(T - p.dp_tiles) * p.kblocks;
+  p.grid = (int)std::min<long long>(grid_cap, sk_total);
+  if (p.dp_tiles > 0 && p.grid < grid_cap) p.grid = grid_cap;
+  p.sk_iters = sk_total;
+  if (p.sk_iters > 0 && p.sk_iters < p.grid) p.grid = (int)p.sk_iters;
+  return p;
+}
+
+double plan_cost(const Plan& p) {
+  const double per_block = (p.bn == 128) ? 512.0 : 256.0;
+  const double slot_bytes = 128.0 * 2 * p.bn * 4;
+  double iters = 0;
+  if (p.dp_tiles > 0)
+    iters += (double)((p.dp_tiles + p.grid - 1) / p.grid) * p.kblocks;
+  double partial = 0;
+  if (p.sk_iters > 0) {
+    const double per_cta = (double)((p.sk_iters + p.grid - 1) / p.grid);
+    iters += per_cta;
+    // every split tile writes and re-reads ~(segments) partials; charge the
+    // busiest CTA two writes and one finishing read of ~3 segments.
+    if (per_cta < p.kblocks || (p.sk_iters % p.kblocks) != 0 ||
+        (p.sk_iters / p.grid) % p.kblocks != 0)
+      partial = (2.0 + 3.0) * slot_bytes / 64.0;
+  }
+  return iters * per_block + partial + 2000.0;
+}
+
+Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
+  const int forced = static_cast<int>(flags & NVFP4DG_FLAG_GRID_MASK);
+  const int cap = forced > 0 ? forced : sms;
+  const bool streamk = (flags & NVFP4DG_FLAG_NO_STREAMK) == 0;
+  int bns[2];
+  int nb = 0;
+  if (flags & NVFP4DG_FLAG_BN64) {
+    bns[nb++] = 64;
+  } else if (flags & NVFP4DG_FLAG_BN128) {
+    bns[nb++] = 128;
+  } else {
+    if (N % 128 == 0) bns[nb++] = 128;
+    bns[nb++] = 64;
+  }
+  Plan best{};
+  double best_cost = 1e300;
+  for (int i = 0; i < nb; ++i) {
+    for (int sk = 0; sk < (streamk ? 2 : 1); ++sk) {
+      Plan p = plan_for(M, N, K, bns[i], cap, sk == 1);
+      const double c = plan_cost(p);
+      if (c < best_cost) {
+        best_cost = c;
+        best = p;
+      }
+    }
+  }
+  return best;
+}
+
+int check_problem(const void* A, const void* B1, const void* B2,
+                  const void* SFA, const void* SFB1, const void* SFB2,
+                  const void* C, int M, int N, int K, int L, unsigned flags) {
+  if (M < 0 || N < 0 || K < 0)
+    return fail(NVFP4DG_ERR_INVALID, "M, N, K must be non-negative");
+  if (L != 1)
+    return fail(NVFP4DG_ERR_INVALID,
+                "L must be 1 (batched problems are not supported)");
+  if (N % 64 != 0)
+    return fail(NVFP4DG_ERR_INVALID, "N must be a multiple of 64");
+  if (K % 256 != 0)
+    return fail(NVFP4DG_ERR_INVALID, "K must be a multiple of 256");
+  if ((flags & NVFP4DG_FLAG_BN128) && N % 128 != 0)
+    return fail(NVFP4DG_ERR_INVALID, "BN=128 forced but N % 128 != 0");
+  if ((flags & NVFP4DG_FLAG_BN64) && (flags & NVFP4DG_FLAG_BN128))
+    return fail(NVFP4DG_ERR_INVALID, "BN64 and BN128 flags are exclusive");
+  if (M == 0 || N == 0) return NVFP4DG_OK;
+  const void* ptrs[7] = {A, B1, B2, SFA, SFB1, SFB2, C};
+  const char* names[7] = {"A", "B1", "B2", "SFA", "SFB1", "SFB2", "C"};
+  for (int i = 0; i < 7; ++i) {
+    if (K == 0 && i < 6) continue;
+    if (ptrs[i] == nullptr)
+      return fail(NVFP4DG_ERR_INVALID, std::string(names[i]) + " is NULL");
+    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
+      return fail(NVFP4DG_ERR_ALIGN,
+                  std::string(names[i]) + " is not 16-byte aligned");
+  }
+  return NVFP4DG_OK;
+}
+
+template <int BN, bool FUSE>
+int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
+           const void* B1, const void* B2, const void* SFA, const void* SFB1,
+           const void* SFB2, void* C, int M, int N, int K, void* ws,
+           cudaStream_t stream) {
+  using Cf = Cfg<BN>;
+  bool& attr = (BN == 64) ? dev.attr64 : (FUSE ? dev.attr128f : dev.attr128);
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(
+        dual_gemm_kernel<BN, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        Cf::kSmemBytes);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+    attr = true;
+  }
+  CUtensorMap ta, tb1, tb2;
+  int rc;
+  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta))) return rc;
+  if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1))) return rc;
+  if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2))) return rc;
+  KParams kp;
+  kp.plan = plan;
+  kp.M = M;
+  kp.N = N;
+  kp.K = K;
+  kp.sfa = static_cast<const uint8_t*>(SFA);
+  kp.sfb1 = static_cast<const uint8_t*>(SFB1);
+  kp.sfb2 = static_cast<const uint8_t*>(SFB2);
+  kp.C = static_cast<__half*>(C);
+  kp.partials = static_cast<float*>(ws);
+  kp.counters = ws ? reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
+                                            workspace_counter_offset(plan))
+                   : nullptr;
+  kp.err = dev.err;
+  dual_gemm_kernel<BN, FUSE><<<plan.grid, kThreads, Cf::kSmemBytes, stream>>>(
+      ta, tb1, tb2, kp);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "dual_gemm_kernel launch");
+  return NVFP4DG_OK;
+}
+
+int read_status(int dev, unsigned* word) {
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaError_t e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  DevInfo* d = nullptr;
+  int rc = device_info(dev, &d);
+  if (rc == NVFP4DG_OK) {
+    unsigned v = 0;
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_err_word, sizeof(v));
+    const unsigned zero = 0;
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_err_word, &zero, sizeof(zero));
+    if (e != cudaSuccess) rc = cuda_fail(e, "reading the device error word");
+    *word = v;
+  }
+  cudaSetDevice(prev);
+  return rc;
+}
+
+int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
+             const void* SFB1, const void* SFB2, void* C, int M, int N, int K,
+             int L, unsigned flags, void* ws, size_t ws_bytes, bool own_ws,
+             void* stream_ptr) {
+  g_last_error.clear();
+  int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return NVFP4DG_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (K == 0) {  // empty sums: silu(0) * 0 = 0
+    cudaError_t e =
+        cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
+    return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "cudaMemsetAsync");
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  int devid = 0;
+  cudaError_t e = cudaGetDevice(&devid);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DevInfo* dev = nullptr;
+  if ((rc = device_info(devid, &dev))) return rc;
+  const Plan plan = choose_plan(M, N, K, flags, dev->sms);
+  const size_t need = static_cast<size_t>(workspace_bytes(plan));
+  if (own_ws && need > 0) {
+    WsEntry& ent = g_ws[{devid, stream_ptr}];
+    if (ent.bytes < need) {
+      if (ent.ptr) {
+        cudaStreamSynchronize(stream);
+        cudaFree(ent.ptr);
+        ent.ptr = nullptr;
+        ent.bytes = 0;
+      }
+      void* p = nullptr;
+      if ((e = cudaMalloc(&p, need)) != cudaSuccess)
+        return cuda_fail(e, "cudaMalloc(workspace)");
+      if ((e = cudaMemsetAsync(p, 0, need, stream)) != cudaSuccess)
+        return cuda_fail(e, "cudaMemsetAsync(workspace)");
+      ent.ptr = p;
+      ent.bytes = need;
+    }
+    ws = ent.ptr;
+    ws_bytes = ent.bytes;
+  }
+  if (need > 0) {
+    if (ws == nullptr || ws_bytes < need)
+      return fail(NVFP4DG_ERR_WORKSPACE,
+                  "workspace of " + std::to_string(need) +
+                      " bytes required, got " + std::to_string(ws_bytes));
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0)
+      return fail(NVFP4DG_ERR_ALIGN, "workspace is not 256-byte aligned");
+  } else {
+    ws = nullptr;
+  }
+  if (plan.bn == 128 && (flags & NVFP4DG_FLAG_SPLIT_MMA))
+    rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
+                            M, N, K, ws, stream);
+  else if (plan.bn == 128)
+    rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                           N, K, ws, stream);
+  else
+    rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                           N, K, ws, stream);
+  if (rc) return rc;
+  if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
+    unsigned word = 0;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess)
+      return cuda_fail(e, "cudaStreamSynchronize");
+    if ((e = cudaMemcpyFromSymbol(&word, g_err_word, sizeof(word))) !=
+        cudaSuccess)
+      return cuda_fail(e, "cudaMemcpyFromSymbol");
+    if (word != 0) {
+      const unsigned zero = 0;
+      cudaMemcpyToSymbol(g_err_word, &zero, sizeof(zero));
+      return fail(NVFP4DG_ERR_DEVICE,
+                  "kernel wait timed out (device error word " +
+                      std::to_string(word) + ")");
+    }
+  }
+  return NVFP4DG_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int nvfp4_dual_gemm_run(const void* A, const void* B1, const void* B2,
+                        const void* SFA, const void* SFB1, const void* SFB2,
+                        void* C, int M, int N, int K, int L, unsigned flags,
+                        void* stream) {
+  return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, nullptr, 0,
+                  true, stream);
+}
+
+int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void* B2,
+                           const void* SFA, const void* SFB1, const void* SFB2,
+                           void* C, int M, int N, int K, int L, unsigned flags,
+                           void* workspace, size_t workspace_bytes,
+                           void* stream) {
+  return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, workspace,
+                  workspace_bytes, false, stream);
+}
+
+size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
+                                      unsigned flags) {
+  g_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || L != 1 || N % 64 || K % 256) return 0;
+  int devid = 0;
+  if (cudaGetDevice(&devid) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DevInfo* dev = nullptr;
+  if (device_info(devid, &dev)) return 0;
+  return static_cast<size_t>(
+      workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+}
+
+int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
+                         int* bn_out, int* grid_out, int* dp_tiles_out,
+                         int* sk_tiles_out) {
+  g_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 256 || num_sms <= 0)
+    return fail(NVFP4DG_ERR_INVALID, "invalid problem for planning");
+  const Plan p = choose_plan(M, N, K, flags, num_sms);
+  if (bn_out) *bn_out = p.bn;
+  if (grid_out) *grid_out = p.grid;
+  if (dp_tiles_out) *dp_tiles_out = p.dp_tiles;
+  if (sk_tiles_out) *sk_tiles_out = p.num_tiles - p.dp_tiles;
+  return NVFP4DG_OK;
+}
+
+int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, int num_sms,
+                              int cta, int* records, int cap) {
+  g_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 256 || num_sms <= 0) {
+    fail(NVFP4DG_ERR_INVALID, "invalid problem for planning");
+    return -1;
+  }
+  const Plan p = choose_plan(M, N, K, flags, num_sms);
+  if (cta < 0 || cta >= p.grid) {
+    fail(NVFP4DG_ERR_INVALID, "cta out of range");
+    return -1;
+  }
+  WorkIter it;
+  work_begin(p, cta, it);
+  Work w;
+  int n = 0;
+  while (work_next(p, it, w)) {
+    if (n < cap && records) {
+      records[4 * n + 0] = w.tile;
+      records[4 * n + 1] = w.kb0;
+      records[4 * n + 2] = w.kb1;
+      records[4 * n + 3] = w.slot;
+    }
+    ++n;
+  }
+  return n;
+}
+
+int nvfp4_quantize(const float* X, int rows, int K, void* codes,
+                   void* sf_plain, void* sf_blocked, void* stream_ptr) {
+  g_last_error.clear();
+  if (rows < 0 || K < 0 || K % 64 != 0)
+    return fail(NVFP4DG_ERR_INVALID, "rows >= 0 and K % 64 == 0 required");
+  if (rows == 0 || K == 0) return NVFP4DG_OK;
+  if (!X || !codes || !sf_blocked)
+    return fail(NVFP4DG_ERR_INVALID, "X, codes and sf_blocked are required");
+  if (reinterpret_cast<uintptr_t>(X) % 16 || reinterpret_cast<uintptr_t>(codes) % 8)
+    return fail(NVFP4DG_ERR_ALIGN, "X must be 16-byte and codes 8-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const size_t blocked = (size_t)((rows + 127) / 128) * (K / 64) * kSfAtomBytes;
+  cudaError_t e = cudaMemsetAsync(sf_blocked, 0, blocked, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(sf_blocked)");
+  const long long nblk = (long long)rows * (K / 16);
+  const int threads = 256;
+  const long long want = (nblk + threads - 1) / threads;
+  const int blocks = (int)std::min<long long>(want, 148LL * 16);
+  quantize_kernel<<<blocks, threads, 0, stream>>>(
+      X, rows, K, static_cast<uint8_t*>(codes),
+      static_cast<uint8_t*>(sf_plain), static_cast<uint8_t*>(sf_blocked));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_kernel launch");
+  return NVFP4DG_OK;
+}
+
+int nvfp4_dual_gemm_device_status(int device, unsigned* word_out) {
+  g_last_error.clear();
+  if (!word_out) return fail(NVFP4DG_ERR_INVALID, "word_out is NULL");
+  std::lock_guard<std::mutex> lock(g_mu);
+  return read_status(device, word_out);
+}
+
+const char* nvfp4_dual_gemm_last_error(void) { return g_last_error.c_str(); }
+
+int nvfp4_dual_gemm_version(void) { return 100; }
+
+}  // extern "C"

@@ -1,0 +1,136 @@
+// schedule.h — persistent tile scheduler of the dual GEMM, shared by the
+// device kernel and the host (planning, workspace sizing, tests).
+//
+// The output is cut into 128 x BN tiles (BN columns of each GEMM); a tile
+// needs `kblocks` = K/256 main-loop iterations.  The reference launches one
+// CTA per tile and never splits K (nvfp4_dual_gemm.cu:95-97, 368-372), which
+// leaves 20-52 of the 148 SMs idle on its decode shapes.  Here a persistent
+// grid of `grid` CTAs (at most one per SM) works through:
+//   1. data-parallel (DP) tiles: tile t < dp_tiles goes whole to CTA t % grid;
+//   2. stream-K (SK) tiles: the remaining tiles' iterations, laid end to end,
+//      are cut into `grid` equal contiguous ranges, CTA b taking
+//      [lo(b), lo(b+1)), lo(b) = b * sk_iters / grid.
+// A tile whose iterations span several CTAs is finished by whichever of them
+// arrives last: every segment writes its fp32 partial accumulator to a
+// workspace slot, bumps the tile's counter, and the CTA that brings the
+// counter to the segment count sums all partials in a fixed order and runs
+// the SiLU epilogue.  No CTA ever waits for another one.
+#pragma once
+
+#include <cstdint>
+
+#if defined(__CUDACC__)
+#define NVFP4DG_HD __host__ __device__ __forceinline__
+#else
+#define NVFP4DG_HD inline
+#endif
+
+namespace nvfp4dg {
+
+struct Plan {
+  int m_tiles;      // ceil(M / 128)
+  int n_tiles;      // N / BN
+  int kblocks;      // K / 256
+  int num_tiles;    // m_tiles * n_tiles
+  int grid;         // persistent CTAs
+  int dp_tiles;     // whole tiles handed out round-robin (multiple of grid)
+  int bn;           // tile width per GEMM (64 or 128)
+  int pad;
+  long long sk_iters;  // (num_tiles - dp_tiles) * kblocks
+};
+
+struct Work {
+  int tile;  // linear tile index; m fastest: m = tile % m_tiles
+  int kb0;   // first 256-wide K block
+  int kb1;   // one past the last K block
+  int slot;  // workspace slot of the partial, -1 for a whole tile
+};
+
+NVFP4DG_HD long long sk_lo(const Plan& p, int b) {
+  return static_cast<long long>(b) * p.sk_iters / p.grid;
+}
+
+// CTA whose stream-K range holds iteration x.
+NVFP4DG_HD int sk_owner(const Plan& p, long long x) {
+  return static_cast<int>(((x + 1) * p.grid - 1) / p.sk_iters);
+}
+
+// Workspace slot used by CTA b for its segment of stream-K tile ts
+// (ts counted from the first SK tile): slot 2b for the CTA's first segment,
+// 2b + 1 for its last one.
+NVFP4DG_HD int sk_slot(const Plan& p, int b, long long ts) {
+  const long long first_ts = sk_lo(p, b) / p.kblocks;
+  return 2 * b + (first_ts == ts ? 0 : 1);
+}
+
+struct WorkIter {
+  int b;
+  int dp_next;
+  int first_sk;
+  int pad;
+  long long it;
+  long long it_end;
+};
+
+NVFP4DG_HD void work_begin(const Plan& p, int b, WorkIter& s) {
+  s.b = b;
+  s.dp_next = b;
+  s.first_sk = 1;
+  s.pad = 0;
+  if (p.sk_iters > 0) {
+    s.it = sk_lo(p, b);
+    s.it_end = sk_lo(p, b + 1);
+  } else {
+    s.it = 0;
+    s.it_end = 0;
+  }
+}
+
+NVFP4DG_HD bool work_next(const Plan& p, WorkIter& s, Work& w) {
+  if (s.dp_next < p.dp_tiles) {
+    w.tile = s.dp_next;
+    w.kb0 = 0;
+    w.kb1 = p.kblocks;
+    w.slot = -1;
+    s.dp_next += p.grid;
+    return true;
+  }
+  if (s.it >= s.it_end) return false;
+  const long long ts = s.it / p.kblocks;
+  const int kb0 = static_cast<int>(s.it - ts * p.kblocks);
+  const long long left = s.it_end - s.it;
+  const int kb1 = (kb0 + left < p.kblocks) ? static_cast<int>(kb0 + left)
+                                           : p.kblocks;
+  w.tile = p.dp_tiles + static_cast<int>(ts);
+  w.kb0 = kb0;
+  w.kb1 = kb1;
+  const bool whole = (kb0 == 0 && kb1 == p.kblocks);
+  w.slot = whole ? -1 : 2 * s.b + (s.first_sk ? 0 : 1);
+  s.first_sk = 0;
+  s.it += kb1 - kb0;
+  return true;
+}
+
+// CTAs [*b_first, *b_last] hold the segments of stream-K tile ts.
+NVFP4DG_HD void sk_tile_owners(const Plan& p, long long ts, int* b_first,
+                               int* b_last) {
+  *b_first = sk_owner(p, ts * p.kblocks);
+  *b_last = sk_owner(p, ts * p.kblocks + p.kblocks - 1);
+}
+
+// Workspace layout: [partials: 2 * grid slots of 128 x 2*BN fp32]
+//                   [counters: one int per stream-K tile], 256-byte aligned.
+NVFP4DG_HD long long partial_slot_floats(const Plan& p) {
+  return 128ll * 2 * p.bn;
+}
+NVFP4DG_HD long long workspace_counter_offset(const Plan& p) {
+  const long long bytes = 2ll * p.grid * partial_slot_floats(p) * 4;
+  return (bytes + 255) / 256 * 256;
+}
+NVFP4DG_HD long long workspace_bytes(const Plan& p) {
+  if (p.sk_iters == 0) return 0;
+  const long long sk_tiles = p.num_tiles - p.dp_tiles;
+  return workspace_counter_offset(p) + (sk_tiles * 4 + 255) / 256 * 256;
+}
+
+}  // namespace nvfp4dg

@@ -1,0 +1,281 @@
+// sm100_ptx.cuh — thin inline-PTX helpers for sm_100a: mbarriers with bounded
+// waits, TMA tensor / bulk copies, tcgen05 (TMEM alloc, copy, block-scaled
+// MMA, commit, load) and the shared-memory / instruction descriptors.
+//
+// Written from the PTX ISA description of each instruction.  The reference
+// keeps equivalent wrappers in tcgen05-interface.cuh and tma-interface.cuh;
+// the differences that matter here: every wait is bounded by %globaltimer and
+// reports through a device error word instead of spinning forever
+// (tma-interface.cuh:64-75 spins unbounded), and the TMEM base address
+// returned by tcgen05.alloc is always used instead of being assumed to be 0.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+
+namespace nvfp4dg {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar,
+                                                      uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+          smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Time limit of every wait in the kernels of this library.  A legitimate wait
+// lasts microseconds; the limit only exists so that a logic error ends the
+// kernel with an error word instead of hanging the GPU.
+constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+
+// Wait until the phase with parity `parity` of `bar` has completed.  Returns
+// false (after setting `code` in *err) if the time limit expires, or at once
+// if *err is already non-zero because another role gave up.
+// With bail_on_err = false the wait ignores *err and only the time limit
+// ends it (used to drain copies and MMAs before the CTA exits).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          unsigned* err, unsigned code,
+                                          bool bail_on_err = true) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0u) {
+      if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u)
+        return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        atomicOr(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// L2 cache policies (createpolicy) and TMA / bulk copies
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;"
+               : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
+               : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m))
+               : "memory");
+}
+
+// 2-D tiled TMA load global -> this CTA's shared memory; completion is
+// signalled as transaction bytes on `bar`.  c0 is the innermost coordinate.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m,
+                                            uint64_t* bar, int c0, int c1,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1),
+      "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Contiguous bulk copy global -> shared (16-byte aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src,
+                                          uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: tensor memory
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst_smem)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Copy a 32-row x 16-byte block from shared memory (described by `sdesc`)
+// into 4 TMEM columns starting at `taddr`, replicated into all four 32-lane
+// sub-partitions: lane 32q+i, column c receives bytes [16i + 4c, 16i + 4c + 4).
+__device__ __forceinline__ void tc_cp_32x128b_x4(uint32_t taddr,
+                                                 uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr),
+               "l"(sdesc)
+               : "memory");
+}
+
+// D(tmem) (+)= A(smem) * B(smem)^T with block scales read from TMEM;
+// kind::mxf4nvf4, one e4m3 scale per 16 K elements (scale_vec::4X).
+// Collector: kCollNone reads A from shared memory; kCollFill reads it and
+// keeps it in the A collector; kCollLastUse takes A from the collector (the
+// immediately preceding MMA must have used kCollFill with the same A).
+enum Collector : int { kCollNone = 0, kCollFill = 1, kCollLastUse = 2 };
+
+#define NVFP4DG_MMA_ASM(COLL)                                                \
+  asm volatile(                                                              \
+      "{\n\t.reg .pred p;\n\t"                                               \
+      "setp.ne.b32 p, %4, 0;\n\t"                                             \
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.scale_vec::4X" COLL \
+      " [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),                  \
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem),  \
+      "r"(sfb_tmem)                                                          \
+      : "memory")
+
+template <int kColl = kCollNone>
+__device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t a_desc,
+                                            uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem,
+                                            uint32_t sfb_tmem,
+                                            uint32_t accumulate) {
+  if constexpr (kColl == kCollFill) {
+    NVFP4DG_MMA_ASM(".collector::a::fill");
+  } else if constexpr (kColl == kCollLastUse) {
+    NVFP4DG_MMA_ASM(".collector::a::lastuse");
+  } else {
+    NVFP4DG_MMA_ASM("");
+  }
+}
+#undef NVFP4DG_MMA_ASM
+
+// Arrive once on `bar` when all previously issued tcgen05 async operations of
+// this thread have completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+// Each thread of the warp reads 32 consecutive fp32 columns of its TMEM lane.
+__device__ __forceinline__ void tc_ld_32cols(uint32_t taddr, float (&v)[32]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Descriptors
+// ---------------------------------------------------------------------------
+// Shared-memory matrix descriptor (tcgen05 format): start address, leading-
+// and stride-dimension byte offsets (all >> 4), the fixed version bits 46-48 =
+// 0b001, base offset 0 and the layout (swizzle) type in bits 61-63.
+enum class SmemLayout : uint32_t { kNone = 0, kSwizzle128B = 2 };
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo,
+                                              uint32_t sbo, SmemLayout lay) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>((lbo & 0x3FFFFu) >> 4) << 16;
+  d |= static_cast<uint64_t>((sbo & 0x3FFFFu) >> 4) << 32;
+  d |= 1ull << 46;
+  d |= static_cast<uint64_t>(lay) << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::mxf4nvf4: A and B e2m1 (format code 1 in
+// bits 7-9 and 10-12), both K-major, dense, N >> 3 in bits 17-22, scale type
+// UE4M3 (bit 23 = 0), M >> 4 in bits 24-28, scale-factor ids 0, K = 64.
+__host__ __device__ constexpr uint32_t idesc_nvf4(int m, int n) {
+  return (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+}  // namespace nvfp4dg

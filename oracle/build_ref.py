@@ -1,0 +1,105 @@
+"""Build the reference's own kernel into ``oracle/_ref/`` — TEST INFRASTRUCTURE.
+
+Recipe: ``oracle/ref_binding.cu`` includes the reference's
+``nvfp4_dual_gemm.cu`` (and through it ``tcgen05-interface.cuh`` and
+``tma-interface.cuh``) from the reference checkout, and is compiled with the
+flags the reference's own JIT build uses (submission.py:1136-1150:
+``-O3 --use_fast_math -gencode=arch=compute_100a,code=sm_100a
+--expt-relaxed-constexpr --relocatable-device-code=false``, linked with
+``-lcuda``) into the Python module ``oracle/_ref/nvfp4_ref*.so``.  Only the
+output lands under ``oracle/_ref/`` (git-ignored); the built module travels
+to GPU machines with the checkout, the reference sources do not.
+
+The reference directory defaults to ``reference`` beside this repository and can be overridden with ``NVFP4DG_REFERENCE_DIR``.
+
+The module exposes ``cuda_nvfp4_dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C)``.
+Safe shapes: only those in the reference's dispatch table
+(nvfp4_dual_gemm.cu:403-442) with K / 256 >= 4; for K / 256 < 4 the
+reference's producer prologue issues scale copies past the end of the scale
+buffers (nvfp4_dual_gemm.cu:246-248), so those shapes are never run.
+"""
+from __future__ import annotations
+
+import glob
+import importlib.machinery
+import importlib.util
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(HERE)
+OUT_DIR = os.path.join(HERE, "_ref")
+MODULE = "nvfp4_ref"
+
+# Shapes of the reference's dispatch table that are safe to run.
+SAFE_SHAPES = {
+    (256, 4096, 7168), (512, 4096, 7168), (256, 3072, 4096),
+    (512, 3072, 7168), (1536, 512, 7168), (3072, 1024, 1536),
+    (7168, 2304, 2048), (4608, 384, 7168), (7168, 384, 2304),
+    (512, 768, 7168),
+}
+# The reference returns C as a transposed view for this shape
+# (nvfp4_dual_gemm.cu:413-415): column-major storage.
+TRANSPOSED_SHAPES = {(512, 3072, 7168)}
+
+
+def reference_dir() -> str:
+    return os.environ.get("NVFP4DG_REFERENCE_DIR",
+                          os.path.join(os.path.dirname(REPO), "reference"))
+
+
+def built_path() -> str | None:
+    hits = sorted(glob.glob(os.path.join(OUT_DIR, MODULE + "*.so")))
+    return hits[0] if hits else None
+
+
+def build(verbose: bool = False) -> str:
+    """Compile the reference kernel module; returns the .so path."""
+    src_dir = reference_dir()
+    if not os.path.exists(os.path.join(src_dir, "nvfp4_dual_gemm.cu")):
+        raise FileNotFoundError(f"reference sources not found in {src_dir}")
+    os.makedirs(OUT_DIR, exist_ok=True)
+    from torch.utils import cpp_extension
+
+    stubs = "/usr/local/cuda/lib64/stubs"
+    cpp_extension.load(
+        name=MODULE,
+        sources=[os.path.join(HERE, "ref_binding.cu")],
+        extra_include_paths=[src_dir],
+        extra_cuda_cflags=[
+            "-O3",
+            "--use_fast_math",
+            "-gencode=arch=compute_100a,code=sm_100a",
+            "--expt-relaxed-constexpr",
+            "--relocatable-device-code=false",
+        ],
+        extra_ldflags=[f"-L{stubs}", "-lcuda"],
+        build_directory=OUT_DIR,
+        verbose=verbose,
+        is_python_module=True,
+    )
+    path = built_path()
+    if path is None:
+        raise RuntimeError("reference build produced no module")
+    return path
+
+
+def load():
+    """Import the prebuilt reference module (no compilation); None if absent."""
+    path = built_path()
+    if path is None:
+        return None
+    import torch  # noqa: F401  (libtorch must be loaded first)
+
+    if MODULE in sys.modules:
+        return sys.modules[MODULE]
+    loader = importlib.machinery.ExtensionFileLoader(MODULE, path)
+    spec = importlib.util.spec_from_file_location(MODULE, path, loader=loader)
+    mod = importlib.util.module_from_spec(spec)
+    loader.exec_module(mod)
+    sys.modules[MODULE] = mod
+    return mod
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))

@@ -1,0 +1,136 @@
+"""CPU tests of the C ABI library: it loads without a GPU, exports every
+symbol the header declares, validates arguments without touching the GPU,
+and its host-side scheduler covers every K block of every tile exactly once."""
+import ctypes
+import os
+import re
+from collections import defaultdict
+
+import pytest
+
+import nvfp4_dual_gemm_b200 as dg
+from nvfp4_dual_gemm_b200 import _lib
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "nvfp4_dual_gemm.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"NVFP4DG_API\s+[\w\s\*]*?\b(nvfp4_\w+)\s*\(",
+                                 text)))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    assert set(_lib.SIGNATURES) == set(names)
+    assert lib.nvfp4_dual_gemm_version() == 100
+
+
+def test_invalid_arguments_rejected_without_gpu():
+    lib = _lib.load()
+    p = ctypes.c_void_p(16)
+    # N not a multiple of 64
+    rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 100, 256, 1, 0, None)
+    assert rc == _lib.ERR_INVALID and "multiple of 64" in _lib.last_error()
+    # K not a multiple of 256
+    rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 128, 100, 1, 0, None)
+    assert rc == _lib.ERR_INVALID
+    # L != 1
+    rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 128, 256, 2, 0, None)
+    assert rc == _lib.ERR_INVALID and "L must be 1" in _lib.last_error()
+    # misaligned pointer
+    q = ctypes.c_void_p(24)
+    rc = lib.nvfp4_dual_gemm_run(q, p, p, p, p, p, p, 128, 128, 256, 1, 0, None)
+    assert rc == _lib.ERR_ALIGN
+    # NULL pointer
+    rc = lib.nvfp4_dual_gemm_run(None, p, p, p, p, p, p, 128, 128, 256, 1, 0,
+                                 None)
+    assert rc == _lib.ERR_INVALID and "NULL" in _lib.last_error()
+    # empty problems are a no-op that never touches the GPU
+    assert lib.nvfp4_dual_gemm_run(None, None, None, None, None, None, None,
+                                   0, 128, 256, 1, 0, None) == _lib.OK
+    assert lib.nvfp4_dual_gemm_run(None, None, None, None, None, None, None,
+                                   128, 0, 256, 1, 0, None) == _lib.OK
+    # quantiser argument checks
+    assert lib.nvfp4_quantize(None, 4, 100, None, None, None, None) == \
+        _lib.ERR_INVALID
+
+
+def test_status_check_raises_python_errors():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_INVALID, "x")
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.ERR_DEVICE, "x")
+    _lib.check(_lib.OK, "x")
+
+
+SHAPES = [
+    (128, 256, 256), (256, 4096, 7168), (512, 3072, 7168), (4096, 14336, 4096),
+    (8192, 3584, 8192), (1536, 512, 7168), (256, 512, 256), (3072, 1024, 1536),
+    (7168, 1024, 256), (7168, 2304, 2048), (4608, 384, 7168),
+    (7168, 384, 2304), (512, 768, 7168), (4096, 768, 512), (200, 192, 768),
+]
+
+
+def cover(m, n, k, flags=0, sms=148):
+    pl = dg.plan(m, n, k, flags, sms)
+    bn = pl["bn"]
+    m_tiles = (m + 127) // 128
+    tiles = m_tiles * (n // bn)
+    kb = k // 256
+    seen = defaultdict(list)
+    slots = set()
+    for cta in range(pl["grid"]):
+        for tile, k0, k1, slot in dg.plan_work(m, n, k, cta, flags, sms):
+            assert 0 <= tile < tiles and 0 <= k0 < k1 <= kb
+            seen[tile].append((k0, k1, slot, cta))
+            if slot >= 0:
+                assert slot // 2 == cta and slot not in slots
+                slots.add(slot)
+            else:
+                assert (k0, k1) == (0, kb)
+    assert sorted(seen) == list(range(tiles))
+    for tile, segs in seen.items():
+        segs.sort()
+        # segments tile K exactly once, in order
+        assert segs[0][0] == 0 and segs[-1][1] == kb
+        for a, b in zip(segs, segs[1:]):
+            assert a[1] == b[0]
+        if len(segs) > 1:
+            assert all(s[2] >= 0 for s in segs)
+            assert tile >= pl["dp_tiles"]
+    return pl, seen
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_schedule_covers_every_block_once(m, n, k):
+    cover(m, n, k)
+
+
+@pytest.mark.parametrize("grid", [1, 2, 3, 5, 7, 13, 148])
+def test_forced_grid_stream_k(grid):
+    pl, seen = cover(256, 512, 2048, flags=grid)
+    assert pl["grid"] <= grid
+
+
+def test_no_streamk_flag_gives_whole_tiles():
+    pl, seen = cover(512, 3072, 7168, flags=dg.FLAG_NO_STREAMK)
+    assert pl["sk_tiles"] == 0
+    assert all(len(s) == 1 for s in seen.values())
+
+
+def test_bn_flags():
+    assert dg.plan(256, 4096, 7168, dg.FLAG_BN64)["bn"] == 64
+    assert dg.plan(256, 4096, 7168, dg.FLAG_BN128)["bn"] == 128
+    assert dg.plan(256, 192, 7168)["bn"] == 64  # N % 128 != 0
+
+
+def test_decode_shape_uses_every_sm_or_whole_tiles():
+    pl = dg.plan(256, 4096, 7168)
+    assert pl["grid"] <= 148

@@ -1,0 +1,153 @@
+"""CPU tests of the oracle: format tables, rounding, packing, blocked layout,
+known-answer dual GEMMs."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import nvfp4_oracle as O
+
+
+def test_e2m1_table_matches_ocp_values():
+    # OCP MX v1.0 e2m1: +-{0, 0.5, 1, 1.5, 2, 3, 4, 6}
+    assert list(O.E2M1_VALUES[:8]) == [0, 0.5, 1, 1.5, 2, 3, 4, 6]
+    assert list(O.E2M1_VALUES[8:]) == [-0.0, -0.5, -1, -1.5, -2, -3, -4, -6]
+    assert np.all(np.signbit(O.E2M1_VALUES[8:]))
+
+
+def test_e2m1_round_to_nearest_even_and_saturation():
+    q = np.array([0.0, 0.25, 0.2501, 0.75, 1.25, 1.2501, 1.75, 2.5, 2.5001,
+                  3.5, 5.0, 5.0001, 100.0, -0.1, -6.5], np.float32)
+    want = [0.0, 0.0, 0.5, 1.0, 1.0, 1.5, 2.0, 2.0, 3.0, 4.0, 4.0, 6.0, 6.0,
+            -0.0, -6.0]
+    got = O.E2M1_VALUES[O.e2m1_encode(q)]
+    assert list(got) == want
+    # every grid value maps to itself
+    for code in range(16):
+        v = O.E2M1_VALUES[code]
+        c = O.e2m1_encode(np.array([v], np.float32))[0]
+        assert O.E2M1_VALUES[c] == v and np.signbit(O.E2M1_VALUES[c]) == np.signbit(v)
+
+
+def test_e4m3_decode_table():
+    t = O.E4M3_TABLE
+    assert t[0x00] == 0 and t[0x01] == 2.0 ** -9 and t[0x08] == 2.0 ** -6
+    assert t[0x38] == 1.0 and t[0x7E] == 448.0 and np.isnan(t[0x7F])
+    assert t[0xB8] == -1.0
+
+
+def test_e4m3_encode_matches_torch_cast_in_range():
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(100_000).astype(np.float32) * s
+                        for s in (1e-3, 1e-2, 0.1, 1.0, 10.0, 100.0)])
+    x = x[np.abs(x) <= 448]
+    vals = O.E4M3_TABLE[:0x7F]
+    mids = ((vals[1:] + vals[:-1]) / 2).astype(np.float32)  # exact ties
+    x = np.concatenate([x, vals, mids, -mids])
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(O.e4m3_encode(x), ref)
+
+
+def test_e4m3_encode_saturates():
+    assert O.e4m3_encode(np.array([500.0, -1e9], np.float32)).tolist() == [0x7E, 0xFE]
+
+
+def test_pack_unpack_nibble_order():
+    codes = np.array([[1, 2, 3, 4]], np.uint8)
+    packed = O.pack_codes(codes)
+    assert packed.tolist() == [[0x21, 0x43]]  # element 2i in the low nibble
+    assert np.array_equal(O.unpack_codes(packed), codes)
+
+
+def test_blocked_layout_matches_reference_addressing():
+    # Reference: atom index = rowblock * (K/64) + k64, 512 B per atom
+    # (nvfp4_dual_gemm.cu:226-243); within an atom row r%32 owns 16 bytes,
+    # 4 per 32-row quadrant.
+    rows, k = 256, 512
+    off = O.blocked_offsets(rows, k)
+    assert off[0, 0] == 0 and off[0, 3] == 3 and off[0, 4] == 512
+    assert off[1, 0] == 16 and off[32, 0] == 4 and off[96, 2] == 14
+    assert off[128, 0] == (k // 64) * 512
+    assert len(np.unique(off)) == off.size
+
+
+def test_blocked_roundtrip_with_padding():
+    rng = np.random.default_rng(1)
+    sf = rng.integers(0, 0x7F, (300, 64)).astype(np.uint8)
+    buf = O.to_blocked(sf)
+    assert buf.size == 3 * 16 * 512
+    assert np.array_equal(O.from_blocked(buf, 300, 1024), sf)
+    mask = np.ones(buf.size, bool)
+    mask[O.blocked_offsets(300, 1024)] = False
+    assert not buf[mask].any()  # padding rows are zero
+
+
+def test_quantize_dequantize_error_bound():
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((64, 256)).astype(np.float32)
+    codes, sf = O.quantize(x)
+    y = O.dequantize(codes, sf)
+    blk = np.abs(x).reshape(64, 16, 16).max(axis=2, keepdims=True)
+    err = np.abs(x - y).reshape(64, 16, 16)
+    # half a grid step of e2m1 (<= 1.0 at the top of the range) times the
+    # scale, plus the e4m3 rounding of the scale itself
+    assert np.all(err <= blk / 6 * 1.0625 * 1.0 + 1e-6)
+
+
+def test_zero_block_gives_zero_codes():
+    x = np.zeros((1, 64), np.float32)
+    x[0, 16:32] = 1e-6  # amax / 6 rounds to 0 in e4m3
+    codes, sf = O.quantize(x)
+    assert not codes.any() and not sf.any()
+
+
+def test_one_hot_known_answer():
+    # A row i has a single non-zero code at k = i (value 1.0 with scale 1.0),
+    # so (A B^T)[i, n] = B[n, i] exactly: checks nibble order and scales.
+    m, n, k = 4, 8, 64
+    a = np.zeros((m, k), np.float32)
+    for i in range(m):
+        a[i, 2 * i + 1] = 6.0  # odd K index -> high nibble
+    b1 = np.arange(n * k, dtype=np.float32).reshape(n, k) % 7 - 3
+    b2 = np.ones((n, k), np.float32) * 2
+    qa, sa = O.quantize(a)
+    q1, s1 = O.quantize(b1)
+    q2, s2 = O.quantize(b2)
+    c = O.dual_gemm(qa, sa, q1, s1, q2, s2).astype(np.float32)
+    d1 = O.dequantize(q1, s1)
+    d2 = O.dequantize(q2, s2)
+    da = O.dequantize(qa, sa)
+    for i in range(m):
+        x1 = da[i, 2 * i + 1] * d1[:, 2 * i + 1]
+        x2 = da[i, 2 * i + 1] * d2[:, 2 * i + 1]
+        want = (x1 / (1 + np.exp(-x1)) * x2).astype(np.float16).astype(np.float32)
+        assert np.array_equal(c[i], want)
+
+
+def test_reference_output_fp32_vs_fp64_config1():
+    p = O.make_problem(128, 256, 256, seed=0)
+    c32 = O.reference_output(p)
+    c64 = O.reference_output(p, accumulate=np.float64)
+    ok, n_bad, _ = O.check_close(c32, c64)
+    assert ok, n_bad
+
+
+def test_sampled_reference_matches_full():
+    p = O.make_problem(128, 256, 512, seed=3)
+    full = O.reference_output(p)
+    rows = np.array([0, 5, 127])
+    cols = np.array([1, 64, 255])
+    part = O.reference_output(p, rows=rows, cols=cols)
+    assert np.array_equal(part, full[np.ix_(rows, cols)])
+
+
+def test_make_problem_is_deterministic():
+    p1 = O.make_problem(128, 128, 256, seed=7)
+    p2 = O.make_problem(128, 128, 256, seed=7)
+    for key in ("a", "b1", "b2", "sfa", "sfb1", "sfb2"):
+        assert np.array_equal(p1[key], p2[key])
+
+
+@pytest.mark.parametrize("bad", [np.nan])
+def test_check_close_rejects_nan(bad):
+    ok, n, _ = O.check_close(np.array([bad], np.float16), np.array([1], np.float16))
+    assert not ok and n == 1
