@@ -64,6 +64,8 @@ extern "C" {
                                               error word after the launch       */
 #define NVFP4DG_FLAG_SPLIT_MMA (1u << 16) /* BN=128: two N=128 MMAs per K step
                                              instead of one N=256 MMA           */
+#define NVFP4DG_FLAG_FORCE_STREAMK (1u << 17) /* always split the last waves of
+                                                 tiles along K (stream-K)      */
 
 /*
  * Run the dual GEMM on `stream` using a workspace the library keeps per

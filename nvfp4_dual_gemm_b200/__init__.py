@@ -17,6 +17,7 @@ from .api import (  # noqa: F401
 from ._lib import (  # noqa: F401
     FLAG_BN64,
     FLAG_BN128,
+    FLAG_FORCE_STREAMK,
     FLAG_NO_STREAMK,
     FLAG_SPLIT_MMA,
     FLAG_SYNC_CHECK,

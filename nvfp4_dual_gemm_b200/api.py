@@ -63,7 +63,7 @@ def _rows_dense(name: str, t: torch.Tensor, rows: int, row_bytes: int) -> None:
     if t.size(0) != rows or t.size(1) != row_bytes:
         raise ValueError(f"{name} has shape {tuple(t.shape)}, expected "
                          f"[{rows}, {row_bytes}(, 1)]")
-    if rows > 1 and t.stride(0) != row_bytes:
+    if rows > 1 and row_bytes > 0 and t.stride(0) != row_bytes:
         raise ValueError(f"{name} rows must be dense (stride(0) == K/2)")
     if row_bytes > 1 and t.stride(1) != 1:
         raise ValueError(f"{name} must be K-major (stride(1) == 1)")

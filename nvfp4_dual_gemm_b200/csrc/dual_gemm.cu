@@ -624,7 +624,8 @@ int tensor_map(const void* ptr, long long rows, long long row_bytes,
 // cycles, so BN = 128 costs ~512 cycles per block and BN = 64 (two N = 64
 // MMAs) ~256.  A split tile costs its partial round trip through L2 at
 // ~64 B/cycle per SM.
-Plan plan_for(int M, int N, int K, int bn, int grid_cap, bool streamk) {
+Plan plan_for(int M, int N, int K, int bn, int grid_cap, bool streamk,
+              bool force_sk = false) {
   Plan p{};
   p.bn = bn;
   p.m_tiles = (M + kBM - 1) / kBM;
@@ -632,7 +633,7 @@ Plan plan_for(int M, int N, int K, int bn, int grid_cap, bool streamk) {
   p.kblocks = K / 256;
   p.num_tiles = p.m_tiles * p.n_tiles;
   const int T = p.num_tiles;
-  if (!streamk || T % grid_cap == 0) {
+  if (!streamk || (T % grid_cap == 0 && !force_sk)) {
     p.grid = std::min(T, grid_cap);
     p.dp_tiles = T;
     p.sk_iters = 0;
@@ -683,9 +684,10 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
   }
   Plan best{};
   double best_cost = 1e300;
+  const bool force_sk = (flags & NVFP4DG_FLAG_FORCE_STREAMK) != 0;
   for (int i = 0; i < nb; ++i) {
-    for (int sk = 0; sk < (streamk ? 2 : 1); ++sk) {
-      Plan p = plan_for(M, N, K, bns[i], cap, sk == 1);
+    for (int sk = force_sk ? 1 : 0; sk < (streamk ? 2 : 1); ++sk) {
+      Plan p = plan_for(M, N, K, bns[i], cap, sk == 1, force_sk);
       const double c = plan_cost(p);
       if (c < best_cost) {
         best_cost = c;
@@ -712,6 +714,9 @@ int check_problem(const void* A, const void* B1, const void* B2,
     return fail(NVFP4DG_ERR_INVALID, "BN=128 forced but N % 128 != 0");
   if ((flags & NVFP4DG_FLAG_BN64) && (flags & NVFP4DG_FLAG_BN128))
     return fail(NVFP4DG_ERR_INVALID, "BN64 and BN128 flags are exclusive");
+  if ((flags & NVFP4DG_FLAG_FORCE_STREAMK) && (flags & NVFP4DG_FLAG_NO_STREAMK))
+    return fail(NVFP4DG_ERR_INVALID,
+                "FORCE_STREAMK and NO_STREAMK flags are exclusive");
   if (M == 0 || N == 0) return NVFP4DG_OK;
   const void* ptrs[7] = {A, B1, B2, SFA, SFB1, SFB2, C};
   const char* names[7] = {"A", "B1", "B2", "SFA", "SFB1", "SFB2", "C"};

@@ -114,9 +114,18 @@ def test_schedule_covers_every_block_once(m, n, k):
 
 
 @pytest.mark.parametrize("grid", [1, 2, 3, 5, 7, 13, 148])
-def test_forced_grid_stream_k(grid):
-    pl, seen = cover(256, 512, 2048, flags=grid)
+@pytest.mark.parametrize("force", [0, dg.FLAG_FORCE_STREAMK])
+def test_forced_grid_stream_k(grid, force):
+    pl, seen = cover(256, 512, 2048, flags=grid | force)
     assert pl["grid"] <= grid
+    if force and grid in (3, 5, 7):  # tile counts 8 / 16 do not divide
+        assert pl["sk_tiles"] > 0
+        assert any(len(s) > 1 for s in seen.values())
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_schedule_forced_stream_k_covers_every_block_once(m, n, k):
+    cover(m, n, k, flags=dg.FLAG_FORCE_STREAMK)
 
 
 def test_no_streamk_flag_gives_whole_tiles():

@@ -67,7 +67,10 @@ def streamk_problem():
 @pytest.mark.parametrize("bn", [64, 128])
 def test_stream_k_forced_grid(streamk_problem, grid, bn):
     p, ref = streamk_problem
-    flag = _lib.FLAG_BN64 if bn == 64 else _lib.FLAG_BN128
+    flag = (_lib.FLAG_BN64 if bn == 64 else _lib.FLAG_BN128) | \
+        _lib.FLAG_FORCE_STREAMK
+    if grid in (3, 5, 7):
+        assert dg.plan(256, 512, 2048, grid | flag)["sk_tiles"] > 0
     assert_close(run(p, grid | flag), ref, f"grid={grid} bn={bn}")
 
 
@@ -80,7 +83,7 @@ def test_stream_k_repeated_calls_reuse_counters(streamk_problem):
         d["c"].fill_(float("nan"))
         dg.dual_gemm(d["a"], d["b1"], d["b2"], d["sfa_blocked"],
                      d["sfb1_blocked"], d["sfb2_blocked"], d["c"],
-                     flags=5 | _lib.FLAG_SYNC_CHECK)
+                     flags=5 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_SYNC_CHECK)
         torch.cuda.synchronize()
         assert_close(d["c"].cpu().numpy(), ref, "repeat")
 
@@ -193,9 +196,13 @@ def test_property_doubling_b2_scales_doubles_output():
     q["sfb2"] = (p["sfb2"] + 8).astype(np.uint8)
     q["sfb2_blocked"] = O.to_blocked(q["sfb2"])
     c2 = run(q)
-    fin = np.isfinite(c2) & (np.abs(c1.astype(np.float32)) < 30000)
+    a1 = np.abs(c1.astype(np.float32))
+    # fp16 normal range on both sides: doubling a subnormal is not exact
+    fin = np.isfinite(c2) & (a1 < 30000) & (a1 >= 2.0 ** -13)
     assert fin.mean() > 0.9
-    assert np.array_equal(c2[fin], (c1[fin].astype(np.float32) * 2).astype(np.float16))
+    want = (c1[fin].astype(np.float32) * 2).astype(np.float16)
+    bad = int((c2[fin] != want).sum())
+    assert bad == 0, f"{bad} of {fin.sum()} outputs did not double exactly"
 
 
 def test_property_row_permutation_equivariance():
@@ -214,7 +221,7 @@ def test_property_row_permutation_equivariance():
 
 def test_caller_owned_workspace_matches_library_workspace(streamk_problem):
     p, ref = streamk_problem
-    flags = 7
+    flags = 7 | _lib.FLAG_FORCE_STREAMK
     need = dg.workspace_size(256, 512, 2048, flags)
     assert need > 0
     ws = torch.zeros(need, dtype=torch.uint8, device="cuda")
