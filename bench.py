@@ -237,6 +237,27 @@ def time_graph(step_fn, steps, warmup, world):
     return ms, clk.summary()
 
 
+def time_eager(step_fn, steps, warmup, world):
+    """Warm up, then time `steps` back-to-back eager calls between two events
+    on the current (default) stream.  Used for implementations whose launches
+    cannot be captured in a CUDA graph."""
+    for i in range(warmup):
+        step_fn(i)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        start.record()
+        for i in range(steps):
+            step_fn(i)
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end), clk.summary()
+
+
 def time_e2e(call, host_inputs, dev_inputs, c_dev, c_host, steps, world):
     """Per step: pinned H2D of the inputs, the call, D2H of C; events around
     all of it."""
@@ -444,7 +465,10 @@ def run_reference(args, world, rank):
             d = sets[i % nsets]
             mod.cuda_nvfp4_dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9])
 
-        ms, clocks = time_graph(step, args.steps, args.warmup, 1)
+        # The reference launches on the legacy default stream
+        # (nvfp4_dual_gemm.cu:368-372), which no CUDA graph can capture, so
+        # its steps are timed as back-to-back eager calls.
+        ms, clocks = time_eager(step, args.steps, args.warmup, 1)
         tflops = algo_flops(m, n, k) * args.steps / (ms * 1e-3) / 1e12
         dev_in = [d0[0], d0[1], d0[2], d0[6], d0[7], d0[8]]
         host_in = [t.cpu().pin_memory() for t in dev_in]
@@ -460,6 +484,8 @@ def run_reference(args, world, rank):
             "reference_kind": "the reference's CUDA kernel, compiled from its "
                               "sources by oracle/build_ref.py, called through "
                               "its cuda_nvfp4_dual_gemm entry",
+            "timed": "back-to-back eager calls (legacy default stream, "
+                     "not capturable in a CUDA graph)",
             "e2e": {"value": round(algo_flops(m, n, k) * e2e_steps /
                                    (e2e_ms * 1e-3) / 1e12, 3),
                     "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,

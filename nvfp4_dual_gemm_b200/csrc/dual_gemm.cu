@@ -79,6 +79,27 @@ struct KParams {
 
 __device__ unsigned g_err_word;
 
+// Optional pipeline trace (compile with -DNVFP4DG_TRACE): per CTA, the SM
+// clock at each hand-off of the first kTraceSlots main-loop iterations —
+// producer after its empty-slot wait (0) and after issuing the copies (1),
+// MMA issuer after its full-slot wait (2) and after its commit (3) — and per
+// work unit the epilogue's accumulator-ready (4) and done (5) times.
+#ifdef NVFP4DG_TRACE
+constexpr int kTraceSlots = 64;
+constexpr int kTraceRoles = 6;
+constexpr int kTraceCtas = 160;
+__device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
+#define NVFP4DG_STAMP(role, idx)                                   \
+  do {                                                             \
+    if (blockIdx.x < kTraceCtas && (idx) < kTraceSlots)            \
+      g_trace[blockIdx.x][role][idx] = clock_cycles();             \
+  } while (0)
+#else
+#define NVFP4DG_STAMP(role, idx) \
+  do {                           \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void epi_bar() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
@@ -212,6 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          NVFP4DG_STAMP(0, issued);
           uint8_t* st = smem + stage * Cf::kStageBytes;
           uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
           mbar_arrive_expect_tx(&full_bar[stage], Cf::kStageBytes);
@@ -226,6 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     kSfRunBytes, &full_bar[stage], pol_b);
           bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
                     kSfRunBytes, &full_bar[stage], pol_b);
+          NVFP4DG_STAMP(1, issued);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -252,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
+      int consumed = 0;
       bool ok = true;
       WorkIter it;
       work_begin(plan, blockIdx.x, it);
@@ -271,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          NVFP4DG_STAMP(2, consumed);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
           const uint32_t b_addr = a_addr + Cf::kABytes;
@@ -308,6 +333,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           tc_commit(&empty_bar[stage]);
+          NVFP4DG_STAMP(3, consumed);
+          ++consumed;
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -327,12 +354,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x;  // TMEM lane == tile row
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     uint32_t acc_phase = 0;
+    int unit = 0;
     WorkIter it;
     work_begin(plan, blockIdx.x, it);
     Work w;
     while (work_next(plan, it, w)) {
       const bool got = mbar_wait(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
       if (!__all_sync(0xffffffffu, got)) break;
+      if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
       tc_fence_after();
       const int m_tile = w.tile % plan.m_tiles;
       const int n_tile = w.tile / plan.m_tiles;
@@ -404,6 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit);
+      ++unit;
       acc_phase ^= 1u;
     }
   }
@@ -759,9 +790,9 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.sfb1 = static_cast<const uint8_t*>(SFB1);
   kp.sfb2 = static_cast<const uint8_t*>(SFB2);
   kp.C = static_cast<__half*>(C);
-  kp.partials = static_cast<float*>(ws);
-  kp.counters = ws ? reinterpret_cast<int*>(static_cast<uint8_t*>(ws) +
-                                            workspace_counter_offset(plan))
+  kp.counters = static_cast<int*>(ws);
+  kp.partials = ws ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
+                                              workspace_partials_offset(plan))
                    : nullptr;
   kp.err = dev.err;
   dual_gemm_kernel<BN, FUSE><<<plan.grid, kThreads, Cf::kSmemBytes, stream>>>(
@@ -984,6 +1015,20 @@ int nvfp4_dual_gemm_device_status(int device, unsigned* word_out) {
 }
 
 const char* nvfp4_dual_gemm_last_error(void) { return g_last_error.c_str(); }
+
+#ifdef NVFP4DG_TRACE
+// Trace builds only: copy the stamp buffer ([160][6][64] int64) to the host.
+NVFP4DG_API int nvfp4_dual_gemm_trace_read(void* host, size_t bytes) {
+  if (bytes < sizeof(g_trace)) return NVFP4DG_ERR_INVALID;
+  cudaError_t e = cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace));
+  const long long zero[kTraceSlots] = {};
+  for (int c = 0; c < kTraceCtas && e == cudaSuccess; ++c)
+    for (int r = 0; r < kTraceRoles && e == cudaSuccess; ++r)
+      e = cudaMemcpyToSymbol(g_trace, zero, sizeof(zero),
+                             ((size_t)c * kTraceRoles + r) * sizeof(zero));
+  return e == cudaSuccess ? NVFP4DG_OK : NVFP4DG_ERR_CUDA;
+}
+#endif
 
 int nvfp4_dual_gemm_version(void) { return 100; }
 

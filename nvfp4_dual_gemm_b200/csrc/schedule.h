@@ -118,19 +118,20 @@ NVFP4DG_HD void sk_tile_owners(const Plan& p, long long ts, int* b_first,
   *b_last = sk_owner(p, ts * p.kblocks + p.kblocks - 1);
 }
 
-// Workspace layout: [partials: 2 * grid slots of 128 x 2*BN fp32]
-//                   [counters: one int per stream-K tile], 256-byte aligned.
+// Workspace layout, independent of the plan so that one buffer serves calls
+// with different plans: [counters: kCounterBytes, one int per stream-K tile,
+// always left at zero by a completed call][partials: 2 * grid slots of
+// 128 x 2*BN fp32].
+constexpr long long kCounterBytes = 64ll * 1024;  // 16384 tiles >= 2 * 4095
 NVFP4DG_HD long long partial_slot_floats(const Plan& p) {
   return 128ll * 2 * p.bn;
 }
-NVFP4DG_HD long long workspace_counter_offset(const Plan& p) {
-  const long long bytes = 2ll * p.grid * partial_slot_floats(p) * 4;
-  return (bytes + 255) / 256 * 256;
+NVFP4DG_HD long long workspace_partials_offset(const Plan&) {
+  return kCounterBytes;
 }
 NVFP4DG_HD long long workspace_bytes(const Plan& p) {
   if (p.sk_iters == 0) return 0;
-  const long long sk_tiles = p.num_tiles - p.dp_tiles;
-  return workspace_counter_offset(p) + (sk_tiles * 4 + 255) / 256 * 256;
+  return kCounterBytes + 2ll * p.grid * partial_slot_floats(p) * 4;
 }
 
 }  // namespace nvfp4dg

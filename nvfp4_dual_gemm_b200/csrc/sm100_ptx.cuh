@@ -4,7 +4,7 @@
 //
 // Written from the PTX ISA description of each instruction.  The reference
 // keeps equivalent wrappers in tcgen05-interface.cuh and tma-interface.cuh;
-// the differences that matter here: every wait is bounded by %globaltimer and
+// the differences that matter here: every wait is bounded by %clock64 and
 // reports through a device error word instead of spinning forever
 // (tma-interface.cuh:64-75 spins unbounded), and the TMEM base address
 // returned by tcgen05.alloc is always used instead of being assumed to be 0.
@@ -17,12 +17,6 @@ namespace nvfp4dg {
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
 }
 
 // ---------------------------------------------------------------------------
@@ -71,27 +65,42 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Time limit of every wait in the kernels of this library.  A legitimate wait
-// lasts microseconds; the limit only exists so that a logic error ends the
-// kernel with an error word instead of hanging the GPU.
-constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;  // 1 s
+// Time limit of every wait in the kernels of this library, in SM clock
+// cycles (about 1-2.5 s between the 1965 MHz boost clock and the ~1.3 GHz
+// power-capped clock).  A legitimate wait lasts microseconds; the limit only
+// exists so that a logic error ends the kernel with an error word instead of
+// hanging the GPU.  The SM-local %clock64 is used because it is a register
+// read; %globaltimer is a slow memory-mapped read that, taken on every missed
+// poll, serialised the whole pipeline.
+constexpr long long kWaitLimitCycles = 2500ll * 1000ll * 1000ll;
+
+__device__ __forceinline__ long long clock_cycles() {
+  long long t;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+  return t;
+}
 
 // Wait until the phase with parity `parity` of `bar` has completed.  Returns
-// false (after setting `code` in *err) if the time limit expires, or at once
-// if *err is already non-zero because another role gave up.
+// false (after setting `code` in *err) if the time limit expires, or early if
+// *err is already non-zero because another role gave up.
 // With bail_on_err = false the wait ignores *err and only the time limit
 // ends it (used to drain copies and MMAs before the CTA exits).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           unsigned* err, unsigned code,
                                           bool bail_on_err = true) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  long long t0 = 0;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0u) {
+    if ((i & 1023u) == 0u) {
+      const long long now = clock_cycles();
+      if (t0 == 0) {
+        t0 = now;
+        continue;
+      }
       if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u)
         return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (now - t0 > kWaitLimitCycles) {
         atomicOr(err, code);
         return false;
       }

@@ -199,7 +199,7 @@ def test_property_doubling_b2_scales_doubles_output():
     a1 = np.abs(c1.astype(np.float32))
     # fp16 normal range on both sides: doubling a subnormal is not exact
     fin = np.isfinite(c2) & (a1 < 30000) & (a1 >= 2.0 ** -13)
-    assert fin.mean() > 0.9
+    assert fin.mean() > 0.4  # silu sends about half the outputs to ~0
     want = (c1[fin].astype(np.float32) * 2).astype(np.float16)
     bad = int((c2[fin] != want).sum())
     assert bad == 0, f"{bad} of {fin.sum()} outputs did not double exactly"
@@ -217,6 +217,16 @@ def test_property_row_permutation_equivariance():
     c = run(p, _lib.FLAG_NO_STREAMK)
     cp = run(q, _lib.FLAG_NO_STREAMK)
     assert np.array_equal(cp, c[perm])
+
+
+def test_workspace_shared_across_plans(streamk_problem):
+    # One library-owned workspace serves calls whose plans differ in tile
+    # width and grid; the counters must never alias earlier partials.
+    p, ref = streamk_problem
+    for flags in (_lib.FLAG_BN64 | 13, _lib.FLAG_BN128 | 3, _lib.FLAG_BN64 | 7,
+                  _lib.FLAG_BN128 | 5, _lib.FLAG_BN128 | 3):
+        got = run(p, flags | _lib.FLAG_FORCE_STREAMK)
+        assert_close(got, ref, f"flags={flags:#x}")
 
 
 def test_caller_owned_workspace_matches_library_workspace(streamk_problem):
