@@ -296,7 +296,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           NVFP4DG_STAMP(2, consumed);
-          tc_fence_after();
+          // No tcgen05 fence here: the mbarrier completion already orders the
+          // TMA writes before the MMAs that read them, and a fence per K block
+          // would serialise the tensor pipe.
           const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
           const uint32_t b_addr = a_addr + Cf::kABytes;
           const uint32_t sf_addr = b_addr + 2 * Cf::kBBytes;
