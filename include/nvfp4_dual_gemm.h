@@ -62,8 +62,6 @@ extern "C" {
 #define NVFP4DG_FLAG_NO_STREAMK (1u << 14) /* whole tiles only (no K split)     */
 #define NVFP4DG_FLAG_SYNC_CHECK (1u << 15) /* synchronize and read the device
                                               error word after the launch       */
-#define NVFP4DG_FLAG_SPLIT_MMA (1u << 16) /* BN=128: two N=128 MMAs per K step
-                                             instead of one N=256 MMA           */
 #define NVFP4DG_FLAG_FORCE_STREAMK (1u << 17) /* always split the last waves of
                                                  tiles along K (stream-K)      */
 

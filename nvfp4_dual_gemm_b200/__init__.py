@@ -19,7 +19,6 @@ from ._lib import (  # noqa: F401
     FLAG_BN128,
     FLAG_FORCE_STREAMK,
     FLAG_NO_STREAMK,
-    FLAG_SPLIT_MMA,
     FLAG_SYNC_CHECK,
     NativeLibraryError,
 )

@@ -28,7 +28,6 @@ FLAG_BN64 = 1 << 12
 FLAG_BN128 = 1 << 13
 FLAG_NO_STREAMK = 1 << 14
 FLAG_SYNC_CHECK = 1 << 15
-FLAG_SPLIT_MMA = 1 << 16
 FLAG_FORCE_STREAMK = 1 << 17
 
 # Every symbol the header declares, with (restype, argtypes).

@@ -1,21 +1,17 @@
 // dual_gemm.cu — B200 (sm_100a) NVFP4 dual GEMM  C = silu(A B1^T) * (A B2^T)
 //
 // One persistent, warp-specialised kernel per tile width BN (64 or 128
-// columns of each GEMM), 192 threads per CTA, one CTA per SM:
-//   warp 4    TMA producer: per 256-wide K block streams the A tile
-//             (128 x 128 B), the B1 and B2 tiles (BN x 128 B each, stacked so
-//             that together they form one 2*BN-row operand) and the three
-//             2 KiB block-scale runs through a ring of shared-memory stages;
-//   warp 5    TMEM owner and MMA issuer: copies the scales of each stage into
-//             a per-stage TMEM region (tcgen05.cp) and issues
-//             tcgen05.mma kind::mxf4nvf4 block_scale into one TMEM
-//             accumulator of 2*BN fp32 columns (d1 | d2).  With BN = 128 a
-//             single N = 256 MMA per K step computes both GEMMs from one read
-//             of the A tile; with BN = 64 two N = 64 MMAs share it;
-//   warps 0-3 epilogue: tcgen05.ld of d1 and d2, silu(d1) * d2 in fp32,
-//             fp16 row stores; for tiles split along K the fp32 partials go
-//             through the workspace and the last segment to arrive finishes.
-// The reference kernel is non-persistent with one tile per CTA
+// columns of each GEMM); warp roles are described above dual_gemm_kernel.
+// Per 256-wide K block the producers stream the A tile (128 x 128 B), the B1
+// and B2 tiles (BN x 128 B each, stacked into one 2*BN-row operand) and the
+// three 2 KiB block-scale runs through a ring of shared-memory stages; the
+// MMA thread issues four tcgen05.mma kind::mxf4nvf4 block_scale (M = 128,
+// N = 2*BN, K = 64) into one TMEM accumulator whose columns [0, BN) hold
+// A B1^T and [BN, 2*BN) hold A B2^T; the epilogue computes silu(x) * y in
+// fp32 and stores fp16 rows, or, for tiles split along K, hands fp32
+// partials through the workspace to the last segment to finish.
+// The reference kernel is non-persistent with one tile per CTA and issues
+// the scale copies and two MMAs per K step from one thread
 // (nvfp4_dual_gemm.cu:77-317); the scheduling here is in schedule.h.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -40,7 +36,7 @@ constexpr int kBM = 128;            // tile rows (TMEM lanes)
 constexpr int kRowBytes = 128;      // one stage = 256 fp4 of K = 128 bytes/row
 constexpr int kSfAtomBytes = 512;   // 128 rows x 4 scales
 constexpr int kSfRunBytes = 2048;   // 4 atoms = the scales of 256 K elements
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;
 constexpr int kTmemCols = 512;
 constexpr int kSfTmemBase = 256;    // scale regions follow the accumulator
 constexpr int kSfTmemPerStage = 48; // SFA 4 x 4 cols, SFB 4 x (4 + 4) cols
@@ -152,11 +148,33 @@ __device__ __forceinline__ void add_f32x32(float (&v)[32], const float* src) {
   }
 }
 
-// FUSE (BN = 128 only): one N = 256 MMA per K step over the stacked B1|B2
-// operand, reading the 8 TMEM scale columns of B1's and B2's atoms side by
-// side.  Without FUSE: two MMAs with N = BN per K step; the first keeps the A
-// tile in the collector and the second reuses it.
-template <int BN, bool FUSE>
+// Warp roles (352 threads, one CTA per SM):
+//   warps 0-3   epilogue (warp w reads TMEM lanes 32w..32w+31 = tile rows)
+//   warp 4      producer A: A tile (TMA) + the three scale runs (bulk copies)
+//   warp 5      producer B: B1 and B2 tiles (TMA)
+//   warp 6      TMEM owner and MMA issuer (one elected thread)
+//   warps 7-10  scale warps, one per TMEM sub-partition (warp % 4)
+// Per K block the scale warps read the 512-byte scale atoms from shared
+// memory and write them into a per-stage TMEM region with tcgen05.st, each
+// warp filling its own 32 lanes with the layout the block-scaled MMA reads:
+// lane 32q+i, column c of a 4-column group holds the 4 scales of row
+// i + 32c for that 64-wide K step — the row of the 128x4 atom.  Writing the
+// scales from four warps keeps the MMA thread's instruction stream down to
+// the four MMAs of the K block: every tcgen05 instruction costs one issuing
+// thread ~50-70 cycles, so moving the twelve scale copies per K block off
+// the MMA thread (as tcgen05.cp issued by the MMA thread would require) is
+// what lets the tensor pipe run at its own rate.  It also lets the B-operand
+// scales of a 64-row tile (half an atom) sit next to each other, so both
+// GEMMs always run as one MMA with N = 2 * BN over the stacked B1|B2 tile.
+constexpr int kEpiWarps = 4;
+constexpr int kProdAWarp = 4;
+constexpr int kProdBWarp = 5;
+constexpr int kMmaWarp = 6;
+constexpr int kSfWarp0 = 7;
+constexpr int kSfWarps = 4;
+static_assert(kThreads == 32 * (kSfWarp0 + kSfWarps), "thread count");
+
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB1,
@@ -164,9 +182,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const KParams p) {
   using Cf = Cfg<BN>;
   constexpr int S = Cf::kStages;
+  constexpr uint32_t kBytesA = Cf::kABytes + 3 * kSfRunBytes;
+  constexpr uint32_t kBytesB = 2 * Cf::kBBytes;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[S];
+  __shared__ __align__(8) uint64_t sf_bar[S];
   __shared__ __align__(8) uint64_t empty_bar[S];
   __shared__ __align__(8) uint64_t acc_full_bar;
   __shared__ __align__(8) uint64_t acc_empty_bar;
@@ -183,13 +204,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
   const Plan& plan = p.plan;
 
-  if (warp == 4 && lane == 0) {
+  if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&full_bar[s], 2);          // producers A and B
+      mbar_init(&sf_bar[s], kSfWarps);     // one arrival per scale warp
+      mbar_init(&empty_bar[s], 1);         // tcgen05.commit of the MMAs
     }
     mbar_init(&acc_full_bar, 1);
-    mbar_init(&acc_empty_bar, 128);
+    mbar_init(&acc_empty_bar, 32 * kEpiWarps);
     mbar_init(&drain_bar, 1);
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -197,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmB1);
     prefetch_tmap(&tmB2);
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&tmem_base_sh, kTmemCols);
     tmem_relinquish();
   }
@@ -207,9 +229,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;  // scale atoms per 128-row block
 
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
+  if (warp == kProdAWarp || warp == kProdBWarp) {
+    // ------------------------------------------------------------ producers
     if (lane == 0) {
+      const bool is_a = (warp == kProdAWarp);
       const uint64_t pol_a = policy_evict_last();
       const uint64_t pol_b = policy_evict_normal();
       int stage = 0;
@@ -233,22 +256,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          NVFP4DG_STAMP(0, issued);
           uint8_t* st = smem + stage * Cf::kStageBytes;
-          uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
-          mbar_arrive_expect_tx(&full_bar[stage], Cf::kStageBytes);
-          tma_load_2d(st, &tmA, &full_bar[stage], kb * kRowBytes, row_a, pol_a);
-          tma_load_2d(st + Cf::kABytes, &tmB1, &full_bar[stage],
-                      kb * kRowBytes, row_b, pol_b);
-          tma_load_2d(st + Cf::kABytes + Cf::kBBytes, &tmB2, &full_bar[stage],
-                      kb * kRowBytes, row_b, pol_b);
-          bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
-                    &full_bar[stage], pol_a);
-          bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
-                    kSfRunBytes, &full_bar[stage], pol_b);
-          bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
-                    kSfRunBytes, &full_bar[stage], pol_b);
-          NVFP4DG_STAMP(1, issued);
+          if (is_a) {
+            NVFP4DG_STAMP(0, issued);
+            uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
+            mbar_arrive_expect_tx(&full_bar[stage], kBytesA);
+            tma_load_2d(st, &tmA, &full_bar[stage], kb * kRowBytes, row_a,
+                        pol_a);
+            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
+                      &full_bar[stage], pol_a);
+            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &full_bar[stage], pol_b);
+            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &full_bar[stage], pol_b);
+            NVFP4DG_STAMP(1, issued);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], kBytesB);
+            tma_load_2d(st + Cf::kABytes, &tmB1, &full_bar[stage],
+                        kb * kRowBytes, row_b, pol_b);
+            tma_load_2d(st + Cf::kABytes + Cf::kBBytes, &tmB2,
+                        &full_bar[stage], kb * kRowBytes, row_b, pol_b);
+          }
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -256,8 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // Never leave with copies in flight: wait (bounded) until the last
-      // load issued into each stage has landed.
+      // Never leave with copies in flight: wait (bounded) until every stage
+      // has completed the fill that holds this thread's last copies.
       for (int s = 0; s < S; ++s) {
         if (issued > s) {
           const long long fill = (issued - 1 - s) / S;
@@ -267,11 +295,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp >= kSfWarp0) {
+    // ------------------------------------------------------------ scale warps
+    // This warp owns TMEM lanes 32q..32q+31; thread i writes lane 32q+i.
+    const uint32_t q = static_cast<uint32_t>(warp % 4);
+    const uint32_t t_lane = tmem + ((32u * q) << 16);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    WorkIter it;
+    work_begin(plan, blockIdx.x, it);
+    Work w;
+    while (ok && work_next(plan, it, w)) {
+      // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
+      // atom words 2h and 2h+1 (rows 64h .. 64h+63).
+      const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        const bool got = mbar_wait(&full_bar[stage], phase, p.err, kErrMma);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
+                                       Cf::kABytes + 2 * Cf::kBBytes) +
+                              16u * lane;
+        const uint32_t col = kSfTmemBase + stage * kSfTmemPerStage;
+        uint32_t ra[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 v = lds128(sf_s + j * kSfAtomBytes);
+          ra[4 * j + 0] = v.x;
+          ra[4 * j + 1] = v.y;
+          ra[4 * j + 2] = v.z;
+          ra[4 * j + 3] = v.w;
+        }
+        __syncwarp();
+        tc_st_16cols(t_lane + col, ra);
+        if constexpr (BN == 128) {
+          // per K step j: 4 columns of B1's atom, then 4 of B2's
+          uint32_t rb[32];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v1 = lds128(sf_s + kSfRunBytes + j * kSfAtomBytes);
+            const uint4 v2 = lds128(sf_s + 2 * kSfRunBytes + j * kSfAtomBytes);
+            rb[8 * j + 0] = v1.x;
+            rb[8 * j + 1] = v1.y;
+            rb[8 * j + 2] = v1.z;
+            rb[8 * j + 3] = v1.w;
+            rb[8 * j + 4] = v2.x;
+            rb[8 * j + 5] = v2.y;
+            rb[8 * j + 6] = v2.z;
+            rb[8 * j + 7] = v2.w;
+          }
+          tc_st_32cols(t_lane + col + 16, rb);
+        } else {
+          // per K step j: B1 rows 0-31 / 32-63 of the tile, then B2's
+          uint32_t rb[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v1 = lds128(sf_s + kSfRunBytes + j * kSfAtomBytes);
+            const uint4 v2 = lds128(sf_s + 2 * kSfRunBytes + j * kSfAtomBytes);
+            rb[4 * j + 0] = half ? v1.z : v1.x;
+            rb[4 * j + 1] = half ? v1.w : v1.y;
+            rb[4 * j + 2] = half ? v2.z : v2.x;
+            rb[4 * j + 3] = half ? v2.w : v2.y;
+          }
+          tc_st_16cols(t_lane + col + 16, rb);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sf_bar[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdesc =
-          FUSE ? idesc_nvf4(128, 2 * BN) : idesc_nvf4(128, BN);
+      constexpr uint32_t kIdesc = idesc_nvf4(128, 2 * BN);
+      constexpr uint32_t kSfbStep = (BN == 128) ? 8u : 4u;
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
@@ -281,58 +386,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       work_begin(plan, blockIdx.x, it);
       Work w;
       while (ok && work_next(plan, it, w)) {
-        const int n_tile = w.tile / plan.m_tiles;
-        // BN = 64: the tile is one half of a 128-row scale atom; its scales
-        // sit in atom columns 0-1 (upper half: 2-3) of the copied block.
-        const uint32_t sfb_half = (BN == 64) ? (uint32_t)(n_tile & 1) * 2u : 0u;
         if (!mbar_wait(&acc_empty_bar, acc_phase ^ 1u, p.err, kErrMma)) {
           ok = false;
           break;
         }
         tc_fence_after();
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma)) {
+          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma) ||
+              !mbar_wait(&sf_bar[stage], phase, p.err, kErrMma)) {
             ok = false;
             break;
           }
           NVFP4DG_STAMP(2, consumed);
-          // No tcgen05 fence here: the mbarrier completion already orders the
-          // TMA writes before the MMAs that read them, and a fence per K block
-          // would serialise the tensor pipe.
+          tc_fence_after();  // orders the scale warps' tcgen05.st before us
           const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
           const uint32_t b_addr = a_addr + Cf::kABytes;
-          const uint32_t sf_addr = b_addr + 2 * Cf::kBBytes;
           const uint32_t sf_t = tmem + kSfTmemBase + stage * kSfTmemPerStage;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint32_t sfa_t = sf_t + 4 * j;
-            const uint32_t sfb_t = sf_t + 16 + 8 * j;
-            tc_cp_32x128b_x4(sfa_t, smem_desc(sf_addr + j * kSfAtomBytes, 128,
-                                              128, SmemLayout::kNone));
-            tc_cp_32x128b_x4(sfb_t,
-                             smem_desc(sf_addr + kSfRunBytes + j * kSfAtomBytes,
-                                       128, 128, SmemLayout::kNone));
-            tc_cp_32x128b_x4(
-                sfb_t + 4, smem_desc(sf_addr + 2 * kSfRunBytes + j * kSfAtomBytes,
-                                     128, 128, SmemLayout::kNone));
-            const uint32_t accum = (kb > w.kb0 || j > 0) ? 1u : 0u;
             const uint64_t a_desc = smem_desc(a_addr + 32 * j, 16, 1024,
                                               SmemLayout::kSwizzle128B);
-            if constexpr (FUSE) {
-              const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
-                                                SmemLayout::kSwizzle128B);
-              tc_mma_nvf4(tmem, a_desc, b_desc, kIdesc, sfa_t, sfb_t, accum);
-            } else {
-              const uint64_t b1_desc = smem_desc(b_addr + 32 * j, 16, 1024,
-                                                 SmemLayout::kSwizzle128B);
-              const uint64_t b2_desc =
-                  smem_desc(b_addr + Cf::kBBytes + 32 * j, 16, 1024,
-                            SmemLayout::kSwizzle128B);
-              tc_mma_nvf4<kCollFill>(tmem, a_desc, b1_desc, kIdesc, sfa_t,
-                                     sfb_t + sfb_half, accum);
-              tc_mma_nvf4<kCollLastUse>(tmem + BN, a_desc, b2_desc, kIdesc,
-                                        sfa_t, sfb_t + 4 + sfb_half, accum);
-            }
+            const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
+                                              SmemLayout::kSwizzle128B);
+            tc_mma_nvf4(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
+                        sf_t + 16 + kSfbStep * j,
+                        (kb > w.kb0 || j > 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[stage]);
           NVFP4DG_STAMP(3, consumed);
@@ -346,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit(&acc_full_bar);
         acc_phase ^= 1u;
       }
-      // No MMA or scale copy may still be running when TMEM is released.
+      // No MMA may still be running when TMEM is released.
       tc_commit(&drain_bar);
       mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
     }
@@ -444,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -554,7 +632,6 @@ struct DevInfo {
   int minor = 0;
   bool attr64 = false;
   bool attr128 = false;
-  bool attr128f = false;
   unsigned* err = nullptr;
 };
 std::map<int, DevInfo> g_dev;
@@ -764,16 +841,16 @@ int check_problem(const void* A, const void* B1, const void* B2,
   return NVFP4DG_OK;
 }
 
-template <int BN, bool FUSE>
+template <int BN>
 int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
            const void* B1, const void* B2, const void* SFA, const void* SFB1,
            const void* SFB2, void* C, int M, int N, int K, void* ws,
            cudaStream_t stream) {
   using Cf = Cfg<BN>;
-  bool& attr = (BN == 64) ? dev.attr64 : (FUSE ? dev.attr128f : dev.attr128);
+  bool& attr = (BN == 64) ? dev.attr64 : dev.attr128;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(
-        dual_gemm_kernel<BN, FUSE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        dual_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
         Cf::kSmemBytes);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr = true;
@@ -797,7 +874,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
                                               workspace_partials_offset(plan))
                    : nullptr;
   kp.err = dev.err;
-  dual_gemm_kernel<BN, FUSE><<<plan.grid, kThreads, Cf::kSmemBytes, stream>>>(
+  dual_gemm_kernel<BN><<<plan.grid, kThreads, Cf::kSmemBytes, stream>>>(
       ta, tb1, tb2, kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dual_gemm_kernel launch");
@@ -876,15 +953,12 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   } else {
     ws = nullptr;
   }
-  if (plan.bn == 128 && (flags & NVFP4DG_FLAG_SPLIT_MMA))
-    rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, stream);
-  else if (plan.bn == 128)
-    rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, stream);
+  if (plan.bn == 128)
+    rc = launch<128>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M, N, K,
+                     ws, stream);
   else
-    rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, stream);
+    rc = launch<64>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M, N, K,
+                    ws, stream);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;

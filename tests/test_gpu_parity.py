@@ -34,7 +34,6 @@ VARIANTS = {
     "auto": 0,
     "bn64": _lib.FLAG_BN64,
     "bn128_fused": _lib.FLAG_BN128,
-    "bn128_split": _lib.FLAG_BN128 | _lib.FLAG_SPLIT_MMA,
     "whole_tiles": _lib.FLAG_NO_STREAMK,
 }
 
