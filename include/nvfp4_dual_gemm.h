@@ -64,6 +64,8 @@ extern "C" {
                                               error word after the launch       */
 #define NVFP4DG_FLAG_FORCE_STREAMK (1u << 17) /* always split the last waves of
                                                  tiles along K (stream-K)      */
+#define NVFP4DG_FLAG_PAIR (1u << 18)    /* force 2-SM pair tiles (256 rows)    */
+#define NVFP4DG_FLAG_NO_PAIR (1u << 19) /* force single-CTA tiles (128 rows)   */
 
 /*
  * Run the dual GEMM on `stream` using a workspace the library keeps per
@@ -127,18 +129,20 @@ NVFP4DG_API int nvfp4_dual_gemm_device_status(int device, unsigned* word_out);
 
 /*
  * Describe the schedule the library would use: writes the tile width per
- * GEMM, persistent grid size, whole-tile count and the number of tiles split
- * along K.  Host-only; usable without a GPU when `num_sms` > 0.
+ * GEMM, the CTAs per work unit (1, or 2 for 2-SM pair tiles of 256 rows),
+ * the persistent grid in work units, the whole-tile count and the number of
+ * tiles split along K.  Host-only; usable without a GPU when `num_sms` > 0.
  */
 NVFP4DG_API int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
-                         int* bn_out, int* grid_out, int* dp_tiles_out,
-                         int* sk_tiles_out);
+                         int* bn_out, int* ctas_out, int* grid_out,
+                         int* dp_tiles_out, int* sk_tiles_out);
 
 /*
- * Enumerate the work of CTA `cta` under the plan for (M, N, K, flags,
- * num_sms): writes up to `cap` records of 4 ints (tile, kb_begin, kb_end,
- * slot; slot = -1 for a whole tile) and returns the record count, or -1 on
- * error.  Host-only mirror of the device scheduler, for tests and tooling.
+ * Enumerate the work of work unit `cta` (a CTA, or a CTA pair) under the plan
+ * for (M, N, K, flags, num_sms): writes up to `cap` records of 4 ints (tile,
+ * kb_begin, kb_end, slot; slot = -1 for a whole tile) and returns the record
+ * count, or -1 on error.  Host-only mirror of the device scheduler, for tests
+ * and tooling.
  */
 NVFP4DG_API int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, int num_sms,
                               int cta, int* records, int cap);

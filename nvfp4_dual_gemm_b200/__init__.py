@@ -18,7 +18,9 @@ from ._lib import (  # noqa: F401
     FLAG_BN64,
     FLAG_BN128,
     FLAG_FORCE_STREAMK,
+    FLAG_NO_PAIR,
     FLAG_NO_STREAMK,
+    FLAG_PAIR,
     FLAG_SYNC_CHECK,
     NativeLibraryError,
 )

@@ -29,6 +29,8 @@ FLAG_BN128 = 1 << 13
 FLAG_NO_STREAMK = 1 << 14
 FLAG_SYNC_CHECK = 1 << 15
 FLAG_FORCE_STREAMK = 1 << 17
+FLAG_PAIR = 1 << 18
+FLAG_NO_PAIR = 1 << 19
 
 # Every symbol the header declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -43,7 +45,8 @@ SIGNATURES = {
                                                 _vp]),
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "nvfp4_dual_gemm_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
-    "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip]),
+    "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip,
+                                  _ip]),
     "nvfp4_dual_gemm_plan_work": (_i, [_i, _i, _i, _u, _i, _i, _ip, _i]),
     "nvfp4_dual_gemm_last_error": (ctypes.c_char_p, []),
     "nvfp4_dual_gemm_version": (_i, []),

@@ -165,18 +165,19 @@ def workspace_size(M: int, N: int, K: int, flags: int = 0,
 def plan(M: int, N: int, K: int, flags: int = 0, num_sms: int = 148) -> dict:
     """The schedule the library would use (host-only; needs no GPU)."""
     lib = _lib.load()
-    bn, grid, dp, sk = (ctypes.c_int() for _ in range(4))
+    bn, ctas, grid, dp, sk = (ctypes.c_int() for _ in range(5))
     rc = lib.nvfp4_dual_gemm_plan(M, N, K, flags, num_sms, ctypes.byref(bn),
-                                  ctypes.byref(grid), ctypes.byref(dp),
-                                  ctypes.byref(sk))
+                                  ctypes.byref(ctas), ctypes.byref(grid),
+                                  ctypes.byref(dp), ctypes.byref(sk))
     _lib.check(rc, "nvfp4_dual_gemm_plan")
-    return {"bn": bn.value, "grid": grid.value, "dp_tiles": dp.value,
-            "sk_tiles": sk.value}
+    return {"bn": bn.value, "ctas": ctas.value, "grid": grid.value,
+            "dp_tiles": dp.value, "sk_tiles": sk.value}
 
 
 def plan_work(M: int, N: int, K: int, cta: int, flags: int = 0,
               num_sms: int = 148) -> list[tuple[int, int, int, int]]:
-    """Work records (tile, kb_begin, kb_end, slot) of one CTA (host-only)."""
+    """Work records (tile, kb_begin, kb_end, slot) of one work unit (a CTA or
+    a 2-SM CTA pair; host-only)."""
     lib = _lib.load()
     n = lib.nvfp4_dual_gemm_plan_work(M, N, K, flags, num_sms, cta, None, 0)
     if n < 0:

@@ -530,6 +530,396 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ===========================================================================
+// 2-SM pair kernel (cta_group::2): a cluster of two CTAs computes a
+// 256 x BN tile of both GEMMs.  The even CTA issues M = 256, N = 2*BN MMAs;
+// CTA r holds A rows [128r, 128r + 128) of the tile and the r-th half of the
+// stacked B operand, i.e. the B1 tile in CTA 0 and the B2 tile in CTA 1, so
+// each byte of B1 and B2 is loaded once per pair and every SM streams
+// 16 + BN/8 KiB of operands per K block instead of 16 + BN/4 KiB.  Each CTA
+// keeps its own scales in TMEM (its A rows, and all 2*BN B rows), and
+// receives its 128 rows of the accumulator, so the epilogue is unchanged.
+// Cross-CTA signals: both CTAs' A/B copies complete on the even CTA's
+// `full` barrier; the odd CTA's scale warps and epilogue arrive remotely on
+// the even CTA's `sf_ready` / `acc_empty`; the even CTA's MMA thread commits
+// to both CTAs' `empty` / `acc_full` barriers.
+// ===========================================================================
+template <int BN>
+struct PairCfg {
+  static constexpr int kStages = (BN == 128) ? 5 : 7;
+  static constexpr int kABytes = kBM * kRowBytes;  // this CTA's A rows
+  static constexpr int kBBytes = BN * kRowBytes;   // this CTA's B half
+  static constexpr int kStageBytes = kABytes + kBBytes + 3 * kSfRunBytes;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  static constexpr int kSfBase = 2 * BN;  // scale regions follow the acc.
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-B aligned");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+  static_assert(kSfBase + kStages * kSfTmemPerStage <= kTmemCols,
+                "TMEM budget");
+};
+
+template <int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    dual_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                          const __grid_constant__ CUtensorMap tmB1,
+                          const __grid_constant__ CUtensorMap tmB2,
+                          const KParams p) {
+  using Cf = PairCfg<BN>;
+  constexpr int S = Cf::kStages;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[S];    // even CTA: A/B of both
+  __shared__ __align__(8) uint64_t sfdata_bar[S];  // own scale runs landed
+  __shared__ __align__(8) uint64_t sf_bar[S];      // even CTA: scales in TMEM
+  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ __align__(8) uint64_t acc_full_bar;
+  __shared__ __align__(8) uint64_t acc_empty_bar;  // even CTA: both drained
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int finisher_sh;
+
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const Plan& plan = p.plan;
+  const uint32_t rank = cluster_ctarank();
+  const int unit = blockIdx.x >> 1;  // the pair's work-unit index
+  const bool leader = (rank == 0);
+
+  if (warp == kProdAWarp && lane == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);           // even CTA's producer A
+      mbar_init(&sfdata_bar[s], 1);         // own producer A
+      mbar_init(&sf_bar[s], 2 * kSfWarps);  // scale warps of both CTAs
+      mbar_init(&empty_bar[s], 1);          // MMA commit
+    }
+    mbar_init(&acc_full_bar, 1);
+    mbar_init(&acc_empty_bar, 2 * kEpiWarps);
+    mbar_init(&drain_bar, 1);
+    fence_mbar_init();
+    fence_proxy_async_smem();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
+  }
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(&tmem_base_sh, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int kblk64 = p.K / 64;
+
+  if (warp == kProdAWarp || warp == kProdBWarp) {
+    // ------------------------------------------------------------ producers
+    if (lane == 0) {
+      const bool is_a = (warp == kProdAWarp);
+      const uint64_t pol_a = policy_evict_last();
+      const uint64_t pol_b = policy_evict_normal();
+      const CUtensorMap* tmB = (rank == 0) ? &tmB1 : &tmB2;
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      bool ok = true;
+      WorkIter it;
+      work_begin(plan, unit, it);
+      Work w;
+      while (ok && work_next(plan, it, w)) {
+        const int m_tile = w.tile % plan.m_tiles;
+        const int n_tile = w.tile / plan.m_tiles;
+        const int row_a = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+        const int row_b = n_tile * BN;
+        const uint8_t* sfa =
+            p.sfa + (size_t)(m_tile * 2 + rank) * kblk64 * kSfAtomBytes;
+        const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
+        const uint8_t* sfb1 = p.sfb1 + sfb_off;
+        const uint8_t* sfb2 = p.sfb2 + sfb_off;
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
+                                 kErrProducer)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + stage * Cf::kStageBytes;
+          const uint32_t full_c = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (is_a) {
+            if (leader)
+              mbar_arrive_expect_tx(&full_bar[stage],
+                                    2 * (Cf::kABytes + Cf::kBBytes));
+            uint8_t* sf = st + Cf::kABytes + Cf::kBBytes;
+            mbar_arrive_expect_tx(&sfdata_bar[stage], 3 * kSfRunBytes);
+            tma_load_2d_pair(st, &tmA, full_c, kb * kRowBytes, row_a, pol_a);
+            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
+                      &sfdata_bar[stage], pol_a);
+            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &sfdata_bar[stage], pol_b);
+            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &sfdata_bar[stage], pol_b);
+          } else {
+            tma_load_2d_pair(st + Cf::kABytes, tmB, full_c, kb * kRowBytes,
+                             row_b, pol_b);
+          }
+          ++issued;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Drain: the scale runs land on this CTA's own barrier; the A/B tiles
+      // of both CTAs land on the even CTA's `full` barrier, which its
+      // producer A drains (the odd CTA cannot pass the final cluster barrier
+      // before that).
+      for (int s = 0; s < S; ++s) {
+        if (issued > s && is_a) {
+          const uint32_t par =
+              static_cast<uint32_t>(((issued - 1 - s) / S) & 1);
+          mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain, false);
+          if (leader)
+            mbar_wait_cluster(&full_bar[s], par, p.err, kErrDrain, false);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp >= kSfWarp0) {
+    // ------------------------------------------------------------ scale warps
+    const uint32_t q = static_cast<uint32_t>(warp % 4);
+    const uint32_t t_lane = tmem + ((32u * q) << 16);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    WorkIter it;
+    work_begin(plan, unit, it);
+    Work w;
+    while (ok && work_next(plan, it, w)) {
+      const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        const bool got =
+            mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
+                                       Cf::kABytes + Cf::kBBytes) +
+                              16u * lane;
+        const uint32_t col = Cf::kSfBase + stage * kSfTmemPerStage;
+        uint32_t ra[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 v = lds128(sf_s + j * kSfAtomBytes);
+          ra[4 * j + 0] = v.x;
+          ra[4 * j + 1] = v.y;
+          ra[4 * j + 2] = v.z;
+          ra[4 * j + 3] = v.w;
+        }
+        __syncwarp();
+        tc_st_16cols(t_lane + col, ra);
+        if constexpr (BN == 128) {
+          uint32_t rb[32];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v1 = lds128(sf_s + kSfRunBytes + j * kSfAtomBytes);
+            const uint4 v2 = lds128(sf_s + 2 * kSfRunBytes + j * kSfAtomBytes);
+            rb[8 * j + 0] = v1.x;
+            rb[8 * j + 1] = v1.y;
+            rb[8 * j + 2] = v1.z;
+            rb[8 * j + 3] = v1.w;
+            rb[8 * j + 4] = v2.x;
+            rb[8 * j + 5] = v2.y;
+            rb[8 * j + 6] = v2.z;
+            rb[8 * j + 7] = v2.w;
+          }
+          tc_st_32cols(t_lane + col + 16, rb);
+        } else {
+          uint32_t rb[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint4 v1 = lds128(sf_s + kSfRunBytes + j * kSfAtomBytes);
+            const uint4 v2 = lds128(sf_s + 2 * kSfRunBytes + j * kSfAtomBytes);
+            rb[4 * j + 0] = half ? v1.z : v1.x;
+            rb[4 * j + 1] = half ? v1.w : v1.y;
+            rb[4 * j + 2] = half ? v2.z : v2.x;
+            rb[4 * j + 3] = half ? v2.w : v2.y;
+          }
+          tc_st_16cols(t_lane + col + 16, rb);
+        }
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&sf_bar[stage]), 0));
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && leader) {
+      constexpr uint32_t kIdesc = idesc_nvf4(256, 2 * BN);
+      constexpr uint32_t kSfbStep = (BN == 128) ? 8u : 4u;
+      const uint32_t peer = 1u;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      WorkIter it;
+      work_begin(plan, unit, it);
+      Work w;
+      while (ok && work_next(plan, it, w)) {
+        if (!mbar_wait_cluster(&acc_empty_bar, acc_phase ^ 1u, p.err,
+                               kErrMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (!mbar_wait_cluster(&full_bar[stage], phase, p.err, kErrMma) ||
+              !mbar_wait_cluster(&sf_bar[stage], phase, p.err, kErrMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
+          const uint32_t b_addr = a_addr + Cf::kABytes;
+          const uint32_t sf_t = tmem + Cf::kSfBase + stage * kSfTmemPerStage;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t a_desc = smem_desc(a_addr + 32 * j, 16, 1024,
+                                              SmemLayout::kSwizzle128B);
+            const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
+                                              SmemLayout::kSwizzle128B);
+            tc_mma_nvf4_pair(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
+                             sf_t + 16 + kSfbStep * j,
+                             (kb > w.kb0 || j > 0) ? 1u : 0u);
+          }
+          const uint32_t eb = smem_u32(&empty_bar[stage]);
+          tc_commit_pair(mapa_shared(eb, 0));
+          tc_commit_pair(mapa_shared(eb, peer));
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        const uint32_t ab = smem_u32(&acc_full_bar);
+        tc_commit_pair(mapa_shared(ab, 0));
+        tc_commit_pair(mapa_shared(ab, peer));
+        acc_phase ^= 1u;
+      }
+      tc_commit_pair(mapa_shared(smem_u32(&drain_bar), 0));
+      mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int row = threadIdx.x;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), 0);
+    uint32_t acc_phase = 0;
+    WorkIter it;
+    work_begin(plan, unit, it);
+    Work w;
+    while (work_next(plan, it, w)) {
+      const bool got =
+          mbar_wait_cluster(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int m_tile = w.tile % plan.m_tiles;
+      const int n_tile = w.tile / plan.m_tiles;
+      const int grow = m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
+      const bool row_ok = grow < p.M;
+      __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+      if (w.slot < 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32], y[32];
+          __syncwarp();
+          tc_ld_32cols(t_row + 32 * c, x);
+          tc_ld_32cols(t_row + BN + 32 * c, y);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+          }
+          if (row_ok) store_row32(crow + 32 * c, x, y);
+        }
+      } else {
+        float* mine = p.partials +
+                      (size_t)cta_slot(plan, w.slot, rank) *
+                          partial_slot_floats(plan) +
+                      (size_t)row * 2 * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float x[32], y[32];
+          __syncwarp();
+          tc_ld_32cols(t_row + 32 * c, x);
+          tc_ld_32cols(t_row + BN + 32 * c, y);
+          tc_wait_ld();
+          if (c == BN / 32 - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+          }
+          store_f32x32(mine + 32 * c, x);
+          store_f32x32(mine + BN + 32 * c, y);
+        }
+        __threadfence();
+        epi_bar();
+        const long long ts = w.tile - plan.dp_tiles;
+        int b_first, b_last;
+        sk_tile_owners(plan, ts, &b_first, &b_last);
+        int* counter = p.counters + ts * plan.ctas + rank;
+        if (threadIdx.x == 0) {
+          const int old = atomicAdd(counter, 1);
+          const int last = (old == b_last - b_first) ? 1 : 0;
+          if (last) *counter = 0;  // ready for the next launch
+          finisher_sh = last;
+        }
+        epi_bar();
+        if (finisher_sh) {
+          __threadfence();
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            float x[32], y[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              x[i] = 0.f;
+              y[i] = 0.f;
+            }
+            for (int b = b_first; b <= b_last; ++b) {
+              const float* src =
+                  p.partials +
+                  (size_t)cta_slot(plan, sk_slot(plan, b, ts), rank) *
+                      partial_slot_floats(plan) +
+                  (size_t)row * 2 * BN;
+              add_f32x32(x, src + 32 * c);
+              add_f32x32(y, src + BN + 32 * c);
+            }
+            if (row_ok) store_row32(crow + 32 * c, x, y);
+          }
+        }
+      }
+      acc_phase ^= 1u;
+    }
+  }
+
+  // ------------------------------------------------------------ teardown
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still signal it
+  if (warp == kMmaWarp) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, kTmemCols);
+  }
+}
+
+// ===========================================================================
 // NVFP4 quantiser (fp32 rows -> e2m1 codes + e4m3 block scales)
 // ===========================================================================
 // Eight fp32 values -> four bytes of e2m1 pairs (round to nearest even,
@@ -632,6 +1022,8 @@ struct DevInfo {
   int minor = 0;
   bool attr64 = false;
   bool attr128 = false;
+  bool attr64p = false;
+  bool attr128p = false;
   unsigned* err = nullptr;
 };
 std::map<int, DevInfo> g_dev;
@@ -728,60 +1120,67 @@ int tensor_map(const void* ptr, long long rows, long long row_bytes,
 }
 
 // ---------------------------------------------------------------- planning
-// Cost model (cycles of the busiest CTA) used to choose the tile width and
-// whether to split tiles along K.  Per 256-wide K block an SM issues 4 K
-// steps; the FP4 tensor pipe retires an M=128 x N=256 x K=64 MMA in ~128
-// cycles, so BN = 128 costs ~512 cycles per block and BN = 64 (two N = 64
-// MMAs) ~256.  A split tile costs its partial round trip through L2 at
-// ~64 B/cycle per SM.
-Plan plan_for(int M, int N, int K, int bn, int grid_cap, bool streamk,
-              bool force_sk = false) {
+// Cost model (cycles of the busiest SM) used to pick the tile width, single
+// CTA or 2-SM pair tiles, and whether to split tiles along K.  Measured on
+// B200: an SM streams its operands from L2 at ~55 B/cycle whatever the copy
+// sizes, so a K block costs max(bytes / 55, MMA cycles); the FP4 tensor pipe
+// retires an M=128, N=256, K=64 MMA in ~128 cycles (N=128: ~70); the
+// epilogue of a tile takes ~34 cycles per output column (not overlapped);
+// a split tile costs its fp32 partial round trip through L2.
+Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
+              bool streamk, bool force_sk) {
   Plan p{};
   p.bn = bn;
-  p.m_tiles = (M + kBM - 1) / kBM;
+  p.ctas = ctas;
+  p.m_tiles = (M + kBM * ctas - 1) / (kBM * ctas);
   p.n_tiles = N / bn;
   p.kblocks = K / 256;
   p.num_tiles = p.m_tiles * p.n_tiles;
   const int T = p.num_tiles;
-  if (!streamk || (T % grid_cap == 0 && !force_sk)) {
-    p.grid = std::min(T, grid_cap);
+  if (!streamk || (T % unit_cap == 0 && !force_sk)) {
+    p.grid = std::min(T, unit_cap);
     p.dp_tiles = T;
     p.sk_iters = 0;
     return p;
   }
-  const int waves = T / grid_cap;
-  p.dp_tiles = waves >= 2 ? (waves - 1) * grid_cap : 0;
+  const int waves = T / unit_cap;
+  p.dp_tiles = waves >= 2 ? (waves - 1) * unit_cap : 0;
   const long long sk_total = (long long)(T - p.dp_tiles) * p.kblocks;
-  p.grid = (int)std::min<long long>(grid_cap, sk_total);
-  if (p.dp_tiles > 0 && p.grid < grid_cap) p.grid = grid_cap;
+  p.grid = (int)std::min<long long>(unit_cap, sk_total);
+  if (p.dp_tiles > 0 && p.grid < unit_cap) p.grid = unit_cap;
   p.sk_iters = sk_total;
-  if (p.sk_iters > 0 && p.sk_iters < p.grid) p.grid = (int)p.sk_iters;
   return p;
 }
 
 double plan_cost(const Plan& p) {
-  const double per_block = (p.bn == 128) ? 512.0 : 256.0;
+  const double a_bytes = 128.0 * kRowBytes;
+  const double b_bytes = (p.ctas == 2 ? 1.0 : 2.0) * p.bn * kRowBytes;
+  const double bytes = a_bytes + b_bytes + 3.0 * kSfRunBytes;
+  const double mma = (p.bn == 128) ? 512.0 : 280.0;
+  const double per_block = std::max(bytes / 55.0, p.ctas == 2 && p.bn == 64
+                                                       ? 256.0
+                                                       : mma);
+  const double epi = 34.0 * p.bn;
   const double slot_bytes = 128.0 * 2 * p.bn * 4;
-  double iters = 0;
-  if (p.dp_tiles > 0)
-    iters += (double)((p.dp_tiles + p.grid - 1) / p.grid) * p.kblocks;
-  double partial = 0;
-  if (p.sk_iters > 0) {
-    const double per_cta = (double)((p.sk_iters + p.grid - 1) / p.grid);
-    iters += per_cta;
-    // every split tile writes and re-reads ~(segments) partials; charge the
-    // busiest CTA two writes and one finishing read of ~3 segments.
-    if (per_cta < p.kblocks || (p.sk_iters % p.kblocks) != 0 ||
-        (p.sk_iters / p.grid) % p.kblocks != 0)
-      partial = (2.0 + 3.0) * slot_bytes / 64.0;
+  double cost = 0;
+  if (p.dp_tiles > 0) {
+    const double tiles = (double)((p.dp_tiles + p.grid - 1) / p.grid);
+    cost += tiles * (p.kblocks * per_block + epi);
   }
-  return iters * per_block + partial + 2000.0;
+  if (p.sk_iters > 0) {
+    const double per_unit = (double)((p.sk_iters + p.grid - 1) / p.grid);
+    const bool split = (p.sk_iters % p.grid) != 0 ||
+                       ((p.sk_iters / p.grid) % p.kblocks) != 0;
+    cost += per_unit * per_block + epi * 2;
+    if (split) cost += 3.0 * slot_bytes / 55.0;
+  }
+  return cost + 2000.0;
 }
 
 Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
   const int forced = static_cast<int>(flags & NVFP4DG_FLAG_GRID_MASK);
-  const int cap = forced > 0 ? forced : sms;
   const bool streamk = (flags & NVFP4DG_FLAG_NO_STREAMK) == 0;
+  const bool force_sk = (flags & NVFP4DG_FLAG_FORCE_STREAMK) != 0;
   int bns[2];
   int nb = 0;
   if (flags & NVFP4DG_FLAG_BN64) {
@@ -792,16 +1191,24 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
     if (N % 128 == 0) bns[nb++] = 128;
     bns[nb++] = 64;
   }
+  int ctas_opts[2];
+  int nc = 0;
+  if (!(flags & NVFP4DG_FLAG_NO_PAIR) && sms >= 2) ctas_opts[nc++] = 2;
+  if (!(flags & NVFP4DG_FLAG_PAIR) || sms < 2) ctas_opts[nc++] = 1;
   Plan best{};
   double best_cost = 1e300;
-  const bool force_sk = (flags & NVFP4DG_FLAG_FORCE_STREAMK) != 0;
-  for (int i = 0; i < nb; ++i) {
-    for (int sk = force_sk ? 1 : 0; sk < (streamk ? 2 : 1); ++sk) {
-      Plan p = plan_for(M, N, K, bns[i], cap, sk == 1, force_sk);
-      const double c = plan_cost(p);
-      if (c < best_cost) {
-        best_cost = c;
-        best = p;
+  for (int c = 0; c < nc; ++c) {
+    const int ctas = ctas_opts[c];
+    // forced grid counts CTAs; pairs use half as many units
+    const int cap = std::max(1, (forced > 0 ? forced : sms) / ctas);
+    for (int i = 0; i < nb; ++i) {
+      for (int sk = force_sk ? 1 : 0; sk < (streamk ? 2 : 1); ++sk) {
+        Plan p = plan_for(M, N, K, bns[i], ctas, cap, sk == 1, force_sk);
+        const double cost = plan_cost(p);
+        if (cost < best_cost) {
+          best_cost = cost;
+          best = p;
+        }
       }
     }
   }
@@ -827,6 +1234,8 @@ int check_problem(const void* A, const void* B1, const void* B2,
   if ((flags & NVFP4DG_FLAG_FORCE_STREAMK) && (flags & NVFP4DG_FLAG_NO_STREAMK))
     return fail(NVFP4DG_ERR_INVALID,
                 "FORCE_STREAMK and NO_STREAMK flags are exclusive");
+  if ((flags & NVFP4DG_FLAG_PAIR) && (flags & NVFP4DG_FLAG_NO_PAIR))
+    return fail(NVFP4DG_ERR_INVALID, "PAIR and NO_PAIR flags are exclusive");
   if (M == 0 || N == 0) return NVFP4DG_OK;
   const void* ptrs[7] = {A, B1, B2, SFA, SFB1, SFB2, C};
   const char* names[7] = {"A", "B1", "B2", "SFA", "SFB1", "SFB2", "C"};
@@ -841,17 +1250,18 @@ int check_problem(const void* A, const void* B1, const void* B2,
   return NVFP4DG_OK;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
            const void* B1, const void* B2, const void* SFA, const void* SFB1,
            const void* SFB2, void* C, int M, int N, int K, void* ws,
            cudaStream_t stream) {
-  using Cf = Cfg<BN>;
-  bool& attr = (BN == 64) ? dev.attr64 : dev.attr128;
+  constexpr int kSmem = PAIR ? PairCfg<BN>::kSmemBytes : Cfg<BN>::kSmemBytes;
+  auto kernel = PAIR ? dual_gemm_pair_kernel<BN> : dual_gemm_kernel<BN>;
+  bool& attr = PAIR ? (BN == 64 ? dev.attr64p : dev.attr128p)
+                    : (BN == 64 ? dev.attr64 : dev.attr128);
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(
-        dual_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        Cf::kSmemBytes);
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr = true;
   }
@@ -874,8 +1284,8 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
                                               workspace_partials_offset(plan))
                    : nullptr;
   kp.err = dev.err;
-  dual_gemm_kernel<BN><<<plan.grid, kThreads, Cf::kSmemBytes, stream>>>(
-      ta, tb1, tb2, kp);
+  kernel<<<plan.grid * plan.ctas, kThreads, kSmem, stream>>>(ta, tb1, tb2,
+                                                              kp);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "dual_gemm_kernel launch");
   return NVFP4DG_OK;
@@ -953,12 +1363,18 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   } else {
     ws = nullptr;
   }
-  if (plan.bn == 128)
-    rc = launch<128>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M, N, K,
-                     ws, stream);
+  if (plan.ctas == 2 && plan.bn == 128)
+    rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                           N, K, ws, stream);
+  else if (plan.ctas == 2)
+    rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                          N, K, ws, stream);
+  else if (plan.bn == 128)
+    rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
+                            M, N, K, ws, stream);
   else
-    rc = launch<64>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M, N, K,
-                    ws, stream);
+    rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
+                           M, N, K, ws, stream);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;
@@ -1016,13 +1432,14 @@ size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
 }
 
 int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
-                         int* bn_out, int* grid_out, int* dp_tiles_out,
-                         int* sk_tiles_out) {
+                         int* bn_out, int* ctas_out, int* grid_out,
+                         int* dp_tiles_out, int* sk_tiles_out) {
   g_last_error.clear();
   if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 256 || num_sms <= 0)
     return fail(NVFP4DG_ERR_INVALID, "invalid problem for planning");
   const Plan p = choose_plan(M, N, K, flags, num_sms);
   if (bn_out) *bn_out = p.bn;
+  if (ctas_out) *ctas_out = p.ctas;
   if (grid_out) *grid_out = p.grid;
   if (dp_tiles_out) *dp_tiles_out = p.dp_tiles;
   if (sk_tiles_out) *sk_tiles_out = p.num_tiles - p.dp_tiles;

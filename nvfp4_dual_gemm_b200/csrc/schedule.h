@@ -28,14 +28,14 @@
 namespace nvfp4dg {
 
 struct Plan {
-  int m_tiles;      // ceil(M / 128)
+  int m_tiles;      // ceil(M / (128 * ctas))
   int n_tiles;      // N / BN
   int kblocks;      // K / 256
   int num_tiles;    // m_tiles * n_tiles
-  int grid;         // persistent CTAs
+  int grid;         // persistent work units (CTAs, or CTA pairs)
   int dp_tiles;     // whole tiles handed out round-robin (multiple of grid)
   int bn;           // tile width per GEMM (64 or 128)
-  int pad;
+  int ctas;         // CTAs per work unit: 1, or 2 for a 2-SM pair (M = 256)
   long long sk_iters;  // (num_tiles - dp_tiles) * kblocks
 };
 
@@ -119,10 +119,10 @@ NVFP4DG_HD void sk_tile_owners(const Plan& p, long long ts, int* b_first,
 }
 
 // Workspace layout, independent of the plan so that one buffer serves calls
-// with different plans: [counters: kCounterBytes, one int per stream-K tile,
-// always left at zero by a completed call][partials: 2 * grid slots of
-// 128 x 2*BN fp32].
-constexpr long long kCounterBytes = 64ll * 1024;  // 16384 tiles >= 2 * 4095
+// with different plans: [counters: kCounterBytes, one int per stream-K tile
+// and CTA of its work unit, always left at zero by a completed call]
+// [partials: 2 slots per CTA of 128 x 2*BN fp32].
+constexpr long long kCounterBytes = 64ll * 1024;  // 16384 >= 2 * 2 * 4095
 NVFP4DG_HD long long partial_slot_floats(const Plan& p) {
   return 128ll * 2 * p.bn;
 }
@@ -131,7 +131,13 @@ NVFP4DG_HD long long workspace_partials_offset(const Plan&) {
 }
 NVFP4DG_HD long long workspace_bytes(const Plan& p) {
   if (p.sk_iters == 0) return 0;
-  return kCounterBytes + 2ll * p.grid * partial_slot_floats(p) * 4;
+  return kCounterBytes +
+         2ll * p.grid * p.ctas * partial_slot_floats(p) * 4;
+}
+// Partial slot of CTA `rank` of the unit whose unit-level slot is `unit_slot`
+// (2 * unit + which).
+NVFP4DG_HD long long cta_slot(const Plan& p, int unit_slot, int rank) {
+  return 2ll * ((unit_slot >> 1) * p.ctas + rank) + (unit_slot & 1);
 }
 
 }  // namespace nvfp4dg

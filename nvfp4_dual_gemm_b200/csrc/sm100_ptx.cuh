@@ -304,6 +304,142 @@ __device__ __forceinline__ void tc_wait_ld() {
 }
 
 // ---------------------------------------------------------------------------
+// Thread-block clusters and the 2-SM (cta_group::2) forms
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+               : "=r"(r)
+               : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Cluster-wide execution barrier (every thread of every CTA of the cluster).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+// Arrive on an mbarrier of any CTA of the cluster (cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile(
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+          cluster_addr)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar,
+                                                      uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait with cluster-scope acquire, for phases completed by arrivals
+// or transactions that come from the peer CTA.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar,
+                                                  uint32_t parity,
+                                                  unsigned* err, unsigned code,
+                                                  bool bail_on_err = true) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  long long t0 = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 1023u) == 0u) {
+      const long long now = clock_cycles();
+      if (t0 == 0) {
+        t0 = now;
+        continue;
+      }
+      if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u)
+        return false;
+      if (now - t0 > kWaitLimitCycles) {
+        atomicOr(err, code);
+        return false;
+      }
+    }
+  }
+}
+
+// 2-D tiled TMA load into this CTA's shared memory whose completion bytes
+// are counted on an mbarrier of either CTA of the pair (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m,
+                                                 uint32_t bar_cluster, int c0,
+                                                 int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::"
+      "complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(bar_cluster),
+      "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem,
+                                                uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_u32(dst_smem)),
+      "r"(ncols)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr,
+                                                  uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(
+                   taddr),
+               "r"(ncols)
+               : "memory");
+}
+
+// 2-SM block-scaled MMA, issued by the even CTA of the pair: each CTA holds
+// M/2 rows of A and N/2 rows of B at the same shared-memory offsets, its own
+// scale factors in TMEM, and receives its M/2 rows of D.
+__device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem,
+                                                 uint64_t a_desc,
+                                                 uint64_t b_desc,
+                                                 uint32_t idesc,
+                                                 uint32_t sfa_tmem,
+                                                 uint32_t sfb_tmem,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.scale_vec::4X "
+      "[%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem),
+      "r"(sfb_tmem)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at `bar_cluster` (either CTA of the pair) when
+// this thread's previously issued 2-SM tcgen05 operations have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(bar_cluster)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Descriptors
 // ---------------------------------------------------------------------------
 // Shared-memory matrix descriptor (tcgen05 format): start address, leading-

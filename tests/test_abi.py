@@ -81,7 +81,7 @@ SHAPES = [
 def cover(m, n, k, flags=0, sms=148):
     pl = dg.plan(m, n, k, flags, sms)
     bn = pl["bn"]
-    m_tiles = (m + 127) // 128
+    m_tiles = (m + 128 * pl["ctas"] - 1) // (128 * pl["ctas"])
     tiles = m_tiles * (n // bn)
     kb = k // 256
     seen = defaultdict(list)
@@ -113,19 +113,40 @@ def test_schedule_covers_every_block_once(m, n, k):
     cover(m, n, k)
 
 
-@pytest.mark.parametrize("grid", [1, 2, 3, 5, 7, 13, 148])
+@pytest.mark.parametrize("grid", [1, 2, 3, 5, 6, 7, 10, 13, 14, 148])
 @pytest.mark.parametrize("force", [0, dg.FLAG_FORCE_STREAMK])
-def test_forced_grid_stream_k(grid, force):
-    pl, seen = cover(256, 512, 2048, flags=grid | force)
-    assert pl["grid"] <= grid
-    if force and grid in (3, 5, 7):  # tile counts 8 / 16 do not divide
+@pytest.mark.parametrize("pair", [dg.FLAG_PAIR, dg.FLAG_NO_PAIR])
+def test_forced_grid_stream_k(grid, force, pair):
+    pl, seen = cover(256, 512, 2048, flags=grid | force | pair)
+    assert pl["grid"] * pl["ctas"] <= max(grid, 2)
+    # 256 x 512 has 8 or 16 single-CTA tiles and 4 or 8 pair tiles, so these
+    # grids (in CTAs) cannot cover them in whole tiles
+    splits = (3, 5, 7) if pair == dg.FLAG_NO_PAIR else (6, 10, 14)
+    if force and grid in splits:
         assert pl["sk_tiles"] > 0
         assert any(len(s) > 1 for s in seen.values())
 
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
-def test_schedule_forced_stream_k_covers_every_block_once(m, n, k):
-    cover(m, n, k, flags=dg.FLAG_FORCE_STREAMK)
+@pytest.mark.parametrize("pair", [dg.FLAG_PAIR, dg.FLAG_NO_PAIR])
+def test_schedule_forced_stream_k_covers_every_block_once(m, n, k, pair):
+    pl, _ = cover(m, n, k, flags=dg.FLAG_FORCE_STREAMK | pair)
+    assert pl["ctas"] == (2 if pair == dg.FLAG_PAIR else 1)
+
+
+@pytest.mark.parametrize("m,n,k", SHAPES)
+@pytest.mark.parametrize("pair", [dg.FLAG_PAIR, dg.FLAG_NO_PAIR])
+def test_schedule_pair_modes_cover_every_block_once(m, n, k, pair):
+    cover(m, n, k, flags=pair)
+
+
+def test_workspace_counters_fit_for_every_plan():
+    # counters live in a fixed 64 KiB region: (tiles split along K) x (CTAs
+    # per unit) must stay below 16384 for every grid the flags allow
+    for grid in (1, 7, 148, 4095):
+        for pair in (dg.FLAG_PAIR, dg.FLAG_NO_PAIR):
+            pl = dg.plan(8192, 28672, 8192, grid | pair | dg.FLAG_FORCE_STREAMK)
+            assert pl["sk_tiles"] * pl["ctas"] <= 16384
 
 
 def test_no_streamk_flag_gives_whole_tiles():
@@ -142,4 +163,4 @@ def test_bn_flags():
 
 def test_decode_shape_uses_every_sm_or_whole_tiles():
     pl = dg.plan(256, 4096, 7168)
-    assert pl["grid"] <= 148
+    assert pl["grid"] * pl["ctas"] <= 148

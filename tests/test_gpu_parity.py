@@ -32,8 +32,10 @@ def run(p, flags=0, use_custom_kernel=False):
 
 VARIANTS = {
     "auto": 0,
-    "bn64": _lib.FLAG_BN64,
-    "bn128_fused": _lib.FLAG_BN128,
+    "bn64": _lib.FLAG_BN64 | _lib.FLAG_NO_PAIR,
+    "bn128": _lib.FLAG_BN128 | _lib.FLAG_NO_PAIR,
+    "pair_bn64": _lib.FLAG_BN64 | _lib.FLAG_PAIR,
+    "pair_bn128": _lib.FLAG_BN128 | _lib.FLAG_PAIR,
     "whole_tiles": _lib.FLAG_NO_STREAMK,
 }
 
@@ -67,10 +69,23 @@ def streamk_problem():
 def test_stream_k_forced_grid(streamk_problem, grid, bn):
     p, ref = streamk_problem
     flag = (_lib.FLAG_BN64 if bn == 64 else _lib.FLAG_BN128) | \
-        _lib.FLAG_FORCE_STREAMK
+        _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR
     if grid in (3, 5, 7):
         assert dg.plan(256, 512, 2048, grid | flag)["sk_tiles"] > 0
     assert_close(run(p, grid | flag), ref, f"grid={grid} bn={bn}")
+
+
+@pytest.mark.parametrize("grid", [2, 4, 6, 10, 14])
+@pytest.mark.parametrize("bn", [64, 128])
+def test_pair_stream_k_forced_grid(streamk_problem, grid, bn):
+    p, ref = streamk_problem
+    flag = (_lib.FLAG_BN64 if bn == 64 else _lib.FLAG_BN128) | \
+        _lib.FLAG_FORCE_STREAMK | _lib.FLAG_PAIR
+    pl = dg.plan(256, 512, 2048, grid | flag)
+    assert pl["ctas"] == 2
+    if grid in (6, 10, 14):
+        assert pl["sk_tiles"] > 0
+    assert_close(run(p, grid | flag), ref, f"pair grid={grid} bn={bn}")
 
 
 def test_stream_k_repeated_calls_reuse_counters(streamk_problem):
@@ -90,9 +105,10 @@ def test_stream_k_repeated_calls_reuse_counters(streamk_problem):
 @pytest.mark.parametrize("m,n,k", [(1, 128, 256), (64, 64, 256),
                                    (200, 256, 512), (130, 384, 768),
                                    (333, 192, 1024)])
-def test_ragged_m_and_small_shapes(m, n, k):
+@pytest.mark.parametrize("pair", [_lib.FLAG_PAIR, _lib.FLAG_NO_PAIR])
+def test_ragged_m_and_small_shapes(m, n, k, pair):
     p = O.make_problem(m, n, k, seed=m + n + k)
-    assert_close(run(p), O.reference_output(p), f"{m}x{n}x{k}")
+    assert_close(run(p, pair), O.reference_output(p), f"{m}x{n}x{k}")
 
 
 # The 13 shapes of the reference's dispatch table (nvfp4_dual_gemm.cu:403-442)
@@ -223,7 +239,9 @@ def test_workspace_shared_across_plans(streamk_problem):
     # width and grid; the counters must never alias earlier partials.
     p, ref = streamk_problem
     for flags in (_lib.FLAG_BN64 | 13, _lib.FLAG_BN128 | 3, _lib.FLAG_BN64 | 7,
-                  _lib.FLAG_BN128 | 5, _lib.FLAG_BN128 | 3):
+                  _lib.FLAG_BN128 | 5 | _lib.FLAG_PAIR,
+                  _lib.FLAG_BN128 | 3 | _lib.FLAG_NO_PAIR,
+                  _lib.FLAG_BN64 | 10 | _lib.FLAG_PAIR):
         got = run(p, flags | _lib.FLAG_FORCE_STREAMK)
         assert_close(got, ref, f"flags={flags:#x}")
 
