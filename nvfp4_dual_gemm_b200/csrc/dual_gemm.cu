@@ -78,11 +78,12 @@ __device__ unsigned g_err_word;
 // Optional pipeline trace (compile with -DNVFP4DG_TRACE): per CTA, the SM
 // clock at each hand-off of the first kTraceSlots main-loop iterations —
 // producer after its empty-slot wait (0) and after issuing the copies (1),
-// MMA issuer after its full-slot wait (2) and after its commit (3) — and per
-// work unit the epilogue's accumulator-ready (4) and done (5) times.
+// MMA issuer after its full-slot wait (2) and after its commit (3), scale
+// warp after its data wait (6) and after its arrival (7) — and per work
+// unit the epilogue's accumulator-ready (4) and done (5) times.
 #ifdef NVFP4DG_TRACE
 constexpr int kTraceSlots = 64;
-constexpr int kTraceRoles = 6;
+constexpr int kTraceRoles = 8;
 constexpr int kTraceCtas = 160;
 __device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
 #define NVFP4DG_STAMP(role, idx)                                   \
@@ -644,6 +645,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           uint8_t* st = smem + stage * Cf::kStageBytes;
           const uint32_t full_c = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (is_a) NVFP4DG_STAMP(0, issued);
           if (is_a) {
             if (leader)
               mbar_arrive_expect_tx(&full_bar[stage],
@@ -657,6 +659,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                       kSfRunBytes, &sfdata_bar[stage], pol_b);
             bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
                       kSfRunBytes, &sfdata_bar[stage], pol_b);
+            NVFP4DG_STAMP(1, issued);
           } else {
             tma_load_2d_pair(st + Cf::kABytes, tmB, full_c, kb * kRowBytes,
                              row_b, pol_b);
@@ -689,6 +692,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t t_lane = tmem + ((32u * q) << 16);
     int stage = 0;
     uint32_t phase = 0;
+    int done = 0;
     bool ok = true;
     WorkIter it;
     work_begin(plan, unit, it);
@@ -702,6 +706,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(6, done);
         const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
                                        Cf::kABytes + Cf::kBBytes) +
                               16u * lane;
@@ -751,6 +756,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0)
           mbar_arrive_cluster(mapa_shared(smem_u32(&sf_bar[stage]), 0));
+        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
+        ++done;
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
@@ -766,6 +773,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
+      int consumed = 0;
       bool ok = true;
       WorkIter it;
       work_begin(plan, unit, it);
@@ -783,6 +791,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          NVFP4DG_STAMP(2, consumed);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
           const uint32_t b_addr = a_addr + Cf::kABytes;
@@ -800,6 +809,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t eb = smem_u32(&empty_bar[stage]);
           tc_commit_pair(mapa_shared(eb, 0));
           tc_commit_pair(mapa_shared(eb, peer));
+          NVFP4DG_STAMP(3, consumed);
+          ++consumed;
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -821,6 +832,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), 0);
     uint32_t acc_phase = 0;
+    int unit_i = 0;
     WorkIter it;
     work_begin(plan, unit, it);
     Work w;
@@ -828,6 +840,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool got =
           mbar_wait_cluster(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
       if (!__all_sync(0xffffffffu, got)) break;
+      if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit_i);
       tc_fence_after();
       const int m_tile = w.tile % plan.m_tiles;
       const int n_tile = w.tile / plan.m_tiles;
@@ -905,6 +918,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit_i);
+      ++unit_i;
       acc_phase ^= 1u;
     }
   }
@@ -1510,7 +1525,7 @@ int nvfp4_dual_gemm_device_status(int device, unsigned* word_out) {
 const char* nvfp4_dual_gemm_last_error(void) { return g_last_error.c_str(); }
 
 #ifdef NVFP4DG_TRACE
-// Trace builds only: copy the stamp buffer ([160][6][64] int64) to the host.
+// Trace builds only: copy the stamp buffer ([160][8][64] int64) to the host.
 NVFP4DG_API int nvfp4_dual_gemm_trace_read(void* host, size_t bytes) {
   if (bytes < sizeof(g_trace)) return NVFP4DG_ERR_INVALID;
   cudaError_t e = cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace));

@@ -329,51 +329,25 @@ __device__ __forceinline__ void cluster_sync() {
           : "memory");
 }
 
-// Arrive on an mbarrier of any CTA of the cluster (cluster address).
+// Arrive on an mbarrier of any CTA of the cluster (cluster address), with
+// the default semantics of mbarrier.arrive.  A cluster-scope release here
+// cost 1000-2000 cycles per arrival on B200 (it waits out the SM's memory
+// traffic); the producers of the data these arrivals publish (TMEM scale
+// stores, TMEM accumulator reads) complete before the arrival
+// (tcgen05.wait::st / ::ld) and are ordered for the MMA by the tcgen05
+// fences around the barrier, the pattern CUTLASS's 2-SM pipelines use.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile(
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
-          cluster_addr)
-      : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(
+                   cluster_addr)
+               : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar,
-                                                      uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait with cluster-scope acquire, for phases completed by arrivals
-// or transactions that come from the peer CTA.
+// Waits on barriers that the peer CTA signals use the ordinary bounded wait.
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar,
                                                   uint32_t parity,
                                                   unsigned* err, unsigned code,
                                                   bool bail_on_err = true) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  long long t0 = 0;
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((i & 1023u) == 0u) {
-      const long long now = clock_cycles();
-      if (t0 == 0) {
-        t0 = now;
-        continue;
-      }
-      if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u)
-        return false;
-      if (now - t0 > kWaitLimitCycles) {
-        atomicOr(err, code);
-        return false;
-      }
-    }
-  }
+  return mbar_wait(bar, parity, err, code, bail_on_err);
 }
 
 // 2-D tiled TMA load into this CTA's shared memory whose completion bytes
