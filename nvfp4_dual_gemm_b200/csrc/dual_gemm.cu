@@ -252,8 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
         const uint8_t* sfb1 = p.sfb1 + sfb_off;
         const uint8_t* sfb2 = p.sfb2 + sfb_off;
-        for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
             ok = false;
             break;
@@ -312,8 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
       const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
-      for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got = mbar_wait(&full_bar[stage], phase, p.err, kErrMma);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
@@ -394,8 +392,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma) ||
               !mbar_wait(&sf_bar[stage], phase, p.err, kErrMma)) {
             ok = false;
@@ -414,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                               SmemLayout::kSwizzle128B);
             tc_mma_nvf4(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
                         sf_t + 16 + kSfbStep * j,
-                        (j_ > 0 || j > 0) ? 1u : 0u);
+                        (kb > w.kb0 || j > 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[stage]);
           NVFP4DG_STAMP(3, consumed);
@@ -640,8 +637,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
         const uint8_t* sfb1 = p.sfb1 + sfb_off;
         const uint8_t* sfb2 = p.sfb2 + sfb_off;
-        for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
                                  kErrProducer)) {
             ok = false;
@@ -703,8 +699,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     Work w;
     while (ok && work_next(plan, it, w)) {
       const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
-      for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got =
             mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
         if (!__all_sync(0xffffffffu, got)) {
@@ -790,8 +785,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        for (int j_ = 0; j_ < w.kb1 - w.kb0; ++j_) {
-          const int kb = work_kb(w, j_);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&full_bar[stage], phase, p.err, kErrMma) ||
               !mbar_wait_cluster(&sf_bar[stage], phase, p.err, kErrMma)) {
             ok = false;
@@ -810,7 +804,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                               SmemLayout::kSwizzle128B);
             tc_mma_nvf4_pair(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
                              sf_t + 16 + kSfbStep * j,
-                             (j_ > 0 || j > 0) ? 1u : 0u);
+                             (kb > w.kb0 || j > 0) ? 1u : 0u);
           }
           const uint32_t eb = smem_u32(&empty_bar[stage]);
           tc_commit_pair(mapa_shared(eb, 0));

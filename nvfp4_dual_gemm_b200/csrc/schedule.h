@@ -44,19 +44,7 @@ struct Work {
   int kb0;   // first 256-wide K block
   int kb1;   // one past the last K block
   int slot;  // workspace slot of the partial, -1 for a whole tile
-  int rot;   // K blocks are visited from kb0 + rot, wrapping (whole tiles)
 };
-
-// K block visited at step j of work unit w.  Whole tiles start their K loop
-// at an offset that depends on the tile's N index, so that the CTAs sharing
-// one A tile (same m, different n) do not all request the same A block from
-// the same L2 slices at the same moment; split tiles keep their order.
-NVFP4DG_HD int work_kb(const Work& w, int j) {
-  const int n = w.kb1 - w.kb0;
-  int k = j + w.rot;
-  if (k >= n) k -= n;
-  return w.kb0 + k;
-}
 
 NVFP4DG_HD long long sk_lo(const Plan& p, int b) {
   return static_cast<long long>(b) * p.sk_iters / p.grid;
@@ -104,7 +92,6 @@ NVFP4DG_HD bool work_next(const Plan& p, WorkIter& s, Work& w) {
     w.kb0 = 0;
     w.kb1 = p.kblocks;
     w.slot = -1;
-    w.rot = (s.dp_next / p.m_tiles) % p.kblocks;
     s.dp_next += p.grid;
     return true;
   }
@@ -119,7 +106,6 @@ NVFP4DG_HD bool work_next(const Plan& p, WorkIter& s, Work& w) {
   w.kb1 = kb1;
   const bool whole = (kb0 == 0 && kb1 == p.kblocks);
   w.slot = whole ? -1 : 2 * s.b + (s.first_sk ? 0 : 1);
-  w.rot = whole ? (w.tile / p.m_tiles) % p.kblocks : 0;
   s.first_sk = 0;
   s.it += kb1 - kb0;
   return true;
