@@ -147,6 +147,41 @@ NVFP4DG_API int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int nu
 NVFP4DG_API int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, int num_sms,
                               int cta, int* records, int cap);
 
+/*
+ * Upper limit, in bytes, of the scratch buffer nvfp4_dual_gemm_run_noalloc
+ * keeps in device memory.
+ */
+#define NVFP4DG_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * Same computation as nvfp4_dual_gemm_run, for callers that cannot allocate
+ * device memory at the time they call: code running where cudaMalloc is not
+ * allowed or not wanted (inside a custom memory arena or pool that owns all
+ * device memory, a framework whose allocator must not be re-entered, a
+ * real-time path that must not block on the allocator).  No counterpart in
+ * the reference: its kernel never needs scratch memory.
+ *
+ * Tiles split along K need fp32 scratch; this entry point takes it from a
+ * static array of NVFP4DG_NOALLOC_SCRATCH_BYTES that every GPU which loads
+ * the library holds until the process exits, and it calls no cudaMalloc,
+ * cudaFree or other allocating routine.  The caller passes inputs and
+ * outputs as for nvfp4_dual_gemm_run.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  A problem whose
+ * schedule needs more scratch than the array holds is rejected with
+ * NVFP4DG_ERR_WORKSPACE (see the message; nvfp4_dual_gemm_run_ws takes a
+ * larger caller-owned buffer, and NVFP4DG_FLAG_NO_STREAMK needs none).
+ * Every call shares the one array, which keeps the last call's contents:
+ * each call clears the tile counters it needs before launching.  Each
+ * device has its own copy of the array, but calls that overlap on the GPU of
+ * one device (for example on two streams) race on it and must be serialised
+ * by the caller.
+ */
+NVFP4DG_API int nvfp4_dual_gemm_run_noalloc(
+    const void* A, const void* B1, const void* B2, const void* SFA,
+    const void* SFB1, const void* SFB2, void* C, int M, int N, int K, int L,
+    unsigned flags, void* stream);
+
 /* Thread-local message describing the last failure ("" if none). */
 NVFP4DG_API const char* nvfp4_dual_gemm_last_error(void);
 

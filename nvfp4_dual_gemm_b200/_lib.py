@@ -32,6 +32,9 @@ FLAG_FORCE_STREAMK = 1 << 17
 FLAG_PAIR = 1 << 18
 FLAG_NO_PAIR = 1 << 19
 
+# Size of the static scratch behind nvfp4_dual_gemm_run_noalloc.
+NOALLOC_SCRATCH_BYTES = 4 << 20
+
 # Every symbol the header declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -43,6 +46,8 @@ SIGNATURES = {
     "nvfp4_dual_gemm_workspace_size": (_sz, [_i, _i, _i, _i, _u]),
     "nvfp4_dual_gemm_run_ws": (_i, [_vp] * 7 + [_i, _i, _i, _i, _u, _vp, _sz,
                                                 _vp]),
+    "nvfp4_dual_gemm_run_noalloc": (_i, [_vp] * 7 + [_i, _i, _i, _i, _u,
+                                                     _vp]),
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "nvfp4_dual_gemm_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip,

@@ -75,6 +75,13 @@ struct KParams {
 
 __device__ unsigned g_err_word;
 
+// Scratch of nvfp4_dual_gemm_run_noalloc: the stream-K counters and fp32
+// partials of one call, for callers that cannot allocate device memory.  In
+// host code this name is only a stand-in for the symbol; the device address
+// comes from cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char
+    g_noalloc_scratch[NVFP4DG_NOALLOC_SCRATCH_BYTES];
+
 // Optional pipeline trace (compile with -DNVFP4DG_TRACE): per CTA, the SM
 // clock at each hand-off of the first kTraceSlots main-loop iterations —
 // producer after its empty-slot wait (0) and after issuing the copies (1),
@@ -1409,6 +1416,26 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   return NVFP4DG_OK;
 }
 
+// Device address of g_noalloc_scratch, looked up once per device with that
+// device current (the symbol name itself is not a device address on the
+// host).
+std::map<int, void*> g_noalloc_ptr;
+
+int noalloc_scratch(int devid, void** out) {
+  auto it = g_noalloc_ptr.find(devid);
+  if (it != g_noalloc_ptr.end()) {
+    *out = it->second;
+    return NVFP4DG_OK;
+  }
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (e != cudaSuccess || ptr == nullptr)
+    return cuda_fail(e, "cudaGetSymbolAddress(no-allocation scratch)");
+  g_noalloc_ptr[devid] = ptr;
+  *out = ptr;
+  return NVFP4DG_OK;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1431,6 +1458,77 @@ int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void* B2,
                            void* stream) {
   return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, workspace,
                   workspace_bytes, false, stream);
+}
+
+int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
+                                const void* SFA, const void* SFB1,
+                                const void* SFB2, void* C, int M, int N, int K,
+                                int L, unsigned flags, void* stream_ptr) {
+  g_last_error.clear();
+  int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return NVFP4DG_OK;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  if (K == 0) {  // empty sums: silu(0) * 0 = 0
+    cudaError_t e =
+        cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
+    return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "cudaMemsetAsync");
+  }
+  std::lock_guard<std::mutex> lock(g_mu);
+  int devid = 0;
+  cudaError_t e = cudaGetDevice(&devid);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  DevInfo* dev = nullptr;
+  if ((rc = device_info(devid, &dev))) return rc;
+  void* scratch = nullptr;
+  if ((rc = noalloc_scratch(devid, &scratch))) return rc;
+  const Plan plan = choose_plan(M, N, K, flags, dev->sms);
+  const size_t need = static_cast<size_t>(workspace_bytes(plan));
+  if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
+    return fail(NVFP4DG_ERR_WORKSPACE,
+                "this schedule needs " + std::to_string(need) +
+                    " bytes of scratch; nvfp4_dual_gemm_run_noalloc holds "
+                    "at most " +
+                    std::to_string(NVFP4DG_NOALLOC_SCRATCH_BYTES) +
+                    " (use nvfp4_dual_gemm_run_ws, a smaller grid, or "
+                    "NVFP4DG_FLAG_NO_STREAMK)");
+  void* ws = nullptr;
+  if (need > 0) {
+    // The array keeps the previous call's contents: zero the tile counters.
+    e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(kCounterBytes),
+                        stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch)");
+    ws = scratch;
+  }
+  if (plan.ctas == 2 && plan.bn == 128)
+    rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                           N, K, ws, stream);
+  else if (plan.ctas == 2)
+    rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
+                          N, K, ws, stream);
+  else if (plan.bn == 128)
+    rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
+                            M, N, K, ws, stream);
+  else
+    rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
+                           M, N, K, ws, stream);
+  if (rc) return rc;
+  if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
+    unsigned word = 0;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess)
+      return cuda_fail(e, "cudaStreamSynchronize");
+    if ((e = cudaMemcpyFromSymbol(&word, g_err_word, sizeof(word))) !=
+        cudaSuccess)
+      return cuda_fail(e, "cudaMemcpyFromSymbol");
+    if (word != 0) {
+      const unsigned zero = 0;
+      cudaMemcpyToSymbol(g_err_word, &zero, sizeof(zero));
+      return fail(NVFP4DG_ERR_DEVICE,
+                  "kernel wait timed out (device error word " +
+                      std::to_string(word) + ")");
+    }
+  }
+  return NVFP4DG_OK;
 }
 
 size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
