@@ -178,10 +178,8 @@ def barrier(world):
 def max_over_ranks(x, world):
     if world == 1:
         return x
-    import torch.distributed as dist
-    t = torch.tensor([x], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    from nvfp4_dual_gemm_b200.shard import max_over_ranks as _max
+    return _max(x, device="cuda")
 
 
 # --------------------------------------------------------------------------

@@ -14,6 +14,13 @@ from .api import (  # noqa: F401
     quantize_nvfp4,
     workspace_size,
 )
+from .shard import (  # noqa: F401
+    ShardSpec,
+    gather_columns,
+    shard_spec,
+    shard_weights,
+    sharded_dual_gemm,
+)
 from ._lib import (  # noqa: F401
     FLAG_BN64,
     FLAG_BN128,

@@ -639,8 +639,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int n_tile = w.tile / plan.m_tiles;
         const int row_a = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
         const int row_b = n_tile * BN;
-        const uint8_t* sfa =
-            p.sfa + (size_t)(m_tile * 2 + rank) * kblk64 * kSfAtomBytes;
+        // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
+        // lie wholly past M (M in (256t, 256t + 128] for the last pair
+        // tile) it copies the last block instead: its A rows are zero-filled
+        // by the tensor map and its accumulator rows are never stored.
+        const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
+                              (p.M + kBM - 1) / kBM - 1);
+        const uint8_t* sfa = p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
         const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
         const uint8_t* sfb1 = p.sfb1 + sfb_off;
         const uint8_t* sfb2 = p.sfb2 + sfb_off;

@@ -104,7 +104,7 @@ def test_stream_k_repeated_calls_reuse_counters(streamk_problem):
 
 @pytest.mark.parametrize("m,n,k", [(1, 128, 256), (64, 64, 256),
                                    (200, 256, 512), (130, 384, 768),
-                                   (333, 192, 1024)])
+                                   (333, 192, 1024), (384, 256, 512)])
 @pytest.mark.parametrize("pair", [_lib.FLAG_PAIR, _lib.FLAG_NO_PAIR])
 def test_ragged_m_and_small_shapes(m, n, k, pair):
     p = O.make_problem(m, n, k, seed=m + n + k)
