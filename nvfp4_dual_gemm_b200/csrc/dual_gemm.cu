@@ -108,6 +108,23 @@ __device__ __forceinline__ void epi_bar() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// Barrier `ID` over 128 threads (four warps) that also ANDs a predicate:
+// every thread gets the same answer, so a group that must later meet at the
+// same named barrier either continues together or leaves together.
+template <int ID>
+__device__ __forceinline__ bool group_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, 128, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred)), "n"(ID)
+      : "memory");
+  return out != 0;
+}
+
 __device__ __forceinline__ float silu_mul(float x, float y) {
   return __fdividef(x, 1.0f + __expf(-x)) * y;
 }
@@ -311,6 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
+    int done = 0;  // K blocks handed over (trace index)
     WorkIter it;
     work_begin(plan, blockIdx.x, it);
     Work w;
@@ -324,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(6, done);
         const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
                                        Cf::kABytes + 2 * Cf::kBBytes) +
                               16u * lane;
@@ -374,6 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sf_bar[stage]);
+        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
+        ++done;
         if (++stage == S) {
           stage = 0;
           phase ^= 1u;
@@ -448,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     Work w;
     while (work_next(plan, it, w)) {
       const bool got = mbar_wait(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
-      if (!__all_sync(0xffffffffu, got)) break;
+      if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
       tc_fence_after();
       const int m_tile = w.tile % plan.m_tiles;
@@ -851,7 +872,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     while (work_next(plan, it, w)) {
       const bool got =
           mbar_wait_cluster(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
-      if (!__all_sync(0xffffffffu, got)) break;
+      if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit_i);
       tc_fence_after();
       const int m_tile = w.tile % plan.m_tiles;

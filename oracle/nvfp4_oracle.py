@@ -102,14 +102,24 @@ def e4m3_encode(x: np.ndarray) -> np.ndarray:
 # --------------------------------------------------------------------------
 # e2m1
 # --------------------------------------------------------------------------
+_E2M1_CUTS = np.array(
+    [0.25, np.nextafter(np.float32(0.75), np.float32(0)), 1.25,
+     np.nextafter(np.float32(1.75), np.float32(0)), 2.5,
+     np.nextafter(np.float32(3.5), np.float32(0)), 5.0], dtype=np.float32)
+
+
 def e2m1_encode(q: np.ndarray) -> np.ndarray:
     """float32 -> e2m1 codes (uint8 in [0, 16)), round to nearest even on the
     grid {0, .5, 1, 1.5, 2, 3, 4, 6}, saturating at 6.  The sign bit is kept
     for negative inputs, including those that round to zero."""
     q = np.asarray(q, dtype=np.float32)
     a = np.abs(q)
-    mag = ((a > 0.25).astype(np.uint8) + (a >= 0.75) + (a > 1.25) +
-           (a >= 1.75) + (a > 2.5) + (a >= 3.5) + (a > 5.0)).astype(np.uint8)
+    # The magnitude code is the number of decision thresholds below |q|.
+    # Ties go to the even code: a tie at 0.25, 1.25, 2.5 or 5.0 rounds down
+    # (strict >), one at 0.75, 1.75 or 3.5 rounds up (>=, written as > the
+    # next float32 below the midpoint).
+    mag = np.searchsorted(_E2M1_CUTS, a, side="left").astype(np.uint8)
+    mag[np.isnan(a)] = 0
     sign = np.where(np.signbit(q), 8, 0).astype(np.uint8)
     return (mag | sign).astype(np.uint8)
 
