@@ -207,12 +207,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const KParams p) {
   using Cf = Cfg<BN>;
   constexpr int S = Cf::kStages;
-  constexpr uint32_t kBytesA = Cf::kABytes + 3 * kSfRunBytes;
+  constexpr uint32_t kBytesA = Cf::kABytes;
   constexpr uint32_t kBytesB = 2 * Cf::kBBytes;
+  constexpr uint32_t kBytesSf = 3 * kSfRunBytes;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[S];
-  __shared__ __align__(8) uint64_t sf_bar[S];
+  __shared__ __align__(8) uint64_t full_bar[S];    // operands + scales ready
+  __shared__ __align__(8) uint64_t sfdata_bar[S];  // scale runs landed
   __shared__ __align__(8) uint64_t empty_bar[S];
   __shared__ __align__(8) uint64_t acc_full_bar;
   __shared__ __align__(8) uint64_t acc_empty_bar;
@@ -231,8 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 2);          // producers A and B
-      mbar_init(&sf_bar[s], kSfWarps);     // one arrival per scale warp
+      // producers A and B (with the tiles' bytes) and the scale warps
+      mbar_init(&full_bar[s], 2 + kSfWarps);
+      mbar_init(&sfdata_bar[s], 1);        // producer A
       mbar_init(&empty_bar[s], 1);         // tcgen05.commit of the MMAs
     }
     mbar_init(&acc_full_bar, 1);
@@ -284,16 +286,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* st = smem + stage * Cf::kStageBytes;
           if (is_a) {
             NVFP4DG_STAMP(0, issued);
+            // The scale runs first, on their own barrier: the scale warps
+            // move them into TMEM while the operand tiles are in flight.
             uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
+            mbar_arrive_expect_tx(&sfdata_bar[stage], kBytesSf);
+            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
+                      &sfdata_bar[stage], pol_a);
+            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &sfdata_bar[stage], pol_b);
+            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &sfdata_bar[stage], pol_b);
             mbar_arrive_expect_tx(&full_bar[stage], kBytesA);
             tma_load_2d(st, &tmA, &full_bar[stage], kb * kRowBytes, row_a,
                         pol_a);
-            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
-                      &full_bar[stage], pol_a);
-            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &full_bar[stage], pol_b);
-            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &full_bar[stage], pol_b);
             NVFP4DG_STAMP(1, issued);
           } else {
             mbar_arrive_expect_tx(&full_bar[stage], kBytesB);
@@ -314,6 +319,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < S; ++s) {
         if (issued > s) {
           const long long fill = (issued - 1 - s) / S;
+          if (is_a)
+            mbar_wait(&sfdata_bar[s], static_cast<uint32_t>(fill & 1), p.err,
+                      kErrDrain, /*bail_on_err=*/false);
           mbar_wait(&full_bar[s], static_cast<uint32_t>(fill & 1), p.err,
                     kErrDrain, /*bail_on_err=*/false);
         }
@@ -337,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
       const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        const bool got = mbar_wait(&full_bar[stage], phase, p.err, kErrMma);
+        const bool got = mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
           break;
@@ -392,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sf_bar[stage]);
+        if (lane == 0) mbar_arrive(&full_bar[stage]);
         if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
         ++done;
         if (++stage == S) {
@@ -406,6 +414,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdesc = idesc_nvf4(128, 2 * BN);
       constexpr uint32_t kSfbStep = (BN == 128) ? 8u : 4u;
+      const uint64_t a_desc0 = smem_desc(smem_u32(smem), 16, 1024,
+                                         SmemLayout::kSwizzle128B);
+      const uint64_t b_desc0 = smem_desc(smem_u32(smem) + Cf::kABytes, 16,
+                                         1024, SmemLayout::kSwizzle128B);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
@@ -421,25 +433,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma) ||
-              !mbar_wait(&sf_bar[stage], phase, p.err, kErrMma)) {
+          // One wait per K block: the barrier completes when the tiles
+          // have landed and all scale warps have written their scales.
+          if (!mbar_wait(&full_bar[stage], phase, p.err, kErrMma)) {
             ok = false;
             break;
           }
           NVFP4DG_STAMP(2, consumed);
           tc_fence_after();  // orders the scale warps' tcgen05.st before us
-          const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
-          const uint32_t b_addr = a_addr + Cf::kABytes;
+          // Descriptors of stage `stage`, K step 0; a K step of 64 fp4 is
+          // 32 bytes, i.e. +2 in the descriptors' address field (the field
+          // holds address >> 4 and shared addresses stay below 2^18).
+          const uint32_t soff = static_cast<uint32_t>(stage) *
+                                (Cf::kStageBytes >> 4);
+          const uint64_t a_desc = a_desc0 + soff;
+          const uint64_t b_desc = b_desc0 + soff;
           const uint32_t sf_t = tmem + kSfTmemBase + stage * kSfTmemPerStage;
+          const uint32_t acc0 = (kb > w.kb0) ? 1u : 0u;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint64_t a_desc = smem_desc(a_addr + 32 * j, 16, 1024,
-                                              SmemLayout::kSwizzle128B);
-            const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
-                                              SmemLayout::kSwizzle128B);
-            tc_mma_nvf4(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
-                        sf_t + 16 + kSfbStep * j,
-                        (kb > w.kb0 || j > 0) ? 1u : 0u);
+            tc_mma_nvf4(tmem, a_desc + 2u * j, b_desc + 2u * j, kIdesc,
+                        sf_t + 4 * j, sf_t + 16 + kSfbStep * j,
+                        j > 0 ? 1u : acc0);
           }
           tc_commit(&empty_bar[stage]);
           NVFP4DG_STAMP(3, consumed);
@@ -596,9 +611,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int S = Cf::kStages;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[S];    // even CTA: A/B of both
+  // even CTA: the A/B tiles of both CTAs landed and the scale warps of both
+  // CTAs have written their scales
+  __shared__ __align__(8) uint64_t full_bar[S];
   __shared__ __align__(8) uint64_t sfdata_bar[S];  // own scale runs landed
-  __shared__ __align__(8) uint64_t sf_bar[S];      // even CTA: scales in TMEM
   __shared__ __align__(8) uint64_t empty_bar[S];
   __shared__ __align__(8) uint64_t acc_full_bar;
   __shared__ __align__(8) uint64_t acc_empty_bar;  // even CTA: both drained
@@ -618,10 +634,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);           // even CTA's producer A
+      // even CTA's producer A (with both CTAs' tile bytes) + the scale
+      // warps of both CTAs
+      mbar_init(&full_bar[s], 1 + 2 * kSfWarps);
       mbar_init(&sfdata_bar[s], 1);         // own producer A
-      mbar_init(&sf_bar[s], 2 * kSfWarps);  // scale warps of both CTAs
-      mbar_init(&empty_bar[s], 1);          // MMA commit
+      // even CTA: the MMA commit; odd CTA: the even producer A's forward
+      mbar_init(&empty_bar[s], 1);
     }
     mbar_init(&acc_full_bar, 1);
     mbar_init(&acc_empty_bar, 2 * kEpiWarps);
@@ -676,6 +694,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          // Even CTA: the MMAs that read this stage in both CTAs are done;
+          // pass that on to the odd CTA (from the second fill on).
+          if (leader && is_a && issued >= S)
+            mbar_arrive_cluster(mapa_shared(smem_u32(&empty_bar[stage]), 1u));
           uint8_t* st = smem + stage * Cf::kStageBytes;
           const uint32_t full_c = mapa_shared(smem_u32(&full_bar[stage]), 0);
           if (is_a) NVFP4DG_STAMP(0, issued);
@@ -788,7 +810,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0)
-          mbar_arrive_cluster(mapa_shared(smem_u32(&sf_bar[stage]), 0));
+          mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), 0));
         if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
         ++done;
         if (++stage == S) {
@@ -803,6 +825,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       constexpr uint32_t kIdesc = idesc_nvf4(256, 2 * BN);
       constexpr uint32_t kSfbStep = (BN == 128) ? 8u : 4u;
       const uint32_t peer = 1u;
+      const uint64_t a_desc0 = smem_desc(smem_u32(smem), 16, 1024,
+                                         SmemLayout::kSwizzle128B);
+      const uint64_t b_desc0 = smem_desc(smem_u32(smem) + Cf::kABytes, 16,
+                                         1024, SmemLayout::kSwizzle128B);
       int stage = 0;
       uint32_t phase = 0;
       uint32_t acc_phase = 0;
@@ -819,29 +845,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait_cluster(&full_bar[stage], phase, p.err, kErrMma) ||
-              !mbar_wait_cluster(&sf_bar[stage], phase, p.err, kErrMma)) {
+          // One wait per K block (tiles of both CTAs + all scales).
+          if (!mbar_wait_cluster(&full_bar[stage], phase, p.err, kErrMma)) {
             ok = false;
             break;
           }
           NVFP4DG_STAMP(2, consumed);
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + stage * Cf::kStageBytes);
-          const uint32_t b_addr = a_addr + Cf::kABytes;
+          // Descriptors of stage `stage`, K step 0 (+2 per 32-byte K step).
+          const uint32_t soff = static_cast<uint32_t>(stage) *
+                                (Cf::kStageBytes >> 4);
+          const uint64_t a_desc = a_desc0 + soff;
+          const uint64_t b_desc = b_desc0 + soff;
           const uint32_t sf_t = tmem + Cf::kSfBase + stage * kSfTmemPerStage;
+          const uint32_t acc0 = (kb > w.kb0) ? 1u : 0u;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const uint64_t a_desc = smem_desc(a_addr + 32 * j, 16, 1024,
-                                              SmemLayout::kSwizzle128B);
-            const uint64_t b_desc = smem_desc(b_addr + 32 * j, 16, 1024,
-                                              SmemLayout::kSwizzle128B);
-            tc_mma_nvf4_pair(tmem, a_desc, b_desc, kIdesc, sf_t + 4 * j,
-                             sf_t + 16 + kSfbStep * j,
-                             (kb > w.kb0 || j > 0) ? 1u : 0u);
+            tc_mma_nvf4_pair(tmem, a_desc + 2u * j, b_desc + 2u * j, kIdesc,
+                             sf_t + 4 * j, sf_t + 16 + kSfbStep * j,
+                             j > 0 ? 1u : acc0);
           }
-          const uint32_t eb = smem_u32(&empty_bar[stage]);
-          tc_commit_pair(mapa_shared(eb, 0));
-          tc_commit_pair(mapa_shared(eb, peer));
+          // The stage is free in both CTAs once these MMAs complete; the
+          // odd CTA learns it from the even producer A (one commit here).
+          tc_commit_pair(mapa_shared(smem_u32(&empty_bar[stage]), 0));
           NVFP4DG_STAMP(3, consumed);
           ++consumed;
           if (++stage == S) {
