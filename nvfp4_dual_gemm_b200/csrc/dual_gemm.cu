@@ -232,9 +232,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      // producers A and B (with the tiles' bytes) and the scale warps
-      mbar_init(&full_bar[s], 2 + kSfWarps);
-      mbar_init(&sfdata_bar[s], 1);        // producer A
+      // the tile producer (with the tiles' bytes) and the scale warps
+      mbar_init(&full_bar[s], 1 + kSfWarps);
+      mbar_init(&sfdata_bar[s], 1);        // the scale-run producer
       mbar_init(&empty_bar[s], 1);         // tcgen05.commit of the MMAs
     }
     mbar_init(&acc_full_bar, 1);
@@ -258,10 +258,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
     // ------------------------------------------------------------ producers
-    if (lane == 0) {
-      const bool is_a = (warp == kProdAWarp);
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_normal();
+    // Warp 4 copies the operand tiles, warp 5 the scale runs.  In each, lanes
+    // 0-2 issue their three copies as one instruction (lane 0: A / SFA,
+    // lane 1: B1 / SFB1, lane 2: B2 / SFB2): an issuing thread's chain of
+    // dependent instructions per K block, not the bytes, bounds the copy
+    // rate of an SM.  The scale runs land on their own barrier so the scale
+    // warps can move them into TMEM while the tiles are in flight.
+    const bool tiles = (warp == kProdAWarp);
+    if (lane < 3) {
+      const uint64_t pol =
+          (lane == 0) ? policy_evict_last() : policy_evict_normal();
+      const CUtensorMap* map = (lane == 0) ? &tmA : (lane == 1 ? &tmB1 : &tmB2);
+      const uint8_t* sf_base =
+          (lane == 0) ? p.sfa : (lane == 1 ? p.sfb1 : p.sfb2);
+      uint64_t* bars = tiles ? full_bar : sfdata_bar;
+      const uint32_t tx = tiles ? kBytesA + kBytesB : kBytesSf;
+      const uint32_t dst_off =
+          tiles ? (lane == 0 ? 0u
+                             : static_cast<uint32_t>(Cf::kABytes +
+                                                     (lane - 1) * Cf::kBBytes))
+                : static_cast<uint32_t>(Cf::kABytes + 2 * Cf::kBBytes +
+                                        lane * kSfRunBytes);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -272,41 +289,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
-        const int row_a = m_tile * kBM;
-        const int row_b = n_tile * BN;
-        const uint8_t* sfa = p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
-        const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
-        const uint8_t* sfb1 = p.sfb1 + sfb_off;
-        const uint8_t* sfb2 = p.sfb2 + sfb_off;
+        const int row = (lane == 0) ? m_tile * kBM : n_tile * BN;
+        const int blk = (lane == 0) ? m_tile : (n_tile * BN) / 128;
+        const uint8_t* sf_src =
+            sf_base + (size_t)blk * kblk64 * kSfAtomBytes;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
             ok = false;
             break;
           }
           uint8_t* st = smem + stage * Cf::kStageBytes;
-          if (is_a) {
-            NVFP4DG_STAMP(0, issued);
-            // The scale runs first, on their own barrier: the scale warps
-            // move them into TMEM while the operand tiles are in flight.
-            uint8_t* sf = st + Cf::kABytes + 2 * Cf::kBBytes;
-            mbar_arrive_expect_tx(&sfdata_bar[stage], kBytesSf);
-            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
-                      &sfdata_bar[stage], pol_a);
-            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &sfdata_bar[stage], pol_b);
-            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &sfdata_bar[stage], pol_b);
-            mbar_arrive_expect_tx(&full_bar[stage], kBytesA);
-            tma_load_2d(st, &tmA, &full_bar[stage], kb * kRowBytes, row_a,
-                        pol_a);
-            NVFP4DG_STAMP(1, issued);
-          } else {
-            mbar_arrive_expect_tx(&full_bar[stage], kBytesB);
-            tma_load_2d(st + Cf::kABytes, &tmB1, &full_bar[stage],
-                        kb * kRowBytes, row_b, pol_b);
-            tma_load_2d(st + Cf::kABytes + Cf::kBBytes, &tmB2,
-                        &full_bar[stage], kb * kRowBytes, row_b, pol_b);
+          if (lane == 0) {
+            if (tiles) NVFP4DG_STAMP(0, issued);
+            mbar_arrive_expect_tx(&bars[stage], tx);
           }
+          __syncwarp(0x7u);
+          if (tiles)
+            tma_load_2d(st + dst_off, map, &bars[stage], kb * kRowBytes, row,
+                        pol);
+          else
+            bulk_load(st + dst_off, sf_src + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &bars[stage], pol);
+          if (tiles && lane == 0) NVFP4DG_STAMP(1, issued);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -315,14 +319,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Never leave with copies in flight: wait (bounded) until every stage
-      // has completed the fill that holds this thread's last copies.
+      // has completed the fill that holds this warp's last copies.
       for (int s = 0; s < S; ++s) {
         if (issued > s) {
           const long long fill = (issued - 1 - s) / S;
-          if (is_a)
-            mbar_wait(&sfdata_bar[s], static_cast<uint32_t>(fill & 1), p.err,
-                      kErrDrain, /*bail_on_err=*/false);
-          mbar_wait(&full_bar[s], static_cast<uint32_t>(fill & 1), p.err,
+          mbar_wait(&bars[s], static_cast<uint32_t>(fill & 1), p.err,
                     kErrDrain, /*bail_on_err=*/false);
         }
       }
@@ -661,11 +662,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
     // ------------------------------------------------------------ producers
-    if (lane == 0) {
-      const bool is_a = (warp == kProdAWarp);
-      const uint64_t pol_a = policy_evict_last();
-      const uint64_t pol_b = policy_evict_normal();
-      const CUtensorMap* tmB = (rank == 0) ? &tmB1 : &tmB2;
+    // Warp 4 copies the operand tiles (lane 0: this CTA's A rows, lane 1:
+    // its B half, as one instruction) with their bytes counted on the even
+    // CTA's `full` barrier; warp 5 copies this CTA's three scale runs
+    // (lanes 0-2, one instruction) onto its own `sfdata` barrier.
+    const bool tiles = (warp == kProdAWarp);
+    const int nl = tiles ? 2 : 3;
+    if (lane < nl) {
+      const uint64_t pol =
+          (lane == 0) ? policy_evict_last() : policy_evict_normal();
+      const CUtensorMap* map =
+          (lane == 0) ? &tmA : (rank == 0 ? &tmB1 : &tmB2);
+      const uint8_t* sf_base =
+          (lane == 0) ? p.sfa : (lane == 1 ? p.sfb1 : p.sfb2);
+      const uint32_t dst_off =
+          tiles ? static_cast<uint32_t>(lane * Cf::kABytes)
+                : static_cast<uint32_t>(Cf::kABytes + Cf::kBBytes +
+                                        lane * kSfRunBytes);
+      const uint32_t mask = tiles ? 0x3u : 0x7u;
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -676,48 +690,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       while (ok && work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
-        const int row_a = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
-        const int row_b = n_tile * BN;
+        const int row = (lane == 0)
+                            ? m_tile * 2 * kBM + static_cast<int>(rank) * kBM
+                            : n_tile * BN;
         // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
         // lie wholly past M (M in (256t, 256t + 128] for the last pair
         // tile) it copies the last block instead: its A rows are zero-filled
         // by the tensor map and its accumulator rows are never stored.
-        const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
-                              (p.M + kBM - 1) / kBM - 1);
-        const uint8_t* sfa = p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
-        const size_t sfb_off = (size_t)(row_b / 128) * kblk64 * kSfAtomBytes;
-        const uint8_t* sfb1 = p.sfb1 + sfb_off;
-        const uint8_t* sfb2 = p.sfb2 + sfb_off;
+        const int blk = (lane == 0)
+                            ? min(m_tile * 2 + static_cast<int>(rank),
+                                  (p.M + kBM - 1) / kBM - 1)
+                            : (n_tile * BN) / 128;
+        const uint8_t* sf_src =
+            sf_base + (size_t)blk * kblk64 * kSfAtomBytes;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
                                  kErrProducer)) {
             ok = false;
             break;
           }
-          // Even CTA: the MMAs that read this stage in both CTAs are done;
-          // pass that on to the odd CTA (from the second fill on).
-          if (leader && is_a && issued >= S)
-            mbar_arrive_cluster(mapa_shared(smem_u32(&empty_bar[stage]), 1u));
           uint8_t* st = smem + stage * Cf::kStageBytes;
-          const uint32_t full_c = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          if (is_a) NVFP4DG_STAMP(0, issued);
-          if (is_a) {
-            if (leader)
-              mbar_arrive_expect_tx(&full_bar[stage],
-                                    2 * (Cf::kABytes + Cf::kBBytes));
-            uint8_t* sf = st + Cf::kABytes + Cf::kBBytes;
-            mbar_arrive_expect_tx(&sfdata_bar[stage], 3 * kSfRunBytes);
-            tma_load_2d_pair(st, &tmA, full_c, kb * kRowBytes, row_a, pol_a);
-            bulk_load(sf, sfa + (size_t)kb * kSfRunBytes, kSfRunBytes,
-                      &sfdata_bar[stage], pol_a);
-            bulk_load(sf + kSfRunBytes, sfb1 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &sfdata_bar[stage], pol_b);
-            bulk_load(sf + 2 * kSfRunBytes, sfb2 + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &sfdata_bar[stage], pol_b);
-            NVFP4DG_STAMP(1, issued);
+          if (tiles) {
+            if (lane == 0) {
+              NVFP4DG_STAMP(0, issued);
+              if (leader) {
+                // The MMAs that read this stage in both CTAs are done: pass
+                // that on to the odd CTA (from the second fill on).
+                if (issued >= S)
+                  mbar_arrive_cluster(
+                      mapa_shared(smem_u32(&empty_bar[stage]), 1u));
+                mbar_arrive_expect_tx(&full_bar[stage],
+                                      2 * (Cf::kABytes + Cf::kBBytes));
+              }
+            }
+            __syncwarp(mask);
+            tma_load_2d_pair(st + dst_off, map,
+                             mapa_shared(smem_u32(&full_bar[stage]), 0),
+                             kb * kRowBytes, row, pol);
+            if (lane == 0) NVFP4DG_STAMP(1, issued);
           } else {
-            tma_load_2d_pair(st + Cf::kABytes, tmB, full_c, kb * kRowBytes,
-                             row_b, pol_b);
+            if (lane == 0)
+              mbar_arrive_expect_tx(&sfdata_bar[stage], 3 * kSfRunBytes);
+            __syncwarp(mask);
+            bulk_load(st + dst_off, sf_src + (size_t)kb * kSfRunBytes,
+                      kSfRunBytes, &sfdata_bar[stage], pol);
           }
           ++issued;
           if (++stage == S) {
@@ -727,15 +743,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: the scale runs land on this CTA's own barrier; the A/B tiles
-      // of both CTAs land on the even CTA's `full` barrier, which its
-      // producer A drains (the odd CTA cannot pass the final cluster barrier
+      // of both CTAs land on the even CTA's `full` barrier, which its tile
+      // producer drains (the odd CTA cannot pass the final cluster barrier
       // before that).
       for (int s = 0; s < S; ++s) {
-        if (issued > s && is_a) {
+        if (issued > s) {
           const uint32_t par =
               static_cast<uint32_t>(((issued - 1 - s) / S) & 1);
-          mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain, false);
-          if (leader)
+          if (!tiles)
+            mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain, false);
+          else if (leader)
             mbar_wait_cluster(&full_bar[s], par, p.err, kErrDrain, false);
         }
       }
