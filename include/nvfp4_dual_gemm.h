@@ -66,6 +66,19 @@ extern "C" {
                                                  tiles along K (stream-K)      */
 #define NVFP4DG_FLAG_PAIR (1u << 18)    /* force 2-SM pair tiles (256 rows)    */
 #define NVFP4DG_FLAG_NO_PAIR (1u << 19) /* force single-CTA tiles (128 rows)   */
+#define NVFP4DG_FLAG_SPLITK (1u << 20)  /* force cluster split-K: the two CTAs
+                                           of a cluster take the two halves of
+                                           each tile's K range and exchange
+                                           their partial sums through
+                                           distributed shared memory; needs
+                                           2 x tiles <= SMs and K >= 512     */
+#define NVFP4DG_FLAG_NO_SPLITK (1u << 21) /* never use cluster split-K       */
+#define NVFP4DG_FLAG_NO_PDL (1u << 22)  /* launch without programmatic
+                                           dependent launch (by default the
+                                           kernel may start while the previous
+                                           grid in the stream finishes, and
+                                           waits for it before touching global
+                                           memory)                            */
 
 /*
  * Run the dual GEMM on `stream` using a workspace the library keeps per
@@ -130,12 +143,16 @@ NVFP4DG_API int nvfp4_dual_gemm_device_status(int device, unsigned* word_out);
 /*
  * Describe the schedule the library would use: writes the tile width per
  * GEMM, the CTAs per work unit (1, or 2 for 2-SM pair tiles of 256 rows),
- * the persistent grid in work units, the whole-tile count and the number of
- * tiles split along K.  Host-only; usable without a GPU when `num_sms` > 0.
+ * the persistent grid in work units, the whole-tile count, the number of
+ * tiles split along K by stream-K, and *split_out = 2 when each tile's K
+ * range is split between the two CTAs of a cluster (cluster split-K; the
+ * grid then counts CTAs, two per tile), else 0.  Any out pointer may be
+ * NULL.  Host-only; usable without a GPU when `num_sms` > 0.
  */
 NVFP4DG_API int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
                          int* bn_out, int* ctas_out, int* grid_out,
-                         int* dp_tiles_out, int* sk_tiles_out);
+                         int* dp_tiles_out, int* sk_tiles_out,
+                         int* split_out);
 
 /*
  * Enumerate the work of work unit `cta` (a CTA, or a CTA pair) under the plan

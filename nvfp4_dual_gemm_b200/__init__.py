@@ -26,8 +26,10 @@ from ._lib import (  # noqa: F401
     FLAG_BN128,
     FLAG_FORCE_STREAMK,
     FLAG_NO_PAIR,
+    FLAG_NO_SPLITK,
     FLAG_NO_STREAMK,
     FLAG_PAIR,
+    FLAG_SPLITK,
     FLAG_SYNC_CHECK,
     NativeLibraryError,
 )

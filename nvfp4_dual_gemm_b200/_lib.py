@@ -31,6 +31,9 @@ FLAG_SYNC_CHECK = 1 << 15
 FLAG_FORCE_STREAMK = 1 << 17
 FLAG_PAIR = 1 << 18
 FLAG_NO_PAIR = 1 << 19
+FLAG_SPLITK = 1 << 20
+FLAG_NO_SPLITK = 1 << 21
+FLAG_NO_PDL = 1 << 22
 
 # Size of the static scratch behind nvfp4_dual_gemm_run_noalloc.
 NOALLOC_SCRATCH_BYTES = 4 << 20
@@ -51,7 +54,7 @@ SIGNATURES = {
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "nvfp4_dual_gemm_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip,
-                                  _ip]),
+                                  _ip, _ip]),
     "nvfp4_dual_gemm_plan_work": (_i, [_i, _i, _i, _u, _i, _i, _ip, _i]),
     "nvfp4_dual_gemm_last_error": (ctypes.c_char_p, []),
     "nvfp4_dual_gemm_version": (_i, []),

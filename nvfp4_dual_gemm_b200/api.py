@@ -165,13 +165,15 @@ def workspace_size(M: int, N: int, K: int, flags: int = 0,
 def plan(M: int, N: int, K: int, flags: int = 0, num_sms: int = 148) -> dict:
     """The schedule the library would use (host-only; needs no GPU)."""
     lib = _lib.load()
-    bn, ctas, grid, dp, sk = (ctypes.c_int() for _ in range(5))
+    bn, ctas, grid, dp, sk, split = (ctypes.c_int() for _ in range(6))
     rc = lib.nvfp4_dual_gemm_plan(M, N, K, flags, num_sms, ctypes.byref(bn),
                                   ctypes.byref(ctas), ctypes.byref(grid),
-                                  ctypes.byref(dp), ctypes.byref(sk))
+                                  ctypes.byref(dp), ctypes.byref(sk),
+                                  ctypes.byref(split))
     _lib.check(rc, "nvfp4_dual_gemm_plan")
     return {"bn": bn.value, "ctas": ctas.value, "grid": grid.value,
-            "dp_tiles": dp.value, "sk_tiles": sk.value}
+            "dp_tiles": dp.value, "sk_tiles": sk.value,
+            "split": split.value}
 
 
 def plan_work(M: int, N: int, K: int, cta: int, flags: int = 0,

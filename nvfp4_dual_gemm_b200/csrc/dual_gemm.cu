@@ -135,6 +135,25 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 }
 
 // 32 outputs of one row -> 64 contiguous bytes of C.
+// fp16(silu(x) * y) of 16 columns -> 32 bytes at dst (16-byte aligned).
+__device__ __forceinline__ void store_row16(__half* dst, const float (&x)[16],
+                                            const float (&y)[16]) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint4 v;
+    v.x = pack_half2(silu_mul(x[8 * q + 0], y[8 * q + 0]),
+                     silu_mul(x[8 * q + 1], y[8 * q + 1]));
+    v.y = pack_half2(silu_mul(x[8 * q + 2], y[8 * q + 2]),
+                     silu_mul(x[8 * q + 3], y[8 * q + 3]));
+    v.z = pack_half2(silu_mul(x[8 * q + 4], y[8 * q + 4]),
+                     silu_mul(x[8 * q + 5], y[8 * q + 5]));
+    v.w = pack_half2(silu_mul(x[8 * q + 6], y[8 * q + 6]),
+                     silu_mul(x[8 * q + 7], y[8 * q + 7]));
+    d[q] = v;
+  }
+}
+
 __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
                                             const float (&y)[32]) {
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -199,6 +218,110 @@ constexpr int kSfWarp0 = 7;
 constexpr int kSfWarps = 4;
 static_assert(kThreads == 32 * (kSfWarp0 + kSfWarps), "thread count");
 
+// 256-thread barrier (id 3) of the split-K epilogue (epilogue warps 0-3 and
+// scale warps 7-10) that also ANDs a predicate.
+__device__ __forceinline__ bool split_group_all(bool pred) {
+  uint32_t out;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 3, 256, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(out)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return out != 0;
+}
+
+// Epilogue of a cluster split-K tile, run once by the four epilogue warps
+// (part 0) and the four scale warps (part 1; idle once the main loop is
+// done): each warp owns TMEM lanes 32 (warp % 4) .. + 31, the two parts take
+// alternate 16-column chunks.  Each CTA of the pair holds the partial sums of
+// half of K; CTA h finishes output columns [h BN/2, (h+1) BN/2).  It sends
+// the other half of its partials (GEMM1 then GEMM2 columns) into the peer's
+// operand ring, idle once the peer's MMAs are done, with st.async counted
+// on the peer's `recv` barrier, and adds the peer's partials for its own
+// half.  In the exchange buffer the 16-byte group g of row r sits at
+// (g * 128 + r) * 16, so a warp's 32 rows are contiguous.
+template <int BN>
+__device__ __forceinline__ void split_epilogue(
+    const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
+    uint64_t* ready_bar, uint64_t* recv_bar, int warp, int lane, int part,
+    bool& cluster_waited) {
+  constexpr int kHalf = BN / 2;
+  constexpr int kHalfChunks = kHalf / 16;
+  constexpr uint32_t kXchgBytes = 128u * 2u * kHalf * 4u;
+  const Plan& plan = p.plan;
+  const int own = static_cast<int>(blockIdx.x & 1);
+  const uint32_t peer = static_cast<uint32_t>(own ^ 1);
+  const int row = 32 * (warp % 4) + lane;
+  const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16);
+  const int tile = static_cast<int>(blockIdx.x >> 1);
+  const int m_tile = tile % plan.m_tiles;
+  const int n_tile = tile / plan.m_tiles;
+  const int grow = m_tile * kBM + row;
+  const bool row_ok = grow < p.M;
+  __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+
+  bool ok = mbar_wait(acc_full_bar, 0, p.err, kErrEpilogue);
+  if (!split_group_all(ok)) return;
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(4, 0);
+  tc_fence_after();
+  cluster_wait();  // the peer's barriers are initialised
+  cluster_waited = true;
+  if (part == 0 && threadIdx.x == 0) {
+    mbar_arrive_expect_tx(recv_bar, kXchgBytes);
+    mbar_arrive_cluster(mapa_shared(smem_u32(ready_bar), peer));
+  }
+  ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
+  if (!split_group_all(ok)) return;
+  const uint32_t xbuf = smem_u32(smem);
+  const uint32_t xdst = mapa_shared(xbuf, peer);
+  const uint32_t xbar = mapa_shared(smem_u32(recv_bar), peer);
+#pragma unroll 1
+  for (int c = part; c < 2 * kHalfChunks; c += 2) {
+    const int xy = c / kHalfChunks;  // 0: GEMM1 columns, 1: GEMM2
+    const uint32_t col = static_cast<uint32_t>(
+        xy * BN + static_cast<int>(peer) * kHalf + 16 * (c % kHalfChunks));
+    float v[16];
+    __syncwarp();
+    tc_ld_16cols(t_row + col, v);
+    tc_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float g[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
+      st_async_v4(xdst + ((c * 4 + q) * 128u + row) * 16u, g, xbar);
+    }
+  }
+  ok = mbar_wait(recv_bar, 0, p.err, kErrEpilogue);
+  if (!split_group_all(ok)) return;
+#pragma unroll 1
+  for (int c = part; c < kHalfChunks; c += 2) {
+    float x[16], y[16];
+    __syncwarp();
+    tc_ld_16cols(t_row + own * kHalf + 16 * c, x);
+    tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, y);
+    tc_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint4 rx = lds128(xbuf + ((c * 4 + q) * 128u + row) * 16u);
+      const uint4 ry =
+          lds128(xbuf + (((kHalfChunks + c) * 4 + q) * 128u + row) * 16u);
+      x[4 * q + 0] += __uint_as_float(rx.x);
+      x[4 * q + 1] += __uint_as_float(rx.y);
+      x[4 * q + 2] += __uint_as_float(rx.z);
+      x[4 * q + 3] += __uint_as_float(rx.w);
+      y[4 * q + 0] += __uint_as_float(ry.x);
+      y[4 * q + 1] += __uint_as_float(ry.y);
+      y[4 * q + 2] += __uint_as_float(ry.z);
+      y[4 * q + 3] += __uint_as_float(ry.w);
+    }
+    if (row_ok) store_row16(crow + own * kHalf + 16 * c, x, y);
+  }
+  tc_fence_before();
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(5, 0);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -218,6 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_full_bar;
   __shared__ __align__(8) uint64_t acc_empty_bar;
   __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(8) uint64_t ready_bar;  // split-K: peer may write
+  __shared__ __align__(8) uint64_t recv_bar;   // split-K: peer's half landed
   __shared__ uint32_t tmem_base_sh;
   __shared__ int finisher_sh;
 
@@ -240,6 +365,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&acc_full_bar, 1);
     mbar_init(&acc_empty_bar, 32 * kEpiWarps);
     mbar_init(&drain_bar, 1);
+    mbar_init(&ready_bar, 1);
+    mbar_init(&recv_bar, 1);
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
@@ -252,6 +379,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // Split-K clusters: every thread arrives on the cluster barrier once the
+  // barriers are initialised; the epilogue waits on it before its first
+  // remote operation, the other warps at teardown.
+  if (plan.split == 2) cluster_arrive();
+  // Whether this thread has waited on that arrival (warp-uniform).
+  bool cluster_waited = false;
+  // Everything above touched only this CTA's on-chip state; the inputs, C and
+  // the workspace may be written by the previous grid in the stream.
+  griddep_launch_dependents();
+  griddep_wait();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;  // scale atoms per 128-row block
@@ -410,6 +547,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // Split-K: the scale warps help finish the tile.
+    if (plan.split == 2)
+      split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, &recv_bar,
+                         warp, lane, 1, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -474,6 +615,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
     }
     __syncwarp();
+  } else if (plan.split == 2) {
+    // ------------------------------------------------------------ epilogue
+    split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, &recv_bar,
+                       warp, lane, 0, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
     const int row = threadIdx.x;  // TMEM lane == tile row
@@ -567,6 +712,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  // Split-K: neither CTA leaves while its peer may still write into it
+  // (the epilogue warps have already waited on the start-up phase).
+  if (plan.split == 2) {
+    if (!cluster_waited) cluster_wait();
+    cluster_sync();
+  }
   if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
@@ -657,6 +808,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
+  griddep_launch_dependents();
+  griddep_wait();  // global memory only after the previous grid completes
   const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;
 
@@ -1243,16 +1396,41 @@ Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
   return p;
 }
 
+// Cluster split-K: one tile per pair of CTAs, each CTA half of K.
+Plan plan_split(int M, int N, int K, int bn) {
+  Plan p{};
+  p.bn = bn;
+  p.ctas = 1;
+  p.m_tiles = (M + kBM - 1) / kBM;
+  p.n_tiles = N / bn;
+  p.kblocks = K / 256;
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.grid = 2 * p.num_tiles;
+  p.dp_tiles = p.num_tiles;
+  p.sk_iters = 0;
+  p.split = 2;
+  return p;
+}
+
+bool split_fits(int M, int N, int K, int bn, int sms) {
+  if (N % bn != 0 || K / 256 < 2) return false;
+  const long long tiles = (long long)((M + kBM - 1) / kBM) * (N / bn);
+  return 2 * tiles <= sms;
+}
+
+// Estimated SM cycles of the busiest work unit.  The K-block period is set
+// by the issuing threads' instruction chains (about 700 cycles for either
+// tile width, measured); the epilogue of a tile costs ~34 cycles per output
+// column; a stream-K partial is written and read back at the ~7.5 B/cycle
+// that the row-per-thread partial layout achieves.
 double plan_cost(const Plan& p) {
-  const double a_bytes = 128.0 * kRowBytes;
-  const double b_bytes = (p.ctas == 2 ? 1.0 : 2.0) * p.bn * kRowBytes;
-  const double bytes = a_bytes + b_bytes + 3.0 * kSfRunBytes;
-  const double mma = (p.bn == 128) ? 512.0 : 280.0;
-  const double per_block = std::max(bytes / 55.0, p.ctas == 2 && p.bn == 64
-                                                       ? 256.0
-                                                       : mma);
+  const double per_block = (p.bn == 128) ? 720.0 : 700.0;
   const double epi = 34.0 * p.bn;
   const double slot_bytes = 128.0 * 2 * p.bn * 4;
+  if (p.split == 2) {
+    const double xchg = 128.0 * p.bn * 4 / 32.0;  // DSMEM exchange
+    return ((p.kblocks + 1) / 2) * per_block + xchg + epi / 2 + 2000.0;
+  }
   double cost = 0;
   if (p.dp_tiles > 0) {
     const double tiles = (double)((p.dp_tiles + p.grid - 1) / p.grid);
@@ -1263,7 +1441,7 @@ double plan_cost(const Plan& p) {
     const bool split = (p.sk_iters % p.grid) != 0 ||
                        ((p.sk_iters / p.grid) % p.kblocks) != 0;
     cost += per_unit * per_block + epi * 2;
-    if (split) cost += 3.0 * slot_bytes / 55.0;
+    if (split) cost += 2.5 * slot_bytes / 7.5;
   }
   return cost + 2000.0;
 }
@@ -1288,6 +1466,25 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
   if (!(flags & NVFP4DG_FLAG_PAIR) || sms < 2) ctas_opts[nc++] = 1;
   Plan best{};
   double best_cost = 1e300;
+  if (flags & NVFP4DG_FLAG_SPLITK) {
+    for (int i = 0; i < nb; ++i)
+      if (split_fits(M, N, K, bns[i], forced > 0 ? forced : sms))
+        return plan_split(M, N, K, bns[i]);
+    return best;  // grid == 0: not possible (rejected by check_problem)
+  }
+  if (!(flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_PAIR |
+                 NVFP4DG_FLAG_FORCE_STREAMK)) &&
+      forced == 0) {
+    for (int i = 0; i < nb; ++i) {
+      if (!split_fits(M, N, K, bns[i], sms)) continue;
+      Plan p = plan_split(M, N, K, bns[i]);
+      const double cost = plan_cost(p);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = p;
+      }
+    }
+  }
   for (int c = 0; c < nc; ++c) {
     const int ctas = ctas_opts[c];
     // forced grid counts CTAs; pairs use half as many units
@@ -1327,6 +1524,11 @@ int check_problem(const void* A, const void* B1, const void* B2,
                 "FORCE_STREAMK and NO_STREAMK flags are exclusive");
   if ((flags & NVFP4DG_FLAG_PAIR) && (flags & NVFP4DG_FLAG_NO_PAIR))
     return fail(NVFP4DG_ERR_INVALID, "PAIR and NO_PAIR flags are exclusive");
+  if ((flags & NVFP4DG_FLAG_SPLITK) &&
+      (flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_PAIR |
+                NVFP4DG_FLAG_FORCE_STREAMK)))
+    return fail(NVFP4DG_ERR_INVALID,
+                "SPLITK excludes NO_SPLITK, PAIR and FORCE_STREAMK");
   if (M == 0 || N == 0) return NVFP4DG_OK;
   const void* ptrs[7] = {A, B1, B2, SFA, SFB1, SFB2, C};
   const char* names[7] = {"A", "B1", "B2", "SFA", "SFB1", "SFB2", "C"};
@@ -1345,7 +1547,7 @@ template <int BN, bool PAIR>
 int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
            const void* B1, const void* B2, const void* SFA, const void* SFB1,
            const void* SFB2, void* C, int M, int N, int K, void* ws,
-           cudaStream_t stream) {
+           unsigned flags, cudaStream_t stream) {
   constexpr int kSmem = PAIR ? PairCfg<BN>::kSmemBytes : Cfg<BN>::kSmemBytes;
   auto kernel = PAIR ? dual_gemm_pair_kernel<BN> : dual_gemm_kernel<BN>;
   bool& attr = PAIR ? (BN == 64 ? dev.attr64p : dev.attr128p)
@@ -1375,9 +1577,31 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
                                               workspace_partials_offset(plan))
                    : nullptr;
   kp.err = dev.err;
-  kernel<<<plan.grid * plan.ctas, kThreads, kSmem, stream>>>(ta, tb1, tb2,
-                                                              kp);
-  cudaError_t e = cudaGetLastError();
+  // Programmatic dependent launch lets this grid be scheduled while the
+  // previous one in the stream finishes (the kernel waits for it before its
+  // first global access); split-K plans run as 2-CTA clusters.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid * plan.ctas, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  unsigned na = 0;
+  if (!(flags & NVFP4DG_FLAG_NO_PDL)) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (!PAIR && plan.split == 2) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = 2;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb1, tb2, kp);
   if (e != cudaSuccess) return cuda_fail(e, "dual_gemm_kernel launch");
   return NVFP4DG_OK;
 }
@@ -1423,6 +1647,9 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   DevInfo* dev = nullptr;
   if ((rc = device_info(devid, &dev))) return rc;
   const Plan plan = choose_plan(M, N, K, flags, dev->sms);
+  if (plan.grid == 0)
+    return fail(NVFP4DG_ERR_UNSUPPORTED,
+                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
   const size_t need = static_cast<size_t>(workspace_bytes(plan));
   if (own_ws && need > 0) {
     WsEntry& ent = g_ws[{devid, stream_ptr}];
@@ -1456,16 +1683,16 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   }
   if (plan.ctas == 2 && plan.bn == 128)
     rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, stream);
+                           N, K, ws, flags, stream);
   else if (plan.ctas == 2)
     rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                          N, K, ws, stream);
+                          N, K, ws, flags, stream);
   else if (plan.bn == 128)
     rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, stream);
+                            M, N, K, ws, flags, stream);
   else
     rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                           M, N, K, ws, stream);
+                           M, N, K, ws, flags, stream);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;
@@ -1552,6 +1779,9 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
   void* scratch = nullptr;
   if ((rc = noalloc_scratch(devid, &scratch))) return rc;
   const Plan plan = choose_plan(M, N, K, flags, dev->sms);
+  if (plan.grid == 0)
+    return fail(NVFP4DG_ERR_UNSUPPORTED,
+                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
   const size_t need = static_cast<size_t>(workspace_bytes(plan));
   if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
     return fail(NVFP4DG_ERR_WORKSPACE,
@@ -1571,16 +1801,16 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
   }
   if (plan.ctas == 2 && plan.bn == 128)
     rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, stream);
+                           N, K, ws, flags, stream);
   else if (plan.ctas == 2)
     rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                          N, K, ws, stream);
+                          N, K, ws, flags, stream);
   else if (plan.bn == 128)
     rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, stream);
+                            M, N, K, ws, flags, stream);
   else
     rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                           M, N, K, ws, stream);
+                           M, N, K, ws, flags, stream);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;
@@ -1615,11 +1845,16 @@ size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
 
 int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
                          int* bn_out, int* ctas_out, int* grid_out,
-                         int* dp_tiles_out, int* sk_tiles_out) {
+                         int* dp_tiles_out, int* sk_tiles_out,
+                         int* split_out) {
   g_last_error.clear();
   if (M <= 0 || N <= 0 || K <= 0 || N % 64 || K % 256 || num_sms <= 0)
     return fail(NVFP4DG_ERR_INVALID, "invalid problem for planning");
   const Plan p = choose_plan(M, N, K, flags, num_sms);
+  if (p.grid == 0)
+    return fail(NVFP4DG_ERR_UNSUPPORTED,
+                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
+  if (split_out) *split_out = p.split;
   if (bn_out) *bn_out = p.bn;
   if (ctas_out) *ctas_out = p.ctas;
   if (grid_out) *grid_out = p.grid;

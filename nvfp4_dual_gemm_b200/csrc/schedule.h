@@ -37,6 +37,8 @@ struct Plan {
   int bn;           // tile width per GEMM (64 or 128)
   int ctas;         // CTAs per work unit: 1, or 2 for a 2-SM pair (M = 256)
   long long sk_iters;  // (num_tiles - dp_tiles) * kblocks
+  int split;        // 2: the two CTAs of a cluster split each tile's K range
+                    // (unit b = CTA b: tile b / 2, K half b % 2); else 0
 };
 
 struct Work {
@@ -87,6 +89,18 @@ NVFP4DG_HD void work_begin(const Plan& p, int b, WorkIter& s) {
 }
 
 NVFP4DG_HD bool work_next(const Plan& p, WorkIter& s, Work& w) {
+  if (p.split == 2) {
+    // Cluster split-K: one work item per CTA, K blocks [0, h) on the even
+    // CTA and [h, kblocks) on the odd one (kblocks >= 2).
+    if (!s.first_sk) return false;
+    s.first_sk = 0;
+    const int h = (p.kblocks + 1) / 2;
+    w.tile = s.b / 2;
+    w.kb0 = (s.b & 1) ? h : 0;
+    w.kb1 = (s.b & 1) ? p.kblocks : h;
+    w.slot = -1;
+    return true;
+  }
   if (s.dp_next < p.dp_tiles) {
     w.tile = s.dp_next;
     w.kb0 = 0;

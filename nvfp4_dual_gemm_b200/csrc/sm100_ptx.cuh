@@ -239,6 +239,21 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 }
 
 // Each thread of the warp reads 32 consecutive fp32 columns of its TMEM lane.
+// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes -> v[0..15].
+__device__ __forceinline__ void tc_ld_16cols(uint32_t taddr, float (&v)[16]) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_ld_32cols(uint32_t taddr, float (&v)[32]) {
   uint32_t* r = reinterpret_cast<uint32_t*>(v);
   asm volatile(
@@ -322,6 +337,47 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 }
 
 // Cluster-wide execution barrier (every thread of every CTA of the cluster).
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their memory is visible (a no-op when launched without
+// the programmatic attribute), and allow the next grid in the stream to be
+// scheduled before this one ends.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Split-phase cluster barrier: every thread of every CTA of the cluster
+// arrives (release) and later waits (acquire); a thread must wait before it
+// arrives again.
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) from
+// this CTA's shared memory to another CTA's (cluster address); completion is
+// counted as transaction bytes on the destination CTA's mbarrier.
+__device__ __forceinline__ void bulk_s2s_cluster(uint32_t dst_cluster,
+                                                 uint32_t src_cta,
+                                                 uint32_t bytes,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(dst_cluster),
+      "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+      : "memory");
+}
+
+__device__ __forceinline__ void sts128(uint32_t saddr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
 __device__ __forceinline__ void cluster_sync() {
   asm volatile(
       "barrier.cluster.arrive.release.aligned;\n\t"
@@ -336,6 +392,20 @@ __device__ __forceinline__ void cluster_sync() {
 // stores, TMEM accumulator reads) complete before the arrival
 // (tcgen05.wait::st / ::ld) and are ordered for the MMA by the tcgen05
 // fences around the barrier, the pattern CUTLASS's 2-SM pipelines use.
+// 16-byte store into another CTA's shared memory (cluster address) whose
+// completion is counted as 16 transaction bytes on an mbarrier of that CTA.
+__device__ __forceinline__ void st_async_v4(uint32_t cluster_addr,
+                                            const float (&v)[4],
+                                            uint32_t cluster_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], "
+      "{%1, %2, %3, %4}, [%5];" ::"r"(cluster_addr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+      "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(cluster_bar)
+      : "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(
                    cluster_addr)

@@ -86,14 +86,18 @@ def cover(m, n, k, flags=0, sms=148):
     kb = k // 256
     seen = defaultdict(list)
     slots = set()
+    split = pl["split"] == 2
     for cta in range(pl["grid"]):
-        for tile, k0, k1, slot in dg.plan_work(m, n, k, cta, flags, sms):
+        recs = dg.plan_work(m, n, k, cta, flags, sms)
+        if split:  # one record per CTA: tile cta // 2, K half cta % 2
+            assert len(recs) == 1 and recs[0][0] == cta // 2
+        for tile, k0, k1, slot in recs:
             assert 0 <= tile < tiles and 0 <= k0 < k1 <= kb
             seen[tile].append((k0, k1, slot, cta))
             if slot >= 0:
                 assert slot // 2 == cta and slot not in slots
                 slots.add(slot)
-            else:
+            elif not split:
                 assert (k0, k1) == (0, kb)
     assert sorted(seen) == list(range(tiles))
     for tile, segs in seen.items():
@@ -102,7 +106,9 @@ def cover(m, n, k, flags=0, sms=148):
         assert segs[0][0] == 0 and segs[-1][1] == kb
         for a, b in zip(segs, segs[1:]):
             assert a[1] == b[0]
-        if len(segs) > 1:
+        if split:
+            assert len(segs) == 2 and [s[3] % 2 for s in segs] == [0, 1]
+        elif len(segs) > 1:
             assert all(s[2] >= 0 for s in segs)
             assert tile >= pl["dp_tiles"]
     return pl, seen
@@ -164,3 +170,34 @@ def test_bn_flags():
 def test_decode_shape_uses_every_sm_or_whole_tiles():
     pl = dg.plan(256, 4096, 7168)
     assert pl["grid"] * pl["ctas"] <= 148
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 7168), (256, 512, 2048),
+                                   (200, 256, 768), (333, 192, 1024),
+                                   (128, 64, 512)])
+def test_cluster_split_k_covers_every_block_once(m, n, k):
+    pl, seen = cover(m, n, k, flags=dg.FLAG_SPLITK)
+    assert pl["split"] == 2 and pl["ctas"] == 1 and pl["sk_tiles"] == 0
+    assert pl["grid"] == 2 * len(seen) <= 148
+    h = (k // 256 + 1) // 2
+    for segs in seen.values():
+        assert [(a, b) for a, b, _, _ in sorted(segs)] == [(0, h), (h, k // 256)]
+
+
+def test_cluster_split_k_choice_and_limits():
+    # decode shape: 64 tiles of 128 columns -> 128 CTAs in 64 clusters
+    pl = dg.plan(256, 4096, 7168)
+    assert pl["split"] == 2 and pl["bn"] == 128 and pl["grid"] == 128
+    assert dg.plan(256, 4096, 7168, dg.FLAG_NO_SPLITK)["split"] == 0
+    # too many tiles for 2 CTAs each, or a single K block: not possible
+    for shape in ((4096, 14336, 4096), (256, 4096, 256)):
+        with pytest.raises(RuntimeError):
+            dg.plan(*shape, dg.FLAG_SPLITK)
+        assert dg.plan(*shape)["split"] == 0
+    # exclusive flags are rejected before any GPU work
+    lib = _lib.load()
+    ptr = ctypes.c_void_p(16)
+    for bad in (dg.FLAG_PAIR, dg.FLAG_NO_SPLITK, dg.FLAG_FORCE_STREAMK):
+        rc = lib.nvfp4_dual_gemm_run(ptr, ptr, ptr, ptr, ptr, ptr, ptr, 256,
+                                     512, 2048, 1, dg.FLAG_SPLITK | bad, None)
+        assert rc == _lib.ERR_INVALID and "SPLITK" in _lib.last_error()

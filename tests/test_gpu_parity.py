@@ -111,6 +111,26 @@ def test_ragged_m_and_small_shapes(m, n, k, pair):
     assert_close(run(p, pair), O.reference_output(p), f"{m}x{n}x{k}")
 
 
+@pytest.mark.parametrize("m,n,k,bn", [(256, 512, 2048, 128),
+                                      (256, 512, 2048, 64),
+                                      (200, 256, 768, 128),
+                                      (333, 192, 1024, 64),
+                                      (128, 128, 512, 128)])
+def test_cluster_split_k(m, n, k, bn):
+    p = O.make_problem(m, n, k, seed=m + 7 * n + k)
+    flags = _lib.FLAG_SPLITK | (_lib.FLAG_BN64 if bn == 64 else
+                                _lib.FLAG_BN128) | _lib.FLAG_SYNC_CHECK
+    assert dg.plan(m, n, k, flags)["split"] == 2
+    ref = O.reference_output(p)
+    d = to_device(p)
+    for _ in range(2):  # twice: no state may leak between launches
+        d["c"].fill_(float("nan"))
+        dg.dual_gemm(d["a"], d["b1"], d["b2"], d["sfa_blocked"],
+                     d["sfb1_blocked"], d["sfb2_blocked"], d["c"], flags=flags)
+        torch.cuda.synchronize()
+        assert_close(d["c"].cpu().numpy(), ref, f"split {m}x{n}x{k} bn={bn}")
+
+
 # The 13 shapes of the reference's dispatch table (nvfp4_dual_gemm.cu:403-442)
 REFERENCE_SHAPES = [
     (256, 4096, 7168), (512, 4096, 7168), (256, 3072, 4096), (512, 3072, 7168),
