@@ -235,14 +235,17 @@ __device__ __forceinline__ bool split_group_all(bool pred) {
 
 // Epilogue of a cluster split-K tile, run once by the four epilogue warps
 // (part 0) and the four scale warps (part 1; idle once the main loop is
-// done): each warp owns TMEM lanes 32 (warp % 4) .. + 31, the two parts take
-// alternate 16-column chunks.  Each CTA of the pair holds the partial sums of
-// half of K; CTA h finishes output columns [h BN/2, (h+1) BN/2).  It sends
-// the other half of its partials (GEMM1 then GEMM2 columns) into the peer's
-// operand ring, idle once the peer's MMAs are done, with st.async counted
-// on the peer's `recv` barrier, and adds the peer's partials for its own
-// half.  In the exchange buffer the 16-byte group g of row r sits at
-// (g * 128 + r) * 16, so a warp's 32 rows are contiguous.
+// done): each warp owns TMEM lanes 32 (warp % 4) .. + 31.  Each CTA of the
+// pair holds the partial sums of half of K; CTA h finishes output columns
+// [h BN/2, (h+1) BN/2) in 16-column chunks j, part (j % 2) taking chunk j.
+// For each of its chunks a warp sends the peer's GEMM1 and GEMM2 partials of
+// chunk j into the peer's operand ring (idle once the peer's MMAs are done)
+// with st.async counted on the peer's barrier recv_bar[j]; then it adds the
+// peer's partials of its own chunks as they land, so the combine of early
+// chunks overlaps the exchange of later ones.  In the exchange buffer the
+// 16-byte group g of row r sits at (g * 128 + r) * 16 (GEMM1 chunk j: groups
+// 4j .. 4j+3, GEMM2 chunk j: groups 4 (BN/32 + j) ..), so a warp's 32 rows
+// are contiguous.
 template <int BN>
 __device__ __forceinline__ void split_epilogue(
     const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
@@ -250,7 +253,7 @@ __device__ __forceinline__ void split_epilogue(
     bool& cluster_waited) {
   constexpr int kHalf = BN / 2;
   constexpr int kHalfChunks = kHalf / 16;
-  constexpr uint32_t kXchgBytes = 128u * 2u * kHalf * 4u;
+  constexpr uint32_t kChunkBytes = 2u * 128u * 16u * 4u;  // GEMM1 + GEMM2
   const Plan& plan = p.plan;
   const int own = static_cast<int>(blockIdx.x & 1);
   const uint32_t peer = static_cast<uint32_t>(own ^ 1);
@@ -270,37 +273,43 @@ __device__ __forceinline__ void split_epilogue(
   cluster_wait();  // the peer's barriers are initialised
   cluster_waited = true;
   if (part == 0 && threadIdx.x == 0) {
-    mbar_arrive_expect_tx(recv_bar, kXchgBytes);
+#pragma unroll
+    for (int c = 0; c < kHalfChunks; ++c)
+      mbar_arrive_expect_tx(&recv_bar[c], kChunkBytes);
     mbar_arrive_cluster(mapa_shared(smem_u32(ready_bar), peer));
   }
   ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
   if (!split_group_all(ok)) return;
   const uint32_t xbuf = smem_u32(smem);
   const uint32_t xdst = mapa_shared(xbuf, peer);
-  const uint32_t xbar = mapa_shared(smem_u32(recv_bar), peer);
 #pragma unroll 1
-  for (int c = part; c < 2 * kHalfChunks; c += 2) {
-    const int xy = c / kHalfChunks;  // 0: GEMM1 columns, 1: GEMM2
-    const uint32_t col = static_cast<uint32_t>(
-        xy * BN + static_cast<int>(peer) * kHalf + 16 * (c % kHalfChunks));
-    float v[16];
-    __syncwarp();
-    tc_ld_16cols(t_row + col, v);
-    tc_wait_ld();
+  for (int c = part; c < kHalfChunks; c += 2) {
+    const uint32_t cbar = mapa_shared(smem_u32(&recv_bar[c]), peer);
+#pragma unroll 1
+    for (int xy = 0; xy < 2; ++xy) {
+      const uint32_t col = static_cast<uint32_t>(
+          xy * BN + static_cast<int>(peer) * kHalf + 16 * c);
+      const int g0 = 4 * (xy * kHalfChunks + c);
+      float v[16];
+      __syncwarp();
+      tc_ld_16cols(t_row + col, v);
+      tc_wait_ld();
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float g[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
-      st_async_v4(xdst + ((c * 4 + q) * 128u + row) * 16u, g, xbar);
+      for (int q = 0; q < 4; ++q) {
+        const float g[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2],
+                            v[4 * q + 3]};
+        st_async_v4(xdst + ((g0 + q) * 128u + row) * 16u, g, cbar);
+      }
     }
   }
-  ok = mbar_wait(recv_bar, 0, p.err, kErrEpilogue);
-  if (!split_group_all(ok)) return;
+  bool all_ok = true;
 #pragma unroll 1
   for (int c = part; c < kHalfChunks; c += 2) {
     float x[16], y[16];
     __syncwarp();
     tc_ld_16cols(t_row + own * kHalf + 16 * c, x);
     tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, y);
+    all_ok = mbar_wait(&recv_bar[c], 0, p.err, kErrEpilogue) && all_ok;
     tc_wait_ld();
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -316,8 +325,11 @@ __device__ __forceinline__ void split_epilogue(
       y[4 * q + 2] += __uint_as_float(ry.z);
       y[4 * q + 3] += __uint_as_float(ry.w);
     }
+    // after an expired wait the values are stale but every access stays in
+    // bounds; the error word reports it
     if (row_ok) store_row16(crow + own * kHalf + 16 * c, x, y);
   }
+  split_group_all(all_ok);  // every participant finishes the tile together
   tc_fence_before();
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(5, 0);
 }
@@ -342,7 +354,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_empty_bar;
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ __align__(8) uint64_t ready_bar;  // split-K: peer may write
-  __shared__ __align__(8) uint64_t recv_bar;   // split-K: peer's half landed
+  // split-K: the peer's partials of chunk j of this CTA's half landed
+  __shared__ __align__(8) uint64_t recv_bar[BN / 32];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int finisher_sh;
 
@@ -366,7 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&acc_empty_bar, 32 * kEpiWarps);
     mbar_init(&drain_bar, 1);
     mbar_init(&ready_bar, 1);
-    mbar_init(&recv_bar, 1);
+    for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
@@ -549,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
-      split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, &recv_bar,
+      split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
                          warp, lane, 1, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -617,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
-    split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, &recv_bar,
+    split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
                        warp, lane, 0, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
