@@ -98,9 +98,24 @@ __device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
     if (blockIdx.x < kTraceCtas && (idx) < kTraceSlots)            \
       g_trace[blockIdx.x][role][idx] = clock_cycles();             \
   } while (0)
+// Global-timer (ns, comparable across SMs) stamps of thread 0 in role 5,
+// slots 61-63: kernel entry, past the dependency wait, exit; the SM clock at
+// the same moments goes to role 4, same slots.
+#define NVFP4DG_STAMP_NS(idx)                                      \
+  do {                                                             \
+    if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {             \
+      long long t_;                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));       \
+      g_trace[blockIdx.x][4][idx] = clock_cycles();                \
+      g_trace[blockIdx.x][5][idx] = t_;                            \
+    }                                                              \
+  } while (0)
 #else
 #define NVFP4DG_STAMP(role, idx) \
   do {                           \
+  } while (0)
+#define NVFP4DG_STAMP_NS(idx) \
+  do {                        \
   } while (0)
 #endif
 
@@ -266,6 +281,7 @@ __device__ __forceinline__ void split_epilogue(
   const bool row_ok = grow < p.M;
   __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
 
+  griddep_wait();  // global memory only after the previous grid
   bool ok = mbar_wait(acc_full_bar, 0, p.err, kErrEpilogue);
   if (!split_group_all(ok)) return;
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(4, 0);
@@ -282,52 +298,75 @@ __device__ __forceinline__ void split_epilogue(
   if (!split_group_all(ok)) return;
   const uint32_t xbuf = smem_u32(smem);
   const uint32_t xdst = mapa_shared(xbuf, peer);
-#pragma unroll 1
-  for (int c = part; c < kHalfChunks; c += 2) {
-    const uint32_t cbar = mapa_shared(smem_u32(&recv_bar[c]), peer);
-#pragma unroll 1
-    for (int xy = 0; xy < 2; ++xy) {
-      const uint32_t col = static_cast<uint32_t>(
-          xy * BN + static_cast<int>(peer) * kHalf + 16 * c);
-      const int g0 = 4 * (xy * kHalfChunks + c);
-      float v[16];
-      __syncwarp();
-      tc_ld_16cols(t_row + col, v);
-      tc_wait_ld();
+  // This warp's chunks j = part, part + 2 (at most two): all TMEM loads are
+  // issued before one wait, then the stores go out.
+  constexpr int kMine = (kHalfChunks + 1) / 2;
+  float v[kMine][2][16];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float g[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2],
-                            v[4 * q + 3]};
-        st_async_v4(xdst + ((g0 + q) * 128u + row) * 16u, g, cbar);
+  for (int i = 0; i < kMine; ++i) {
+    const int c = part + 2 * i;
+    if (c < kHalfChunks) {
+#pragma unroll
+      for (int xy = 0; xy < 2; ++xy)
+        tc_ld_16cols(t_row + static_cast<uint32_t>(
+                                 xy * BN + static_cast<int>(peer) * kHalf +
+                                 16 * c),
+                     v[i][xy]);
+    }
+  }
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    const int c = part + 2 * i;
+    if (c < kHalfChunks) {
+      const uint32_t cbar = mapa_shared(smem_u32(&recv_bar[c]), peer);
+#pragma unroll
+      for (int xy = 0; xy < 2; ++xy) {
+        const int g0 = 4 * (xy * kHalfChunks + c);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float g[4] = {v[i][xy][4 * q], v[i][xy][4 * q + 1],
+                              v[i][xy][4 * q + 2], v[i][xy][4 * q + 3]};
+          st_async_v4(xdst + ((g0 + q) * 128u + row) * 16u, g, cbar);
+        }
       }
     }
   }
   bool all_ok = true;
-#pragma unroll 1
-  for (int c = part; c < kHalfChunks; c += 2) {
-    float x[16], y[16];
-    __syncwarp();
-    tc_ld_16cols(t_row + own * kHalf + 16 * c, x);
-    tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, y);
+  // Own chunks: both TMEM reads before one wait, then each chunk as soon as
+  // the peer's partials of it have landed.
+  float ox[kMine][16], oy[kMine][16];
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    const int c = part + 2 * i;
+    if (c < kHalfChunks) {
+      tc_ld_16cols(t_row + own * kHalf + 16 * c, ox[i]);
+      tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, oy[i]);
+    }
+  }
+  tc_wait_ld();
+#pragma unroll
+  for (int i = 0; i < kMine; ++i) {
+    const int c = part + 2 * i;
+    if (c >= kHalfChunks) continue;
     all_ok = mbar_wait(&recv_bar[c], 0, p.err, kErrEpilogue) && all_ok;
-    tc_wait_ld();
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 rx = lds128(xbuf + ((c * 4 + q) * 128u + row) * 16u);
       const uint4 ry =
           lds128(xbuf + (((kHalfChunks + c) * 4 + q) * 128u + row) * 16u);
-      x[4 * q + 0] += __uint_as_float(rx.x);
-      x[4 * q + 1] += __uint_as_float(rx.y);
-      x[4 * q + 2] += __uint_as_float(rx.z);
-      x[4 * q + 3] += __uint_as_float(rx.w);
-      y[4 * q + 0] += __uint_as_float(ry.x);
-      y[4 * q + 1] += __uint_as_float(ry.y);
-      y[4 * q + 2] += __uint_as_float(ry.z);
-      y[4 * q + 3] += __uint_as_float(ry.w);
+      ox[i][4 * q + 0] += __uint_as_float(rx.x);
+      ox[i][4 * q + 1] += __uint_as_float(rx.y);
+      ox[i][4 * q + 2] += __uint_as_float(rx.z);
+      ox[i][4 * q + 3] += __uint_as_float(rx.w);
+      oy[i][4 * q + 0] += __uint_as_float(ry.x);
+      oy[i][4 * q + 1] += __uint_as_float(ry.y);
+      oy[i][4 * q + 2] += __uint_as_float(ry.z);
+      oy[i][4 * q + 3] += __uint_as_float(ry.w);
     }
     // after an expired wait the values are stale but every access stays in
     // bounds; the error word reports it
-    if (row_ok) store_row16(crow + own * kHalf + 16 * c, x, y);
+    if (row_ok) store_row16(crow + own * kHalf + 16 * c, ox[i], oy[i]);
   }
   split_group_all(all_ok);  // every participant finishes the tile together
   tc_fence_before();
@@ -364,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
 
+  NVFP4DG_STAMP_NS(61);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const Plan& plan = p.plan;
@@ -395,13 +435,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Split-K clusters: every thread arrives on the cluster barrier once the
   // barriers are initialised; the epilogue waits on it before its first
   // remote operation, the other warps at teardown.
-  if (plan.split == 2) cluster_arrive();
+  if (plan.split == 2) cluster_arrive_relaxed();
   // Whether this thread has waited on that arrival (warp-uniform).
   bool cluster_waited = false;
+  // The producers' L2 cache policies (createpolicy is slow; its latency
+  // overlaps the wait for the previous grid).
+  uint64_t copy_policy = 0;
+  if ((warp == kProdAWarp || warp == kProdBWarp) && lane < 3)
+    copy_policy = (lane == 0) ? policy_evict_last() : policy_evict_normal();
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
+  // Each role waits for the previous grid (griddepcontrol.wait) only after
+  // its own setup, so the first pass through its code overlaps that wait.
   griddep_launch_dependents();
-  griddep_wait();
+  NVFP4DG_STAMP_NS(62);
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;  // scale atoms per 128-row block
@@ -416,8 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warps can move them into TMEM while the tiles are in flight.
     const bool tiles = (warp == kProdAWarp);
     if (lane < 3) {
-      const uint64_t pol =
-          (lane == 0) ? policy_evict_last() : policy_evict_normal();
+      const uint64_t pol = copy_policy;
       const CUtensorMap* map = (lane == 0) ? &tmA : (lane == 1 ? &tmB1 : &tmB2);
       const uint8_t* sf_base =
           (lane == 0) ? p.sfa : (lane == 1 ? p.sfb1 : p.sfb2);
@@ -436,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       WorkIter it;
       work_begin(plan, blockIdx.x, it);
       Work w;
-      while (ok && work_next(plan, it, w)) {
+      bool have = work_next(plan, it, w);
+      griddep_wait();  // global memory only after the previous grid
+      for (; ok && have; have = work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
         const int row = (lane == 0) ? m_tile * kBM : n_tile * BN;
@@ -491,7 +539,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     WorkIter it;
     work_begin(plan, blockIdx.x, it);
     Work w;
-    while (ok && work_next(plan, it, w)) {
+    bool have = work_next(plan, it, w);
+    griddep_wait();  // global memory only after the previous grid
+    for (; ok && have; have = work_next(plan, it, w)) {
       // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
       const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
@@ -581,7 +631,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       WorkIter it;
       work_begin(plan, blockIdx.x, it);
       Work w;
-      while (ok && work_next(plan, it, w)) {
+      bool have = work_next(plan, it, w);
+      griddep_wait();  // global memory only after the previous grid
+      for (; ok && have; have = work_next(plan, it, w)) {
         if (!mbar_wait(&acc_empty_bar, acc_phase ^ 1u, p.err, kErrMma)) {
           ok = false;
           break;
@@ -641,7 +693,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     WorkIter it;
     work_begin(plan, blockIdx.x, it);
     Work w;
-    while (work_next(plan, it, w)) {
+    bool have = work_next(plan, it, w);
+    griddep_wait();  // global memory only after the previous grid
+    for (; have; have = work_next(plan, it, w)) {
       const bool got = mbar_wait(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
@@ -736,6 +790,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  NVFP4DG_STAMP_NS(63);
 }
 
 // ===========================================================================
@@ -790,6 +845,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
 
+  NVFP4DG_STAMP_NS(61);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const Plan& plan = p.plan;
@@ -819,10 +875,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tmem_relinquish_pair();
   }
   tc_fence_before();
-  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  __syncthreads();  // TMEM base and barrier inits visible within the CTA
+  // Barriers of both CTAs initialised (published by the mbarrier-init fence)
+  // before any remote use.
+  cluster_arrive_relaxed();
+  cluster_wait();
   tc_fence_after();
+  // The producers' L2 cache policies (createpolicy is slow; its latency
+  // overlaps the wait for the previous grid).
+  uint64_t copy_policy = 0;
+  if ((warp == kProdAWarp || warp == kProdBWarp) && lane < 3)
+    copy_policy = (lane == 0) ? policy_evict_last() : policy_evict_normal();
+  // Each role waits for the previous grid (griddepcontrol.wait) only after
+  // its own setup, so the first pass through its code overlaps that wait.
   griddep_launch_dependents();
-  griddep_wait();  // global memory only after the previous grid completes
+  NVFP4DG_STAMP_NS(62);
   const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;
 
@@ -835,8 +902,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const bool tiles = (warp == kProdAWarp);
     const int nl = tiles ? 2 : 3;
     if (lane < nl) {
-      const uint64_t pol =
-          (lane == 0) ? policy_evict_last() : policy_evict_normal();
+      const uint64_t pol = copy_policy;
       const CUtensorMap* map =
           (lane == 0) ? &tmA : (rank == 0 ? &tmB1 : &tmB2);
       const uint8_t* sf_base =
@@ -853,7 +919,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       WorkIter it;
       work_begin(plan, unit, it);
       Work w;
-      while (ok && work_next(plan, it, w)) {
+      bool have = work_next(plan, it, w);
+      griddep_wait();  // global memory only after the previous grid
+      for (; ok && have; have = work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
         const int row = (lane == 0)
@@ -935,7 +1003,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     WorkIter it;
     work_begin(plan, unit, it);
     Work w;
-    while (ok && work_next(plan, it, w)) {
+    bool have = work_next(plan, it, w);
+    griddep_wait();  // global memory only after the previous grid
+    for (; ok && have; have = work_next(plan, it, w)) {
       const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got =
@@ -1020,7 +1090,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       WorkIter it;
       work_begin(plan, unit, it);
       Work w;
-      while (ok && work_next(plan, it, w)) {
+      bool have = work_next(plan, it, w);
+      griddep_wait();  // global memory only after the previous grid
+      for (; ok && have; have = work_next(plan, it, w)) {
         if (!mbar_wait_cluster(&acc_empty_bar, acc_phase ^ 1u, p.err,
                                kErrMma)) {
           ok = false;
@@ -1078,7 +1150,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     WorkIter it;
     work_begin(plan, unit, it);
     Work w;
-    while (work_next(plan, it, w)) {
+    bool have = work_next(plan, it, w);
+    griddep_wait();  // global memory only after the previous grid
+    for (; have; have = work_next(plan, it, w)) {
       const bool got =
           mbar_wait_cluster(&acc_full_bar, acc_phase, p.err, kErrEpilogue);
       if (!group_all<1>(got)) break;  // the four warps leave together
@@ -1174,6 +1248,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem, kTmemCols);
   }
+  NVFP4DG_STAMP_NS(63);
 }
 
 // ===========================================================================

@@ -10,7 +10,10 @@ prints the median per-CTA timeline in SM cycles::
 Columns: first MMA (cycles from the producer's first copy to the first MMA),
 period (cycles between consecutive K blocks at the MMA issuer), the MMA
 issuer's per-block issue time, the scale warps' store time, the time from the
-producer's empty-slot wait to the scales landing, and the epilogue's length.
+producer's empty-slot wait to the scales landing, and the epilogue's length;
+then, from global-timer stamps (ns), the spread of CTA start times, the
+prologue up to the dependency wait, a CTA's median life and the kernel's span
+from the first CTA's start to the last CTA's exit.
 The traced build is slower than the product build (every stamp is a global
 store); use it for where the cycles go, not for absolute speed.
 """
@@ -71,6 +74,28 @@ def summarise(buf: np.ndarray) -> dict:
             "epilogue", "kblocks"]
     out = {k: float(v) for k, v in zip(keys, med)}
     out["ctas"] = len(rows)
+    # global-timer stamps (ns) of every CTA: entry, past the dependency wait,
+    # exit
+    ent = buf[:, 5, 61]
+    ok = ent > 0
+    if ok.any():
+        ent, dep, ext = ent[ok], buf[ok, 5, 62], buf[ok, 5, 63]
+        out["ns_entry_skew"] = float(ent.max() - ent.min())
+        out["ns_prologue"] = float(np.median(dep - ent))
+        out["ns_cta_span"] = float(np.median(ext - ent))
+        out["ns_kernel_span"] = float(ext.max() - ent.min())
+        clk = buf[ok, 4, 63] - buf[ok, 4, 61]
+        out["sm_mhz"] = float(np.median(clk / np.maximum(ext - ent, 1)) * 1e3)
+        # SM cycles from entry to the first copy, and from the end of the
+        # epilogue (role 5 slot 0) to exit, of CTAs that ran an epilogue
+        first = buf[ok, 0, 0]
+        epi_end = buf[ok, 5, 0]
+        has = (first > 0) & (epi_end > 0)
+        if has.any():
+            out["cyc_entry_to_first_copy"] = float(
+                np.median(first[has] - buf[ok, 4, 61][has]))
+            out["cyc_epilogue_to_exit"] = float(
+                np.median(buf[ok, 4, 63][has] - epi_end[has]))
     return out
 
 
