@@ -256,19 +256,24 @@ def time_eager(step_fn, steps, warmup, world):
     return start.elapsed_time(end), clk.summary()
 
 
-def time_e2e(call, host_inputs, dev_inputs, c_dev, c_host, steps, world):
-    """Per step: pinned H2D of the inputs, the call, D2H of C; events around
-    all of it."""
-    stream = torch.cuda.current_stream()
-    h2d = sum(t.numel() * t.element_size() for t in host_inputs)
-    d2h = c_dev.numel() * c_dev.element_size()
-
+def copy_call_copy(call, host_inputs, dev_inputs, c_dev, c_host):
+    """One end-to-end step through a device-buffer API: pinned H2D of the
+    inputs, the call, D2H of C, one after another on the current stream."""
     def one():
         for h, d in zip(host_inputs, dev_inputs):
             d.copy_(h, non_blocking=True)
         call()
         c_host.copy_(c_dev, non_blocking=True)
+    return one
 
+
+def time_e2e(one, host_inputs, c_host, steps, world):
+    """Events around `steps` end-to-end steps (each uploads its inputs from
+    pinned host memory and downloads C); returns (ms, H2D and D2H bytes per
+    step)."""
+    stream = torch.cuda.current_stream()
+    h2d = sum(t.numel() * t.element_size() for t in host_inputs)
+    d2h = c_host.numel() * c_host.element_size()
     one()
     torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
@@ -360,14 +365,18 @@ def run_ours(args, world, rank):
         f"{peaks['source']} HBM copy GB/s; FP4 dense = 4 x {peaks['source']} "
         "bf16 cuBLAS TF/s")
 
-    # end to end through the public API with pinned host buffers
+    # end to end through the public host-buffer API: pinned host inputs and
+    # output, the library uploads, computes and downloads (slab-pipelined)
     d = sets[0]
     dev_in = [d[0], d[1], d[2], d[6], d[7], d[8]]
-    host_in = [t.cpu().pin_memory() for t in dev_in]
-    c_host = torch.empty(d[9].shape, dtype=torch.float16).pin_memory()
+    host_in = [t.cpu().view(torch.uint8).pin_memory() for t in dev_in]
+    c_host = torch.empty(d[9].shape[:2], dtype=torch.float16).pin_memory()
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
-    e2e_ms, h2d, d2h = time_e2e(lambda: dg.custom_kernel(d), host_in, dev_in,
-                                d[9], c_host, e2e_steps, world)
+
+    def e2e_step():
+        dg.dual_gemm_host(*host_in, c_host, flags=flags)
+
+    e2e_ms, h2d, d2h = time_e2e(e2e_step, host_in, c_host, e2e_steps, world)
     e2e_ms = max_over_ranks(e2e_ms, world)
     e2e_val = ranks_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
 
@@ -391,7 +400,8 @@ def run_ours(args, world, rank):
         "e2e": {"value": round(e2e_val, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "steps": e2e_steps,
-                "api": "nvfp4_dual_gemm_b200.custom_kernel (C ABI)"},
+                "api": "nvfp4_dual_gemm_b200.dual_gemm_host "
+                       "(C ABI nvfp4_dual_gemm_run_host)"},
         "gpu_launches": args.steps,
         "clocks": clocks,
     }
@@ -473,9 +483,11 @@ def run_reference(args, world, rank):
         c_host = torch.empty(d0[9].shape, dtype=torch.float16).pin_memory()
         e2e_steps = max(1, min(args.steps, args.e2e_steps))
         e2e_ms, h2d, d2h = time_e2e(
-            lambda: mod.cuda_nvfp4_dual_gemm(d0[0], d0[1], d0[2], d0[6],
-                                             d0[7], d0[8], d0[9]),
-            host_in, dev_in, d0[9], c_host, e2e_steps, 1)
+            copy_call_copy(
+                lambda: mod.cuda_nvfp4_dual_gemm(d0[0], d0[1], d0[2], d0[6],
+                                                 d0[7], d0[8], d0[9]),
+                host_in, dev_in, d0[9], c_host),
+            host_in, c_host, e2e_steps, 1)
         line.update({
             "value": round(tflops, 3), "ms_per_step": ms / args.steps,
             "us_per_call": round(ms * 1e3 / args.steps, 3),

@@ -199,6 +199,41 @@ NVFP4DG_API int nvfp4_dual_gemm_run_noalloc(
     const void* SFB1, const void* SFB2, void* C, int M, int N, int K, int L,
     unsigned flags, void* stream);
 
+/*
+ * Host-buffer entry point: A, B1, B2, SFA, SFB1, SFB2 and C are HOST buffers
+ * (page-locked for the copies to overlap; any alignment), with the sizes and
+ * layouts listed at the top of this file.  The library uploads the inputs
+ * into `staging`, a caller-owned device buffer of at least
+ * nvfp4_dual_gemm_host_staging_size(M, N, K, L) bytes (256-byte aligned),
+ * computes, and downloads C.  The weights go up in slabs of whole 128-row
+ * groups of B1/B2; each slab's kernel starts as soon as its slab has landed
+ * and each slab of C goes back while later slabs still go up, so the two
+ * directions of the host link and the kernels overlap.  Each copy costs a
+ * few microseconds beyond its bytes, so more slabs pay only when the
+ * download is long enough to hide behind the upload: `slabs` = 0 picks the
+ * count (1 to 16) from a model of the link; 1 runs upload, kernel and
+ * download back to back.  The copies run on two streams of the library's
+ * own, ordered after the work already queued on `stream`; `stream` waits for
+ * them, so host C is complete once `stream` is.  Calls on one `stream` may
+ * share a staging buffer.
+ *
+ * Replaces the reference's `custom_kernel(data)` (submission.py:1153-1157)
+ * for a caller whose tensors are in host memory: the reference's entry
+ * takes device tensors only (nvfp4_dual_gemm.cu:381-446), so such a caller
+ * copies every input up, calls it and copies C back, one after another.
+ */
+NVFP4DG_API size_t nvfp4_dual_gemm_host_staging_size(int M, int N, int K, int L);
+
+/* Slab count nvfp4_dual_gemm_run_host uses for M, N, K and a requested
+ * count (0 = automatic); 0 for invalid arguments.  Host-only. */
+NVFP4DG_API int nvfp4_dual_gemm_host_slabs(int M, int N, int K, int slabs);
+
+NVFP4DG_API int nvfp4_dual_gemm_run_host(
+    const void* A, const void* B1, const void* B2, const void* SFA,
+    const void* SFB1, const void* SFB2, void* C, int M, int N, int K, int L,
+    unsigned flags, int slabs, void* staging, size_t staging_bytes,
+    void* stream);
+
 /* Thread-local message describing the last failure ("" if none). */
 NVFP4DG_API const char* nvfp4_dual_gemm_last_error(void);
 

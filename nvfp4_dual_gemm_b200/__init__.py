@@ -8,7 +8,9 @@ from .api import (  # noqa: F401
     cuda_nvfp4_dual_gemm,
     custom_kernel,
     dual_gemm,
+    dual_gemm_host,
     generate_input,
+    host_staging_size,
     plan,
     plan_work,
     quantize_nvfp4,
@@ -26,6 +28,7 @@ from ._lib import (  # noqa: F401
     FLAG_BN128,
     FLAG_FORCE_STREAMK,
     FLAG_NO_PAIR,
+    FLAG_NO_PDL,
     FLAG_NO_SPLITK,
     FLAG_NO_STREAMK,
     FLAG_PAIR,
@@ -34,4 +37,4 @@ from ._lib import (  # noqa: F401
     NativeLibraryError,
 )
 
-__version__ = "1.0.0"
+__version__ = "1.1.0"

@@ -35,6 +35,9 @@ FLAG_SPLITK = 1 << 20
 FLAG_NO_SPLITK = 1 << 21
 FLAG_NO_PDL = 1 << 22
 
+# Most weight slabs nvfp4_dual_gemm_run_host uses.
+MAX_HOST_SLABS = 16
+
 # Size of the static scratch behind nvfp4_dual_gemm_run_noalloc.
 NOALLOC_SCRATCH_BYTES = 4 << 20
 
@@ -56,6 +59,10 @@ SIGNATURES = {
     "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip,
                                   _ip, _ip]),
     "nvfp4_dual_gemm_plan_work": (_i, [_i, _i, _i, _u, _i, _i, _ip, _i]),
+    "nvfp4_dual_gemm_host_staging_size": (_sz, [_i, _i, _i, _i]),
+    "nvfp4_dual_gemm_host_slabs": (_i, [_i, _i, _i, _i]),
+    "nvfp4_dual_gemm_run_host": (_i, [_vp] * 7 + [_i, _i, _i, _i, _u, _i, _vp,
+                                                  _sz, _vp]),
     "nvfp4_dual_gemm_last_error": (ctypes.c_char_p, []),
     "nvfp4_dual_gemm_version": (_i, []),
 }

@@ -29,6 +29,8 @@ __all__ = [
     "custom_kernel",
     "cuda_nvfp4_dual_gemm",
     "dual_gemm",
+    "dual_gemm_host",
+    "host_staging_size",
     "quantize_nvfp4",
     "generate_input",
     "workspace_size",
@@ -44,14 +46,16 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
-def _check_bytes(name: str, t: torch.Tensor) -> None:
+def _check_bytes(name: str, t: torch.Tensor, cuda: bool = True) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
     if t.element_size() != 1:
         raise ValueError(f"{name} must hold 1-byte elements "
                          f"(fp4x2 / fp8 / uint8), got {t.dtype}")
-    if not t.is_cuda:
-        raise ValueError(f"{name} must be a CUDA tensor")
+    placed = t.is_cuda if cuda else t.device.type == "cpu"
+    if not placed:
+        raise ValueError(f"{name} must be a {'CUDA' if cuda else 'CPU'} "
+                         "tensor")
 
 
 def _rows_dense(name: str, t: torch.Tensor, rows: int, row_bytes: int) -> None:
@@ -73,8 +77,9 @@ def _blocked_bytes(rows: int, k: int) -> int:
     return ((rows + 127) // 128) * (k // 64) * 512
 
 
-def _check_blocked(name: str, t: torch.Tensor, rows: int, k: int) -> None:
-    _check_bytes(name, t)
+def _check_blocked(name: str, t: torch.Tensor, rows: int, k: int,
+                   cuda: bool = True) -> None:
+    _check_bytes(name, t, cuda)
     need = _blocked_bytes(rows, k)
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
@@ -83,16 +88,11 @@ def _check_blocked(name: str, t: torch.Tensor, rows: int, k: int) -> None:
                          f"needs {need}")
 
 
-def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
-              workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """C = silu(A B1^T) * (A B2^T) on the current stream; returns C.
-
-    ``flags`` are the NVFP4DG_FLAG_* bits of the C ABI (0 = automatic).  With
-    ``workspace`` (a zero-initialised uint8 CUDA tensor of at least
-    :func:`workspace_size` bytes) the caller owns the split-K scratch;
-    otherwise the library keeps one per (device, stream)."""
+def _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda: bool):
+    """Shape, dtype and placement checks shared by both entry points;
+    returns (M, N, K)."""
     for name, t in (("A", A), ("B1", B1), ("B2", B2)):
-        _check_bytes(name, t)
+        _check_bytes(name, t, cuda)
     M = A.size(0)
     N = B1.size(0)
     K = 2 * A.size(1) if A.dim() >= 2 else 0
@@ -103,15 +103,29 @@ def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
         raise ValueError(f"N = {N} must be a multiple of 64")
     if K % 256 != 0:
         raise ValueError(f"K = {K} must be a multiple of 256")
-    _check_blocked("SFA", SFA, M, K)
-    _check_blocked("SFB1", SFB1, N, K)
-    _check_blocked("SFB2", SFB2, N, K)
+    _check_blocked("SFA", SFA, M, K, cuda)
+    _check_blocked("SFB1", SFB1, N, K, cuda)
+    _check_blocked("SFB2", SFB2, N, K, cuda)
     if C.dtype != torch.float16:
         raise ValueError(f"C must be float16, got {C.dtype}")
-    if not C.is_cuda or not C.is_contiguous():
-        raise ValueError("C must be a contiguous CUDA tensor")
+    where = "CUDA" if cuda else "CPU"
+    placed = C.is_cuda if cuda else C.device.type == "cpu"
+    if not placed or not C.is_contiguous():
+        raise ValueError(f"C must be a contiguous {where} tensor")
     if C.numel() != M * N or C.size(0) != M:
         raise ValueError(f"C has shape {tuple(C.shape)}, expected [{M}, {N}(, 1)]")
+    return M, N, K
+
+
+def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """C = silu(A B1^T) * (A B2^T) on the current stream; returns C.
+
+    ``flags`` are the NVFP4DG_FLAG_* bits of the C ABI (0 = automatic).  With
+    ``workspace`` (a zero-initialised uint8 CUDA tensor of at least
+    :func:`workspace_size` bytes) the caller owns the split-K scratch;
+    otherwise the library keeps one per (device, stream)."""
+    M, N, K = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=True)
     dev = C.device
     for name, t in (("A", A), ("B1", B1), ("B2", B2), ("SFA", SFA),
                     ("SFB1", SFB1), ("SFB2", SFB2)):
@@ -133,6 +147,63 @@ def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
                 _ptr(C), M, N, K, 1, flags, _ptr(workspace),
                 workspace.numel() * workspace.element_size(), stream)
     _lib.check(rc, "nvfp4_dual_gemm_run")
+    return C
+
+
+def host_staging_size(M: int, N: int, K: int) -> int:
+    """Bytes of device staging :func:`dual_gemm_host` needs (host-only)."""
+    lib = _lib.load()
+    n = lib.nvfp4_dual_gemm_host_staging_size(M, N, K, 1)
+    msg = _lib.last_error()
+    if n == 0 and msg:
+        raise ValueError(msg)
+    return int(n)
+
+
+# Staging buffers dual_gemm_host keeps per (device, stream): calls on one
+# stream are ordered, so they may share one.
+_staging: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def dual_gemm_host(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
+                   slabs: int = 0, device: torch.device | int | None = None,
+                   staging: torch.Tensor | None = None) -> torch.Tensor:
+    """The same product with every tensor in HOST memory (page-locked, e.g.
+    ``tensor.pin_memory()``, for the copies to overlap).
+
+    Uploads the inputs to ``device`` (default: the current CUDA device),
+    computes and downloads C, overlapping the weight upload, the kernels and
+    the download slab by slab (``nvfp4_dual_gemm_run_host``).  Work is queued
+    on the device's current stream; C is complete once that stream is
+    (``torch.cuda.current_stream(device).synchronize()``).  ``staging``, a
+    uint8 CUDA tensor of at least :func:`host_staging_size` bytes, is the
+    device buffer the inputs go through; by default the library keeps one per
+    (device, stream)."""
+    M, N, K = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=False)
+    dev = torch.device("cuda", torch.cuda.current_device()
+                       if device is None else torch.device(device).index or 0)
+    lib = _lib.load()
+    need = host_staging_size(M, N, K)
+    with torch.cuda.device(dev):
+        stream = _stream(dev)
+        if staging is None:
+            key = (dev.index, stream)
+            buf = _staging.get(key)
+            if buf is None or buf.numel() < need:
+                buf = torch.empty(max(need, 1), dtype=torch.uint8,
+                                  device=dev)
+                _staging[key] = buf
+        else:
+            if (not staging.is_cuda or staging.device != dev or
+                    not staging.is_contiguous()):
+                raise ValueError("staging must be a contiguous CUDA tensor on "
+                                 f"{dev}")
+            buf = staging
+        rc = lib.nvfp4_dual_gemm_run_host(
+            _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
+            _ptr(C), M, N, K, 1, flags, slabs, _ptr(buf),
+            buf.numel() * buf.element_size(), stream)
+    _lib.check(rc, "nvfp4_dual_gemm_run_host")
     return C
 
 

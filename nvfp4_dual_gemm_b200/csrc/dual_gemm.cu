@@ -59,6 +59,8 @@ struct Cfg {
   static_assert(kSfTmemBase + kStages * kSfTmemPerStage <= kTmemCols,
                 "TMEM budget");
   static_assert(2 * BN <= kSfTmemBase, "accumulator must fit below scales");
+  static_assert(kStages * kStageBytes >= 4 * 32768,
+                "stream-K fixup staging reuses the stage buffers");
 };
 
 struct KParams {
@@ -187,30 +189,26 @@ __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
   }
 }
 
-__device__ __forceinline__ void store_f32x32(float* dst, const float (&v)[32]) {
-  float4* d = reinterpret_cast<float4*>(dst);
+// Stream-K partials: within a slot, 16-byte group g (4 consecutive columns;
+// GEMM1 columns are groups [0, BN/4), GEMM2 columns [BN/4, BN/2)) of row r
+// sits at float offset (g * 128 + r) * 4, so each warp store or load covers
+// 512 contiguous bytes.  This writes the 32 columns of groups [g0, g0 + 8)
+// of one row.
+__device__ __forceinline__ void store_f32x32_t(float* slot, int g0, int row,
+                                               const float (&v)[32]) {
+  float4* d = reinterpret_cast<float4*>(slot);
 #pragma unroll
   for (int q = 0; q < 8; ++q)
-    __stcg(d + q, make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2],
-                              v[4 * q + 3]));
-}
-
-__device__ __forceinline__ void add_f32x32(float (&v)[32], const float* src) {
-  const float4* s = reinterpret_cast<const float4*>(src);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float4 t = __ldcg(s + q);
-    v[4 * q] += t.x;
-    v[4 * q + 1] += t.y;
-    v[4 * q + 2] += t.z;
-    v[4 * q + 3] += t.w;
-  }
+    __stcg(d + (size_t)(g0 + q) * 128 + row,
+           make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
 }
 
 // Warp roles (352 threads, one CTA per SM):
 //   warps 0-3   epilogue (warp w reads TMEM lanes 32w..32w+31 = tile rows)
-//   warp 4      producer A: A tile (TMA) + the three scale runs (bulk copies)
-//   warp 5      producer B: B1 and B2 tiles (TMA)
+//   warp 4      tile producer: lanes 0-2 issue the A, B1 and B2 tiles (TMA)
+//               of a K block as one instruction
+//   warp 5      scale producer: lanes 0-2 issue the three scale runs (bulk
+//               copies) as one instruction, onto their own barrier
 //   warp 6      TMEM owner and MMA issuer (one elected thread)
 //   warps 7-10  scale warps, one per TMEM sub-partition (warp % 4)
 // Per K block the scale warps read the 512-byte scale atoms from shared
@@ -219,12 +217,11 @@ __device__ __forceinline__ void add_f32x32(float (&v)[32], const float* src) {
 // lane 32q+i, column c of a 4-column group holds the 4 scales of row
 // i + 32c for that 64-wide K step — the row of the 128x4 atom.  Writing the
 // scales from four warps keeps the MMA thread's instruction stream down to
-// the four MMAs of the K block: every tcgen05 instruction costs one issuing
-// thread ~50-70 cycles, so moving the twelve scale copies per K block off
-// the MMA thread (as tcgen05.cp issued by the MMA thread would require) is
-// what lets the tensor pipe run at its own rate.  It also lets the B-operand
-// scales of a 64-row tile (half an atom) sit next to each other, so both
-// GEMMs always run as one MMA with N = 2 * BN over the stacked B1|B2 tile.
+// the four MMAs of the K block: every tcgen05 instruction costs its issuing
+// thread ~50-70 cycles, and the K-block period is set by such single-thread
+// instruction chains.  It also lets the B-operand scales of a 64-row tile
+// (half an atom) sit next to each other, so both GEMMs always run as one MMA
+// with N = 2 * BN over the stacked B1|B2 tile.
 constexpr int kEpiWarps = 4;
 constexpr int kProdAWarp = 4;
 constexpr int kProdBWarp = 5;
@@ -232,6 +229,100 @@ constexpr int kMmaWarp = 6;
 constexpr int kSfWarp0 = 7;
 constexpr int kSfWarps = 4;
 static_assert(kThreads == 32 * (kSfWarp0 + kSfWarps), "thread count");
+
+// Owner side of a stream-K tile (the 128 epilogue threads, thread = row):
+// adds the partials of the other contributors to this CTA's accumulator and
+// writes C.  Called on the CTA's last item after its accumulator is complete,
+// so the pipeline's stage buffers (`stage`, >= kFixSlots * 32 KB) are idle:
+// the partials are staged through them by bulk copies, kFixSlots items of
+// 32 KB (one contributor's 32 columns of both GEMMs for the 128 rows) in
+// flight, instead of being loaded row by row by the threads themselves.
+// `slot_ptr(b)` is contributor b's partial slot; `arrive_empty()` releases
+// the accumulator after its last TMEM load.  Partials are added in
+// contributor order, so the result does not depend on timing.
+constexpr int kFixSlots = 4;
+constexpr uint32_t kFixItemBytes = 32768;
+
+template <int BN, typename SlotPtr, typename ArriveEmpty>
+__device__ __forceinline__ void sk_owner_fixup(
+    uint8_t* stage, uint64_t* fix_bar, int b_first, int b_last,
+    SlotPtr slot_ptr, ArriveEmpty arrive_empty, uint32_t t_row, int row,
+    bool row_ok, __half* crow, unsigned* err) {
+  const int nb = b_last - b_first;
+  const int n_items = (BN / 32) * nb;
+  uint64_t pol = 0;
+  int issued = 0;  // thread 0: items whose copies have been issued
+  auto issue = [&](int i) {
+    ++issued;
+    const int c = i / nb;
+    const float* src = slot_ptr(b_first + 1 + i % nb);
+    uint8_t* dst = stage + (i % kFixSlots) * kFixItemBytes;
+    uint64_t* bar = &fix_bar[i % kFixSlots];
+    mbar_arrive_expect_tx(bar, kFixItemBytes);
+    bulk_load(dst, src + (size_t)(8 * c) * 128 * 4, kFixItemBytes / 2, bar,
+              pol);
+    bulk_load(dst + kFixItemBytes / 2,
+              src + (size_t)(BN / 4 + 8 * c) * 128 * 4, kFixItemBytes / 2,
+              bar, pol);
+  };
+  if (threadIdx.x == 0) {
+    NVFP4DG_STAMP(4, 40);
+    // the partials were acquired through the counter (generic proxy); the
+    // copies read them through the async proxy
+    fence_proxy_async_global();
+    pol = policy_evict_first();
+    for (int i = 0; i < n_items && i < kFixSlots; ++i) issue(i);
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN / 32; ++c) {
+    float x[32], y[32];
+    __syncwarp();
+    tc_ld_32cols(t_row + 32 * c, x);
+    tc_ld_32cols(t_row + BN + 32 * c, y);
+    tc_wait_ld();
+    if (c == BN / 32 - 1) arrive_empty();
+#pragma unroll 1
+    for (int j = 0; j < nb; ++j) {
+      const int i = c * nb + j;
+      // after a timeout every later wait returns at once (err is set); the
+      // threads still meet at each barrier below
+      mbar_wait(&fix_bar[i % kFixSlots], (i / kFixSlots) & 1, err,
+                kErrEpilogue);
+      if (threadIdx.x == 0 && i < 16) NVFP4DG_STAMP(5, 41 + i);
+      const float4* sx = reinterpret_cast<const float4*>(
+                             stage + (i % kFixSlots) * kFixItemBytes) +
+                         row;
+      const float4* sy = sx + kFixItemBytes / 2 / 16;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 a = sx[q * 128];
+        const float4 b = sy[q * 128];
+        x[4 * q] += a.x;
+        x[4 * q + 1] += a.y;
+        x[4 * q + 2] += a.z;
+        x[4 * q + 3] += a.w;
+        y[4 * q] += b.x;
+        y[4 * q + 1] += b.y;
+        y[4 * q + 2] += b.z;
+        y[4 * q + 3] += b.w;
+      }
+      epi_bar();  // every thread is done with the slot
+      if (threadIdx.x == 0 && i + kFixSlots < n_items) {
+        fence_proxy_async_smem();  // generic reads before the async refill
+        issue(i + kFixSlots);
+      }
+    }
+    if (row_ok) store_row32(crow + 32 * c, x, y);
+    if (threadIdx.x == 0) NVFP4DG_STAMP(4, 41 + c);
+  }
+  // After a timeout, copies may still be in flight: let them land (bounded)
+  // before the CTA can exit.
+  if (threadIdx.x == 0 && *reinterpret_cast<volatile unsigned*>(err) != 0u) {
+    for (int i = issued > kFixSlots ? issued - kFixSlots : 0; i < issued; ++i)
+      mbar_wait(&fix_bar[i % kFixSlots], (i / kFixSlots) & 1, err, kErrDrain,
+                /*bail_on_err=*/false);
+  }
+}
 
 // 256-thread barrier (id 3) of the split-K epilogue (epilogue warps 0-3 and
 // scale warps 7-10) that also ANDs a predicate.
@@ -393,10 +484,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_empty_bar;
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ __align__(8) uint64_t ready_bar;  // split-K: peer may write
+  __shared__ __align__(8) uint64_t fix_bar[kFixSlots];  // stream-K owner
   // split-K: the peer's partials of chunk j of this CTA's half landed
   __shared__ __align__(8) uint64_t recv_bar[BN / 32];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int finisher_sh;
 
   // Operand tiles use the 128-byte swizzle, whose pattern repeats every
   // 1024 bytes: align the ring to 1024 in the shared window.
@@ -419,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&acc_empty_bar, 32 * kEpiWarps);
     mbar_init(&drain_bar, 1);
     mbar_init(&ready_bar, 1);
+    for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
     for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -720,54 +812,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (row_ok) store_row32(crow + 32 * c, x, y);
         }
       } else {
-        float* mine = p.partials + (size_t)w.slot * partial_slot_floats(plan) +
-                      (size_t)row * 2 * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float x[32], y[32];
-          __syncwarp();
-          tc_ld_32cols(t_row + 32 * c, x);
-          tc_ld_32cols(t_row + BN + 32 * c, y);
-          tc_wait_ld();
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            mbar_arrive(&acc_empty_bar);
-          }
-          store_f32x32(mine + 32 * c, x);
-          store_f32x32(mine + BN + 32 * c, y);
-        }
-        __threadfence();
-        epi_bar();
+        // A stream-K tile shared by CTAs b_first..b_last.  Its first K
+        // blocks are b_first's last item, the later ones the others' first
+        // items, so when b_first gets here the others have normally already
+        // published their partials: it waits for their count, adds them to
+        // its own accumulator and writes C; the others store a partial and
+        // count it.
         const long long ts = w.tile - plan.dp_tiles;
         int b_first, b_last;
         sk_tile_owners(plan, ts, &b_first, &b_last);
-        if (threadIdx.x == 0) {
-          const int old = atomicAdd(&p.counters[ts], 1);
-          const int last = (old == b_last - b_first) ? 1 : 0;
-          if (last) p.counters[ts] = 0;  // ready for the next launch
-          finisher_sh = last;
-        }
-        epi_bar();
-        if (finisher_sh) {
-          __threadfence();
+        int* counter = p.counters + ts;
+        if (static_cast<int>(blockIdx.x) != b_first) {
+          float* mine =
+              p.partials + (size_t)w.slot * partial_slot_floats(plan);
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             float x[32], y[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              x[i] = 0.f;
-              y[i] = 0.f;
+            __syncwarp();
+            tc_ld_32cols(t_row + 32 * c, x);
+            tc_ld_32cols(t_row + BN + 32 * c, y);
+            tc_wait_ld();
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              mbar_arrive(&acc_empty_bar);
             }
-            for (int b = b_first; b <= b_last; ++b) {
-              const float* src = p.partials +
-                                 (size_t)sk_slot(plan, b, ts) *
-                                     partial_slot_floats(plan) +
-                                 (size_t)row * 2 * BN;
-              add_f32x32(x, src + 32 * c);
-              add_f32x32(y, src + BN + 32 * c);
-            }
-            if (row_ok) store_row32(crow + 32 * c, x, y);
+            store_f32x32_t(mine, 8 * c, row, x);
+            store_f32x32_t(mine, BN / 4 + 8 * c, row, y);
           }
+          __threadfence();
+          epi_bar();
+          if (threadIdx.x == 0) red_release_add(counter, 1);
+        } else {
+          bool ready = true;
+          if (threadIdx.x == 0) {
+            NVFP4DG_STAMP(5, 40);
+            ready = wait_count(counter, b_last - b_first, p.err, kErrEpilogue);
+            if (ready) *counter = 0;  // ready for the next launch
+          }
+          if (!group_all<1>(ready)) break;
+          sk_owner_fixup<BN>(
+              smem, fix_bar, b_first, b_last,
+              [&](int b) {
+                return p.partials +
+                       (size_t)sk_slot(plan, b, ts) * partial_slot_floats(plan);
+              },
+              [&] {
+                tc_fence_before();
+                mbar_arrive(&acc_empty_bar);
+              },
+              t_row, row, row_ok, crow, p.err);
         }
       }
       if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit);
@@ -819,6 +912,8 @@ struct PairCfg {
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
   static_assert(kSfBase + kStages * kSfTmemPerStage <= kTmemCols,
                 "TMEM budget");
+  static_assert(kStages * kStageBytes >= 4 * 32768,
+                "stream-K fixup staging reuses the stage buffers");
 };
 
 template <int BN>
@@ -839,8 +934,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_full_bar;
   __shared__ __align__(8) uint64_t acc_empty_bar;  // even CTA: both drained
   __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ __align__(8) uint64_t fix_bar[kFixSlots];  // stream-K owner
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int finisher_sh;
 
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -865,6 +960,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(&acc_full_bar, 1);
     mbar_init(&acc_empty_bar, 2 * kEpiWarps);
     mbar_init(&drain_bar, 1);
+    for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
     fence_mbar_init();
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
@@ -1179,59 +1275,57 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           if (row_ok) store_row32(crow + 32 * c, x, y);
         }
       } else {
-        float* mine = p.partials +
-                      (size_t)cta_slot(plan, w.slot, rank) *
-                          partial_slot_floats(plan) +
-                      (size_t)row * 2 * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float x[32], y[32];
-          __syncwarp();
-          tc_ld_32cols(t_row + 32 * c, x);
-          tc_ld_32cols(t_row + BN + 32 * c, y);
-          tc_wait_ld();
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc_empty_c);
-          }
-          store_f32x32(mine + 32 * c, x);
-          store_f32x32(mine + BN + 32 * c, y);
-        }
-        __threadfence();
-        epi_bar();
+        // Stream-K tile shared by units b_first..b_last: as in the 1-SM
+        // kernel, unit b_first (for which these are its last K blocks) adds
+        // the others' partials to its accumulator; each CTA of a pair deals
+        // with its own 128 rows and its own counter.
         const long long ts = w.tile - plan.dp_tiles;
         int b_first, b_last;
         sk_tile_owners(plan, ts, &b_first, &b_last);
         int* counter = p.counters + ts * plan.ctas + rank;
-        if (threadIdx.x == 0) {
-          const int old = atomicAdd(counter, 1);
-          const int last = (old == b_last - b_first) ? 1 : 0;
-          if (last) *counter = 0;  // ready for the next launch
-          finisher_sh = last;
-        }
-        epi_bar();
-        if (finisher_sh) {
-          __threadfence();
+        if (unit != b_first) {
+          float* mine = p.partials +
+                        (size_t)cta_slot(plan, w.slot, rank) *
+                            partial_slot_floats(plan);
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             float x[32], y[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              x[i] = 0.f;
-              y[i] = 0.f;
+            __syncwarp();
+            tc_ld_32cols(t_row + 32 * c, x);
+            tc_ld_32cols(t_row + BN + 32 * c, y);
+            tc_wait_ld();
+            if (c == BN / 32 - 1) {
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive_cluster(acc_empty_c);
             }
-            for (int b = b_first; b <= b_last; ++b) {
-              const float* src =
-                  p.partials +
-                  (size_t)cta_slot(plan, sk_slot(plan, b, ts), rank) *
-                      partial_slot_floats(plan) +
-                  (size_t)row * 2 * BN;
-              add_f32x32(x, src + 32 * c);
-              add_f32x32(y, src + BN + 32 * c);
-            }
-            if (row_ok) store_row32(crow + 32 * c, x, y);
+            store_f32x32_t(mine, 8 * c, row, x);
+            store_f32x32_t(mine, BN / 4 + 8 * c, row, y);
           }
+          __threadfence();
+          epi_bar();
+          if (threadIdx.x == 0) red_release_add(counter, 1);
+        } else {
+          bool ready = true;
+          if (threadIdx.x == 0) {
+            NVFP4DG_STAMP(5, 40);
+            ready = wait_count(counter, b_last - b_first, p.err, kErrEpilogue);
+            if (ready) *counter = 0;  // ready for the next launch
+          }
+          if (!group_all<1>(ready)) break;
+          sk_owner_fixup<BN>(
+              smem, fix_bar, b_first, b_last,
+              [&](int b) {
+                return p.partials +
+                       (size_t)cta_slot(plan, sk_slot(plan, b, ts), rank) *
+                           partial_slot_floats(plan);
+              },
+              [&] {
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+              },
+              t_row, row, row_ok, crow, p.err);
         }
       }
       if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit_i);
@@ -1506,32 +1600,54 @@ bool split_fits(int M, int N, int K, int bn, int sms) {
   return 2 * tiles <= sms;
 }
 
-// Estimated SM cycles of the busiest work unit.  The K-block period is set
-// by the issuing threads' instruction chains (about 700 cycles for either
-// tile width, measured); the epilogue of a tile costs ~34 cycles per output
-// column; a stream-K partial is written and read back at the ~7.5 B/cycle
-// that the row-per-thread partial layout achieves.
+// Estimated SM cycles of the busiest work unit, from pipeline traces on B200
+// (nvfp4_dual_gemm_b200.trace): the K-block period is set by the
+// issuing threads' instruction chains (~700 cycles for N = 128 MMAs, ~710
+// for 2-SM N = 256, ~790 for single-CTA N = 256); the first stage lands
+// ~2300 cycles after start; an epilogue costs ~2100 / ~3900 cycles for
+// BN = 64 / 128 (overlapped with the next tile's main loop except for a
+// CTA's last tile); teardown ~500 cycles, ~2100 for 2-SM pairs.  Cluster
+// split-K: a later first stage (~3200), ~830-cycle blocks (BN = 128), a
+// ~5100-cycle exchange-and-combine epilogue (BN = 128; about half for 64)
+// and ~1600 cycles of teardown.  Stream-K pays for its owners' partial
+// fixups (below).
 double plan_cost(const Plan& p) {
-  const double per_block = (p.bn == 128) ? 720.0 : 700.0;
-  const double epi = 34.0 * p.bn;
-  const double slot_bytes = 128.0 * 2 * p.bn * 4;
-  if (p.split == 2) {
-    const double xchg = 128.0 * p.bn * 4 / 32.0;  // DSMEM exchange
-    return ((p.kblocks + 1) / 2) * per_block + xchg + epi / 2 + 2000.0;
-  }
-  double cost = 0;
+  const bool pair = (p.ctas == 2);
+  const double per_block = pair ? (p.bn == 128 ? 710.0 : 700.0)
+                                : (p.bn == 128 ? 790.0 : 715.0);
+  const double epi = (p.bn == 128) ? 3900.0 : 2100.0;
+  const double tear = pair ? 2100.0 : 500.0;
+  const double start = 2300.0;
+  if (p.split == 2)
+    return 3200.0 + ((p.kblocks + 1) / 2) * (p.bn == 128 ? 830.0 : 715.0) +
+           (p.bn == 128 ? 5100.0 : 2800.0) + 1600.0;
+  double cost = start + tear;
+  double tiles = 0;
   if (p.dp_tiles > 0) {
-    const double tiles = (double)((p.dp_tiles + p.grid - 1) / p.grid);
-    cost += tiles * (p.kblocks * per_block + epi);
+    tiles = (double)((p.dp_tiles + p.grid - 1) / p.grid);
+    cost += tiles * p.kblocks * per_block;
   }
   if (p.sk_iters > 0) {
     const double per_unit = (double)((p.sk_iters + p.grid - 1) / p.grid);
     const bool split = (p.sk_iters % p.grid) != 0 ||
                        ((p.sk_iters / p.grid) % p.kblocks) != 0;
-    cost += per_unit * per_block + epi * 2;
-    if (split) cost += 2.5 * slot_bytes / 7.5;
+    cost += per_unit * per_block;
+    tiles += 2;
+    if (split) {
+      // The tile's owner stages the other contributors' partials through
+      // shared memory, 32 KB per (contributor, 32-column chunk): ~3600
+      // cycles to the first, then ~1250 (1-SM) / ~1800 (pair) per item
+      // with every SM doing the same (measured); ~1500 more for the last
+      // contributor's partial store.
+      const double others =
+          std::ceil((p.kblocks - 1) / per_unit);  // contributors - 1
+      const double items = others * (p.bn / 32);
+      cost += 1500.0 + 3600.0 + (items - 1.0) * (pair ? 1800.0 : 1250.0);
+    }
   }
-  return cost + 2000.0;
+  // one exposed epilogue, the others mostly hidden behind the next tile
+  cost += epi + (tiles > 1 ? (tiles - 1) * 0.3 * epi : 0.0);
+  return cost;
 }
 
 Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
@@ -1579,11 +1695,24 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
     const int cap = std::max(1, (forced > 0 ? forced : sms) / ctas);
     for (int i = 0; i < nb; ++i) {
       for (int sk = force_sk ? 1 : 0; sk < (streamk ? 2 : 1); ++sk) {
-        Plan p = plan_for(M, N, K, bns[i], ctas, cap, sk == 1, force_sk);
-        const double cost = plan_cost(p);
-        if (cost < best_cost) {
-          best_cost = cost;
-          best = p;
+        // Stream-K over fewer tiles than units may also run on a smaller
+        // grid: fewer contributors per tile, cheaper fixups.
+        int caps[6];
+        int ncap = 0;
+        caps[ncap++] = cap;
+        if (sk == 1 && forced == 0) {
+          const long long tiles =
+              (long long)((M + kBM * ctas - 1) / (kBM * ctas)) * (N / bns[i]);
+          for (int f : {2, 3, 4, 6, 8})
+            if (tiles * f < cap) caps[ncap++] = static_cast<int>(tiles * f);
+        }
+        for (int j = 0; j < ncap; ++j) {
+          Plan p = plan_for(M, N, K, bns[i], ctas, caps[j], sk == 1, force_sk);
+          const double cost = plan_cost(p);
+          if (cost < best_cost) {
+            best_cost = cost;
+            best = p;
+          }
         }
       }
     }
@@ -1593,7 +1722,8 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
 
 int check_problem(const void* A, const void* B1, const void* B2,
                   const void* SFA, const void* SFB1, const void* SFB2,
-                  const void* C, int M, int N, int K, int L, unsigned flags) {
+                  const void* C, int M, int N, int K, int L, unsigned flags,
+                  bool device_ptrs = true) {
   if (M < 0 || N < 0 || K < 0)
     return fail(NVFP4DG_ERR_INVALID, "M, N, K must be non-negative");
   if (L != 1)
@@ -1624,7 +1754,7 @@ int check_problem(const void* A, const void* B1, const void* B2,
     if (K == 0 && i < 6) continue;
     if (ptrs[i] == nullptr)
       return fail(NVFP4DG_ERR_INVALID, std::string(names[i]) + " is NULL");
-    if (reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
+    if (device_ptrs && reinterpret_cast<uintptr_t>(ptrs[i]) % 16 != 0)
       return fail(NVFP4DG_ERR_ALIGN,
                   std::string(names[i]) + " is not 16-byte aligned");
   }
@@ -1820,6 +1950,254 @@ int noalloc_scratch(int devid, void** out) {
   return NVFP4DG_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Host-buffer pipeline.  The weights are uploaded in slabs of whole 128-row
+// groups of B1/B2 (a slab of the blocked scales is then a contiguous run of
+// atoms), each slab's kernel starts as soon as its slab has landed, and each
+// slab of C goes back to the host while the next slabs upload: the upload
+// (host -> device), the kernels and the download (device -> host, the other
+// direction of the link) overlap instead of running back to back.
+// ---------------------------------------------------------------------------
+constexpr int kMaxSlabs = 16;
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+size_t blocked_bytes(int rows, int K) {
+  return static_cast<size_t>((rows + 127) / 128) * (K / 64) * 512;
+}
+
+// Device staging buffer: full-size copies of the six inputs, then C stored
+// slab by slab (slab j as a dense [M, w_j] block at M * n0_j halves).
+struct Staging {
+  size_t a, sfa, b1, b2, sfb1, sfb2, c, total;
+};
+
+Staging staging_layout(int M, int N, int K) {
+  Staging s;
+  size_t off = 0;
+  s.a = off;
+  off += align256(static_cast<size_t>(M) * (K / 2));
+  s.sfa = off;
+  off += align256(blocked_bytes(M, K));
+  s.b1 = off;
+  off += align256(static_cast<size_t>(N) * (K / 2));
+  s.b2 = off;
+  off += align256(static_cast<size_t>(N) * (K / 2));
+  s.sfb1 = off;
+  off += align256(blocked_bytes(N, K));
+  s.sfb2 = off;
+  off += align256(blocked_bytes(N, K));
+  s.c = off;
+  off += align256(static_cast<size_t>(M) * N * sizeof(__half));
+  s.total = off;
+  return s;
+}
+
+// Rows per slab for `req` slabs, rounded up to whole 128-row groups.
+int slab_rows_for(int N, int req) {
+  const int groups = (N + 127) / 128;
+  const int s = std::max(1, std::min({req, kMaxSlabs, groups}));
+  return (groups + s - 1) / s * 128;
+}
+
+// Modelled time (us) of the host-buffer pipeline with `rows`-row slabs,
+// fitted to B200 measurements over PCIe 5: ~54 GB/s up and ~57 GB/s down,
+// the two directions overlapping; ~5 us per copy that back-to-back copies do
+// not hide (issuing them from more streams does not help); ~12 ns per row
+// when a slab of C is a strided (2-D) copy.  Upload of A and its scales,
+// then per slab 4 uploads (B1, B2 and their scales); each slab's kernel
+// (~4 PFLOP/s plus a 6 us floor) after its uploads; each slab of C
+// downloaded after its kernel, behind the previous download.
+double host_pipeline_us(int M, int N, int K, int rows) {
+  const double bw_up = 54e3, bw_down = 57e3;  // bytes per us
+  const double per_copy = 5.0, per_row_2d = 0.012;
+  const double a_bytes = (double)M * (K / 2) + (double)blocked_bytes(M, K);
+  double up = a_bytes / bw_up + 2 * per_copy;
+  double down = 0;
+  for (int n0 = 0; n0 < N; n0 += rows) {
+    const int w = std::min(rows, N - n0);
+    const double b_bytes = 2.0 * w * (K / 2) + 2.0 * blocked_bytes(w, K);
+    up += b_bytes / bw_up + 4 * per_copy;
+    const double kernel = 6.0 + 4.0 * M * (double)w * K / 4e9;
+    down = std::max(down, up + kernel) + (double)M * w * 2 / bw_down +
+           per_copy + (w < N ? per_row_2d * M : 0.0);
+  }
+  return down;
+}
+
+// Slab rows: `req` slabs when given, else the count with the least modelled
+// time, preferring fewer slabs unless more save at least 2 %.
+int host_slab_rows(int M, int N, int K, int req) {
+  const int groups = (N + 127) / 128;
+  if (groups == 0) return 128;
+  if (req > 0) return slab_rows_for(N, req);
+  int best = slab_rows_for(N, 1);
+  double best_t = host_pipeline_us(M, N, K, best);
+  for (int s = 2; s <= std::min(kMaxSlabs, groups); ++s) {
+    const int rows = slab_rows_for(N, s);
+    const double t = host_pipeline_us(M, N, K, rows);
+    if (t < 0.98 * best_t) {
+      best = rows;
+      best_t = t;
+    }
+  }
+  return best;
+}
+
+struct HostPipe {
+  cudaStream_t up = nullptr;    // host -> device copies
+  cudaStream_t down = nullptr;  // device -> host copies
+  cudaEvent_t start = nullptr, up_done = nullptr, down_done = nullptr;
+  cudaEvent_t landed[kMaxSlabs] = {};
+  cudaEvent_t computed[kMaxSlabs] = {};
+};
+std::map<int, HostPipe> g_pipe;
+std::mutex g_pipe_mu;
+
+int host_pipe(int devid, HostPipe** out) {
+  HostPipe& p = g_pipe[devid];
+  if (p.up == nullptr) {
+    cudaError_t e;
+    const unsigned ev = cudaEventDisableTiming;
+    if ((e = cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking)) ||
+        (e = cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking)) ||
+        (e = cudaEventCreateWithFlags(&p.start, ev)) ||
+        (e = cudaEventCreateWithFlags(&p.up_done, ev)) ||
+        (e = cudaEventCreateWithFlags(&p.down_done, ev)))
+      return cuda_fail(e, "creating the host-pipeline streams");
+    for (int j = 0; j < kMaxSlabs; ++j)
+      if ((e = cudaEventCreateWithFlags(&p.landed[j], ev)) ||
+          (e = cudaEventCreateWithFlags(&p.computed[j], ev)))
+        return cuda_fail(e, "creating the host-pipeline events");
+  }
+  *out = &p;
+  return NVFP4DG_OK;
+}
+
+int copy_up(void* dst, const void* src, size_t bytes, cudaStream_t s) {
+  if (bytes == 0) return NVFP4DG_OK;
+  cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, s);
+  return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "upload");
+}
+
+int run_host_impl(const void* A, const void* B1, const void* B2,
+                  const void* SFA, const void* SFB1, const void* SFB2, void* C,
+                  int M, int N, int K, int L, unsigned flags, int slabs,
+                  void* staging, size_t staging_bytes, void* stream_ptr) {
+  g_last_error.clear();
+  if (slabs < 0 || slabs > kMaxSlabs)
+    return fail(NVFP4DG_ERR_INVALID,
+                "slabs must be 0 (automatic) to " + std::to_string(kMaxSlabs));
+  // Host buffers need no alignment (the copies take any address).
+  int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags,
+                         false);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return NVFP4DG_OK;
+  const Staging lay = staging_layout(M, N, K);
+  if (staging == nullptr || staging_bytes < lay.total)
+    return fail(NVFP4DG_ERR_WORKSPACE,
+                "staging buffer of " + std::to_string(lay.total) +
+                    " bytes required, got " + std::to_string(staging_bytes));
+  if (reinterpret_cast<uintptr_t>(staging) % 256 != 0)
+    return fail(NVFP4DG_ERR_ALIGN, "staging buffer is not 256-byte aligned");
+  const int rows = host_slab_rows(M, N, K, slabs);
+  const int nslab = (N + rows - 1) / rows;
+  // Every slab's schedule must exist before anything is enqueued.
+  if (K > 0) {
+    int devid = 0;
+    cudaError_t e = cudaGetDevice(&devid);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DevInfo* dev = nullptr;
+    {
+      std::lock_guard<std::mutex> lock(g_mu);
+      if ((rc = device_info(devid, &dev))) return rc;
+    }
+    for (int j = 0; j < nslab; ++j) {
+      const int w = std::min(rows, N - j * rows);
+      if (choose_plan(M, w, K, flags, dev->sms).grid == 0)
+        return fail(NVFP4DG_ERR_UNSUPPORTED,
+                    "cluster split-K needs 2 x tiles <= SMs and K >= 512 "
+                    "(slab of " + std::to_string(w) + " columns)");
+    }
+  }
+  std::lock_guard<std::mutex> lock(g_pipe_mu);
+  int devid = 0;
+  cudaError_t e = cudaGetDevice(&devid);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  HostPipe* pp = nullptr;
+  if ((rc = host_pipe(devid, &pp))) return rc;
+  HostPipe& p = *pp;
+  cudaStream_t s0 = static_cast<cudaStream_t>(stream_ptr);
+  uint8_t* st = static_cast<uint8_t*>(staging);
+  const size_t row_b = static_cast<size_t>(K) / 2;
+  const size_t atom_row = static_cast<size_t>(K / 64) * 512;  // per 128 rows
+  // Uploads start once everything before this call on the caller's stream
+  // (an earlier call still reading the staging buffer) is done.
+  if ((e = cudaEventRecord(p.start, s0)) ||
+      (e = cudaStreamWaitEvent(p.up, p.start, 0)))
+    return cuda_fail(e, "ordering the upload stream");
+  rc = copy_up(st + lay.a, A, M * row_b, p.up);
+  if (!rc) rc = copy_up(st + lay.sfa, SFA, blocked_bytes(M, K), p.up);
+  for (int j = 0; j < nslab && !rc; ++j) {
+    const size_t n0 = static_cast<size_t>(j) * rows;
+    const size_t n1 = std::min<size_t>(N, n0 + rows);
+    rc = copy_up(st + lay.b1 + n0 * row_b, static_cast<const uint8_t*>(B1) +
+                 n0 * row_b, (n1 - n0) * row_b, p.up);
+    if (!rc)
+      rc = copy_up(st + lay.b2 + n0 * row_b,
+                   static_cast<const uint8_t*>(B2) + n0 * row_b,
+                   (n1 - n0) * row_b, p.up);
+    const size_t g0 = n0 / 128, g1 = (n1 + 127) / 128;
+    if (!rc)
+      rc = copy_up(st + lay.sfb1 + g0 * atom_row,
+                   static_cast<const uint8_t*>(SFB1) + g0 * atom_row,
+                   (g1 - g0) * atom_row, p.up);
+    if (!rc)
+      rc = copy_up(st + lay.sfb2 + g0 * atom_row,
+                   static_cast<const uint8_t*>(SFB2) + g0 * atom_row,
+                   (g1 - g0) * atom_row, p.up);
+    if (!rc && (e = cudaEventRecord(p.landed[j], p.up)))
+      rc = cuda_fail(e, "recording an upload event");
+  }
+  // Kernels on the caller's stream, one per slab, each after its slab lands;
+  // downloads on their own stream, each after its slab's kernel.
+  for (int j = 0; j < nslab && !rc; ++j) {
+    const size_t n0 = static_cast<size_t>(j) * rows;
+    const int w = std::min(rows, N - j * rows);
+    if ((e = cudaStreamWaitEvent(s0, p.landed[j], 0))) {
+      rc = cuda_fail(e, "waiting for an upload");
+      break;
+    }
+    __half* cs = reinterpret_cast<__half*>(st + lay.c) + n0 * M;
+    rc = run_impl(st + lay.a, st + lay.b1 + n0 * row_b, st + lay.b2 + n0 * row_b,
+                  st + lay.sfa, st + lay.sfb1 + (n0 / 128) * atom_row,
+                  st + lay.sfb2 + (n0 / 128) * atom_row, cs, M, w, K, 1, flags,
+                  nullptr, 0, true, s0);
+    if (rc) break;
+    if ((e = cudaEventRecord(p.computed[j], s0)) ||
+        (e = cudaStreamWaitEvent(p.down, p.computed[j], 0))) {
+      rc = cuda_fail(e, "ordering the download stream");
+      break;
+    }
+    const size_t pitch = static_cast<size_t>(N) * sizeof(__half);
+    const size_t width = static_cast<size_t>(w) * sizeof(__half);
+    if ((e = cudaMemcpy2DAsync(static_cast<uint8_t*>(C) + n0 * sizeof(__half),
+                               pitch, cs, width, width, M,
+                               cudaMemcpyDeviceToHost, p.down))) {
+      rc = cuda_fail(e, "download");
+      break;
+    }
+  }
+  // The caller's stream completes only after both copy streams have, also
+  // when an error stopped the loop part-way.
+  cudaError_t e1 = cudaEventRecord(p.up_done, p.up);
+  if (!e1) e1 = cudaEventRecord(p.down_done, p.down);
+  if (!e1) e1 = cudaStreamWaitEvent(s0, p.up_done, 0);
+  if (!e1) e1 = cudaStreamWaitEvent(s0, p.down_done, 0);
+  if (e1 && !rc) rc = cuda_fail(e1, "joining the copy streams");
+  return rc;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1833,6 +2211,31 @@ int nvfp4_dual_gemm_run(const void* A, const void* B1, const void* B2,
                         void* stream) {
   return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, nullptr, 0,
                   true, stream);
+}
+
+size_t nvfp4_dual_gemm_host_staging_size(int M, int N, int K, int L) {
+  g_last_error.clear();
+  if (M < 0 || N < 0 || K < 0 || L != 1 || N % 64 != 0 || K % 256 != 0) {
+    fail(NVFP4DG_ERR_INVALID, "invalid problem shape");
+    return 0;
+  }
+  if (M == 0 || N == 0) return 0;
+  return staging_layout(M, N, K).total;
+}
+
+int nvfp4_dual_gemm_host_slabs(int M, int N, int K, int slabs) {
+  if (M < 0 || N <= 0 || K < 0 || slabs < 0 || slabs > kMaxSlabs) return 0;
+  const int rows = host_slab_rows(M, N, K, slabs);
+  return (N + rows - 1) / rows;
+}
+
+int nvfp4_dual_gemm_run_host(const void* A, const void* B1, const void* B2,
+                             const void* SFA, const void* SFB1,
+                             const void* SFB2, void* C, int M, int N, int K,
+                             int L, unsigned flags, int slabs, void* staging,
+                             size_t staging_bytes, void* stream) {
+  return run_host_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, slabs,
+                       staging, staging_bytes, stream);
 }
 
 int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void* B2,
@@ -2028,6 +2431,6 @@ NVFP4DG_API int nvfp4_dual_gemm_trace_read(void* host, size_t bytes) {
 }
 #endif
 
-int nvfp4_dual_gemm_version(void) { return 100; }
+int nvfp4_dual_gemm_version(void) { return 101; }
 
 }  // extern "C"

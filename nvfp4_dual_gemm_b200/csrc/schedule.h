@@ -10,11 +10,14 @@
 //   2. stream-K (SK) tiles: the remaining tiles' iterations, laid end to end,
 //      are cut into `grid` equal contiguous ranges, CTA b taking
 //      [lo(b), lo(b+1)), lo(b) = b * sk_iters / grid.
-// A tile whose iterations span several CTAs is finished by whichever of them
-// arrives last: every segment writes its fp32 partial accumulator to a
-// workspace slot, bumps the tile's counter, and the CTA that brings the
-// counter to the segment count sums all partials in a fixed order and runs
-// the SiLU epilogue.  No CTA ever waits for another one.
+// A tile whose iterations span CTAs b_first..b_last is finished by b_first,
+// which holds the tile's first K blocks as the LAST item of its range, while
+// for every other contributor its segment is the FIRST item of its range:
+// those write their fp32 partial accumulators to workspace slots and bump the
+// tile's counter; b_first waits (bounded) for the count, adds the partials to
+// its own accumulator in a fixed order and runs the SiLU epilogue.  Waits
+// only go from a CTA's last item to other CTAs' first items, so none can
+// wait on a CTA that waits, and in practice the partials are already there.
 #pragma once
 
 #include <cstdint>

@@ -36,6 +36,12 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Orders this thread's earlier (generic-proxy) view of global memory before
+// its later bulk copies (async proxy) that read it.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .b64 st;\n\t"
@@ -104,6 +110,35 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         atomicOr(err, code);
         return false;
       }
+    }
+  }
+}
+
+// GPU-scope release add and acquire load of a 32-bit counter in global
+// memory (stream-K tile counters).
+__device__ __forceinline__ void red_release_add(int* ptr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v)
+               : "memory");
+}
+__device__ __forceinline__ int ld_acquire(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ptr)
+               : "memory");
+  return v;
+}
+
+// Wait until the counter at `ptr` reaches `target`, bounded like mbar_wait.
+__device__ __forceinline__ bool wait_count(const int* ptr, int target,
+                                           unsigned* err, unsigned code) {
+  if (ld_acquire(ptr) == target) return true;
+  const long long t0 = clock_cycles();
+  for (;;) {
+    __nanosleep(32);
+    if (ld_acquire(ptr) == target) return true;
+    if (*reinterpret_cast<volatile unsigned*>(err) != 0u) return false;
+    if (clock_cycles() - t0 > kWaitLimitCycles) {
+      atomicOr(err, code);
+      return false;
     }
   }
 }

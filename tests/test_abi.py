@@ -29,7 +29,7 @@ def test_library_loads_and_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
     assert set(_lib.SIGNATURES) == set(names)
-    assert lib.nvfp4_dual_gemm_version() == 100
+    assert lib.nvfp4_dual_gemm_version() == 101
 
 
 def test_invalid_arguments_rejected_without_gpu():
@@ -201,3 +201,147 @@ def test_cluster_split_k_choice_and_limits():
         rc = lib.nvfp4_dual_gemm_run(ptr, ptr, ptr, ptr, ptr, ptr, ptr, 256,
                                      512, 2048, 1, dg.FLAG_SPLITK | bad, None)
         assert rc == _lib.ERR_INVALID and "SPLITK" in _lib.last_error()
+
+
+def _blocked(rows, k):
+    return ((rows + 127) // 128) * (k // 64) * 512
+
+
+def _align(x):
+    return (x + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 7168), (200, 320, 512),
+                                   (4096, 14336, 4096), (1, 64, 256)])
+def test_host_staging_size_holds_every_buffer(m, n, k):
+    want = (_align(m * k // 2) + _align(_blocked(m, k)) + 2 * _align(n * k // 2)
+            + 2 * _align(_blocked(n, k)) + _align(m * n * 2))
+    assert dg.host_staging_size(m, n, k) == want
+
+
+def test_host_slab_counts():
+    lib = _lib.load()
+    slabs = lib.nvfp4_dual_gemm_host_slabs
+    # automatic: one slab (upload, kernel, download back to back) when C is
+    # small next to the weights, several when its download is long enough
+    # to hide behind the upload
+    assert slabs(256, 4096, 7168, 0) == 1
+    assert slabs(128, 7168, 2048, 0) == 1
+    assert 3 <= slabs(4096, 14336, 4096, 0) <= 6
+    assert 2 <= slabs(1024, 7168, 4096, 0) <= 6
+    # requested counts, rounded to whole 128-row groups
+    assert slabs(64, 320, 512, 2) == 2    # 256 + 64 rows
+    assert slabs(64, 320, 512, 3) == 3
+    assert slabs(64, 320, 512, 16) == 3
+    assert slabs(64, 1024, 512, 3) == 3   # 384 + 384 + 256
+    assert slabs(64, 1024, 512, 17) == 0
+    assert slabs(64, 0, 512, 1) == 0
+
+
+def test_host_entry_rejects_bad_arguments_without_gpu():
+    lib = _lib.load()
+    h = ctypes.c_void_p(8)  # host buffers may have any alignment
+    m, n, k = 256, 512, 1024
+    need = lib.nvfp4_dual_gemm_host_staging_size(m, n, k, 1)
+    st = ctypes.c_void_p(1 << 20)
+
+    def run(*, m=m, n=n, k=k, slabs=0, staging=st, nbytes=need, a=h):
+        return lib.nvfp4_dual_gemm_run_host(a, h, h, h, h, h, h, m, n, k, 1, 0,
+                                            slabs, staging, nbytes, None)
+
+    assert run(n=100) == _lib.ERR_INVALID
+    assert run(k=100) == _lib.ERR_INVALID
+    assert run(slabs=17) == _lib.ERR_INVALID
+    assert run(slabs=-1) == _lib.ERR_INVALID
+    assert run(a=None) == _lib.ERR_INVALID and "NULL" in _lib.last_error()
+    assert run(staging=None) == _lib.ERR_WORKSPACE
+    assert run(nbytes=need - 1) == _lib.ERR_WORKSPACE
+    assert run(staging=ctypes.c_void_p((1 << 20) + 16)) == _lib.ERR_ALIGN
+    assert run(m=0, staging=None, nbytes=0) == _lib.OK
+    assert lib.nvfp4_dual_gemm_host_staging_size(m, 100, k, 1) == 0
+    with pytest.raises(ValueError):
+        dg.host_staging_size(m, 100, k)
+
+
+def test_host_api_checks_placement():
+    import torch
+    m, n, k = 128, 128, 256
+    a = torch.zeros(m, k // 2, dtype=torch.uint8)
+    b = torch.zeros(n, k // 2, dtype=torch.uint8)
+    sfa = torch.zeros(_blocked(m, k), dtype=torch.uint8)
+    sfb = torch.zeros(_blocked(n, k), dtype=torch.uint8)
+    c = torch.zeros(m, n, dtype=torch.float16)
+    with pytest.raises(ValueError, match="CPU tensor"):
+        dg.dual_gemm_host(a, b, b, sfa, sfb, sfb, c.to("meta"))
+    with pytest.raises(ValueError, match="multiple of 64"):
+        dg.dual_gemm_host(a, b[:100], b[:100], sfa, sfb, sfb, c)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        dg.dual_gemm(a, b, b, sfa, sfb, sfb, c)
+
+
+SK_CASES = [
+    (m, n, k, f)
+    for (m, n, k) in [(256, 3072, 4096), (512, 3072, 7168), (1024, 7168, 4096),
+                      (4096, 14336, 4096), (384, 1024, 2048), (7168, 384, 2304),
+                      (200, 192, 768), (2048, 2048, 2048)]
+    for f in (0, _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR,
+              _lib.FLAG_FORCE_STREAMK | _lib.FLAG_PAIR,
+              _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN64 | _lib.FLAG_NO_PAIR,
+              13 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR)
+]
+
+
+@pytest.mark.parametrize("m,n,k,flags", SK_CASES)
+def test_stream_k_waits_cannot_cycle(m, n, k, flags):
+    """The CTA (unit) holding a stream-K tile's first K blocks finishes the
+    tile after waiting for the other contributors' partials.  That wait ends
+    only if (a) the owner's segment is the owner's last item, (b) every other
+    contributor's segment is its first stream-K item (computed before any
+    wait of its own), and (c) all units are resident at once."""
+    p = dg.plan(m, n, k, flags)
+    if p["sk_tiles"] == 0:
+        return
+    assert p["grid"] * p["ctas"] <= 148
+    kblocks = k // 256
+    segs = defaultdict(list)
+    for u in range(p["grid"]):
+        recs = dg.plan_work(m, n, k, u, flags)
+        sk = [r for r in recs if r[0] >= p["dp_tiles"]]
+        for i, (tile, kb0, kb1, slot) in enumerate(sk):
+            segs[tile].append((u, kb0, kb1, i == 0, i == len(sk) - 1, slot))
+    for tile, ss in segs.items():
+        ss.sort()
+        if len(ss) == 1:
+            assert ss[0][1:3] == (0, kblocks) and ss[0][5] == -1
+            continue
+        owner = ss[0]
+        assert owner[1] == 0 and owner[4], (tile, ss)       # (a)
+        for u, kb0, kb1, first, last, slot in ss[1:]:
+            assert first and slot >= 0, (tile, ss)           # (b)
+        # the segments tile the K range in unit order
+        assert [s[1] for s in ss[1:]] == [s[2] for s in ss[:-1]]
+        assert ss[-1][2] == kblocks
+
+
+@pytest.mark.parametrize("flags", [
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN128,
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN64,
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_PAIR | _lib.FLAG_BN128,
+])
+def test_many_contributor_plans(flags):
+    # the plans the GPU test of many stream-K contributors per tile relies on
+    m, n, k = 256, 512, 7168
+    pl = dg.plan(m, n, k, flags)
+    assert pl["grid"] * pl["ctas"] == 148 and pl["dp_tiles"] == 0
+    per_tile = defaultdict(int)
+    for u in range(pl["grid"]):
+        for tile, kb0, kb1, slot in dg.plan_work(m, n, k, u, flags):
+            per_tile[tile] += 1
+    assert min(per_tile.values()) >= 9, dict(per_tile)
+
+
+def test_stream_k_small_grid_search():
+    # whole-problem stream-K may pick a grid smaller than the SM count
+    flags = _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN128
+    pl = dg.plan(256, 512, 7168, flags)
+    assert pl["sk_tiles"] == 8 and pl["grid"] < 148

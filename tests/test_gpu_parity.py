@@ -17,6 +17,15 @@ from tests.helpers import assert_close, data_tuple, to_device
 pytestmark = pytest.mark.gpu
 
 
+# Stream-K over all 148 SMs (the grid forced), so that each tile of
+# 256 x 512 x 7168 has 9 to 19 contributors.
+MANY_CONTRIBUTOR_FLAGS = [
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN128,
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN64,
+    148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_PAIR | _lib.FLAG_BN128,
+]
+
+
 def run(p, flags=0, use_custom_kernel=False):
     d = to_device(p)
     if use_custom_kernel:
@@ -88,9 +97,22 @@ def test_pair_stream_k_forced_grid(streamk_problem, grid, bn):
     assert_close(run(p, grid | flag), ref, f"pair grid={grid} bn={bn}")
 
 
+@pytest.mark.parametrize("flags", MANY_CONTRIBUTOR_FLAGS)
+def test_stream_k_many_contributors_per_tile(flags):
+    # A long K split over every SM: each tile's owner adds the partials of
+    # many other CTAs, more than its staging ring holds at once (the plan
+    # itself is checked on the CPU in test_abi.py).
+    m, n, k = 256, 512, 7168
+    p = O.make_problem(m, n, k, seed=77)
+    ref = O.reference_output(p)
+    for _ in range(2):
+        assert_close(run(p, flags | _lib.FLAG_SYNC_CHECK), ref,
+                     f"many contributors {flags:#x}")
+
+
 def test_stream_k_repeated_calls_reuse_counters(streamk_problem):
-    # The finishing CTA resets each tile counter, so back-to-back launches on
-    # the same workspace must all be correct.
+    # Each tile's owner resets its counter, so back-to-back launches on the
+    # same workspace must all be correct.
     p, ref = streamk_problem
     d = to_device(p)
     for _ in range(3):
@@ -315,3 +337,28 @@ def test_device_error_word_clean_after_runs():
     rc = _lib.load().nvfp4_dual_gemm_device_status(0, ctypes.byref(w))
     assert rc == 0 and w.value == 0
     del word
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_slices_equal_full_product(world):
+    """N-sharding through views (nvfp4_dual_gemm_b200.shard): the column
+    slices computed from each rank's B rows and blocked-scale byte range
+    equal the full product bit for bit under one whole-tile schedule."""
+    from nvfp4_dual_gemm_b200 import shard
+    m, n, k = 256, 128 * world * 2, 1024
+    p = O.make_problem(m, n, k, seed=50 + world)
+    d = to_device(p)
+    flags = (_lib.FLAG_BN128 | _lib.FLAG_NO_PAIR | _lib.FLAG_NO_STREAMK |
+             _lib.FLAG_NO_SPLITK)
+    full = torch.empty(m, n, dtype=torch.float16, device="cuda")
+    dg.dual_gemm(d["a"], d["b1"], d["b2"], d["sfa_blocked"],
+                 d["sfb1_blocked"], d["sfb2_blocked"], full, flags=flags)
+    parts = []
+    for r in range(world):
+        spec = shard.shard_spec(n, k, world, r)
+        parts.append(shard.sharded_dual_gemm(
+            spec, d["a"], d["b1"], d["b2"], d["sfa_blocked"],
+            d["sfb1_blocked"], d["sfb2_blocked"], flags=flags))
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts, dim=1), full)
+    assert_close(full.cpu().numpy(), O.reference_output(p), "full")
