@@ -79,6 +79,11 @@ extern "C" {
                                            grid in the stream finishes, and
                                            waits for it before touching global
                                            memory)                            */
+#define NVFP4DG_FLAG_NO_MERGED_B (1u << 23) /* copy B1 and B2 tiles with
+                                              separate copies (by default one
+                                              copy brings both when B2 lies
+                                              above B1 at a multiple of 16
+                                              bytes)                          */
 
 /*
  * Run the dual GEMM on `stream` using a workspace the library keeps per

@@ -34,6 +34,7 @@ FLAG_NO_PAIR = 1 << 19
 FLAG_SPLITK = 1 << 20
 FLAG_NO_SPLITK = 1 << 21
 FLAG_NO_PDL = 1 << 22
+FLAG_NO_MERGED_B = 1 << 23
 
 # Most weight slabs nvfp4_dual_gemm_run_host uses.
 MAX_HOST_SLABS = 16

@@ -73,6 +73,9 @@ struct KParams {
   float* partials;
   int* counters;
   unsigned* err;
+  // 1-SM kernel: tmB1 is a 3-D map whose third coordinate selects B1 (0) or
+  // B2 (1), so one copy brings both tiles of a K block (see b_pair_map)
+  int b_merged;
 };
 
 __device__ unsigned g_err_word;
@@ -92,7 +95,7 @@ static __device__ __align__(256) unsigned char
 // unit the epilogue's accumulator-ready (4) and done (5) times.
 #ifdef NVFP4DG_TRACE
 constexpr int kTraceSlots = 64;
-constexpr int kTraceRoles = 8;
+constexpr int kTraceRoles = 10;
 constexpr int kTraceCtas = 160;
 __device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
 #define NVFP4DG_STAMP(role, idx)                                   \
@@ -270,7 +273,7 @@ __device__ __forceinline__ void sk_owner_fixup(
     // the partials were acquired through the counter (generic proxy); the
     // copies read them through the async proxy
     fence_proxy_async_global();
-    pol = policy_evict_first();
+    pol = kPolicyEvictFirst;
     for (int i = 0; i < n_items && i < kFixSlots; ++i) issue(i);
   }
 #pragma unroll 1
@@ -501,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      // the tile producer (with the tiles' bytes) and the scale warps
-      mbar_init(&full_bar[s], 1 + kSfWarps);
-      mbar_init(&sfdata_bar[s], 1);        // the scale-run producer
+      // the scale warps; the first one's arrival carries the tiles' bytes
+      mbar_init(&full_bar[s], kSfWarps);
+      mbar_init(&sfdata_bar[s], 1);        // one arming arrival
       mbar_init(&empty_bar[s], 1);         // tcgen05.commit of the MMAs
     }
     mbar_init(&acc_full_bar, 1);
@@ -513,6 +516,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
     for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
     fence_mbar_init();
+    // arm the first scale fill of every stage (bytes may land before or
+    // after an arming: a barrier's transaction count may go negative
+    // meanwhile)
+    for (int s = 0; s < S; ++s)
+      mbar_arrive_expect_tx(&sfdata_bar[s], kBytesSf);
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB1);
@@ -524,17 +532,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 32 * kProdAWarp) NVFP4DG_STAMP(1, 60);
   // Split-K clusters: every thread arrives on the cluster barrier once the
   // barriers are initialised; the epilogue waits on it before its first
   // remote operation, the other warps at teardown.
   if (plan.split == 2) cluster_arrive_relaxed();
   // Whether this thread has waited on that arrival (warp-uniform).
   bool cluster_waited = false;
-  // The producers' L2 cache policies (createpolicy is slow; its latency
-  // overlaps the wait for the previous grid).
-  uint64_t copy_policy = 0;
-  if ((warp == kProdAWarp || warp == kProdBWarp) && lane < 3)
-    copy_policy = (lane == 0) ? policy_evict_last() : policy_evict_normal();
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -547,26 +551,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
     // ------------------------------------------------------------ producers
-    // Warp 4 copies the operand tiles, warp 5 the scale runs.  In each, lanes
-    // 0-2 issue their three copies as one instruction (lane 0: A / SFA,
-    // lane 1: B1 / SFB1, lane 2: B2 / SFB2): an issuing thread's chain of
-    // dependent instructions per K block, not the bytes, bounds the copy
-    // rate of an SM.  The scale runs land on their own barrier so the scale
-    // warps can move them into TMEM while the tiles are in flight.
-    const bool tiles = (warp == kProdAWarp);
-    if (lane < 3) {
-      const uint64_t pol = copy_policy;
-      const CUtensorMap* map = (lane == 0) ? &tmA : (lane == 1 ? &tmB1 : &tmB2);
-      const uint8_t* sf_base =
-          (lane == 0) ? p.sfa : (lane == 1 ? p.sfb1 : p.sfb2);
-      uint64_t* bars = tiles ? full_bar : sfdata_bar;
-      const uint32_t tx = tiles ? kBytesA + kBytesB : kBytesSf;
-      const uint32_t dst_off =
-          tiles ? (lane == 0 ? 0u
-                             : static_cast<uint32_t>(Cf::kABytes +
-                                                     (lane - 1) * Cf::kBBytes))
-                : static_cast<uint32_t>(Cf::kABytes + 2 * Cf::kBBytes +
-                                        lane * kSfRunBytes);
+    // Lane 0 of warp 4 copies the A scale run and the A tile, lane 0 of
+    // warp 5 the two B scale runs and the B tiles (one copy for B1 and B2
+    // with the pair map).  A thread issues its copy instructions one at a
+    // time (~100 cycles each, measured) while separate warps issue side by
+    // side, so a K block's copies are split between two warps.  The
+    // producers only copy; the expected bytes come from elsewhere: the first
+    // scale warp's arrival on a stage's tile barrier carries the tiles'
+    // bytes, and the same warp re-arms the stage's scale barrier for the
+    // next fill once it has seen this one (the kernel's start arms the first
+    // fills).  Keeping these off the MMA thread matters: its per-K-block
+    // chain of waits and tcgen05 instructions sets the pace.  Scale runs go
+    // first and land on their own barrier, so the scale warps move them into
+    // TMEM while the tiles are in flight.
+    if (lane == 0) {
+      const bool a_side = (warp == kProdAWarp);
+      // A is read by every CTA of its row of tiles: keep it in L2 longer
+      const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -575,32 +576,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       work_begin(plan, blockIdx.x, it);
       Work w;
       bool have = work_next(plan, it, w);
+      if (a_side) NVFP4DG_STAMP(1, 61);
       griddep_wait();  // global memory only after the previous grid
+      if (a_side) NVFP4DG_STAMP(1, 62);
       for (; ok && have; have = work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
-        const int row = (lane == 0) ? m_tile * kBM : n_tile * BN;
-        const int blk = (lane == 0) ? m_tile : (n_tile * BN) / 128;
-        const uint8_t* sf_src =
-            sf_base + (size_t)blk * kblk64 * kSfAtomBytes;
+        const uint8_t* sfa_src =
+            p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
+        const size_t sfb_off =
+            (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
+          if (a_side) NVFP4DG_STAMP(9, issued);
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
             ok = false;
             break;
           }
+          if (a_side) NVFP4DG_STAMP(0, issued);
           uint8_t* st = smem + stage * Cf::kStageBytes;
-          if (lane == 0) {
-            if (tiles) NVFP4DG_STAMP(0, issued);
-            mbar_arrive_expect_tx(&bars[stage], tx);
+          uint8_t* sf_dst = st + Cf::kABytes + 2 * Cf::kBBytes;
+          const size_t run = (size_t)kb * kSfRunBytes;
+          if (a_side) {
+            bulk_load(sf_dst, sfa_src + run, kSfRunBytes, &sfdata_bar[stage],
+                      pol);
+            bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
+                      kSfRunBytes, &sfdata_bar[stage], pol);
+            tma_load_3d(st, &tmA, &full_bar[stage], kb * kRowBytes,
+                        m_tile * kBM, 0, pol);
+          } else {
+            bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
+                      kSfRunBytes, &sfdata_bar[stage], pol);
+            tma_load_3d(st + Cf::kABytes, &tmB1, &full_bar[stage],
+                        kb * kRowBytes, n_tile * BN, 0, pol);
+            if (!p.b_merged)
+              tma_load_3d(st + Cf::kABytes + Cf::kBBytes, &tmB2,
+                          &full_bar[stage], kb * kRowBytes, n_tile * BN, 0,
+                          pol);
           }
-          __syncwarp(0x7u);
-          if (tiles)
-            tma_load_2d(st + dst_off, map, &bars[stage], kb * kRowBytes, row,
-                        pol);
-          else
-            bulk_load(st + dst_off, sf_src + (size_t)kb * kSfRunBytes,
-                      kSfRunBytes, &bars[stage], pol);
-          if (tiles && lane == 0) NVFP4DG_STAMP(1, issued);
+          if (a_side) NVFP4DG_STAMP(1, issued);
           ++issued;
           if (++stage == S) {
             stage = 0;
@@ -609,12 +622,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Never leave with copies in flight: wait (bounded) until every stage
-      // has completed the fill that holds this warp's last copies.
+      // has completed the fill that holds this thread's last copies.
       for (int s = 0; s < S; ++s) {
         if (issued > s) {
-          const long long fill = (issued - 1 - s) / S;
-          mbar_wait(&bars[s], static_cast<uint32_t>(fill & 1), p.err,
-                    kErrDrain, /*bail_on_err=*/false);
+          const uint32_t par =
+              static_cast<uint32_t>(((issued - 1 - s) / S) & 1);
+          mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain,
+                    /*bail_on_err=*/false);
+          mbar_wait(&full_bar[s], par, p.err, kErrDrain,
+                    /*bail_on_err=*/false);
         }
       }
     }
@@ -643,7 +659,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(6, done);
+        if (warp == kSfWarp0 && lane == 0) {
+          NVFP4DG_STAMP(6, done);
+          // arm the stage's next scale fill; it cannot complete before all
+          // four scale warps have passed this fill (the copies wait for the
+          // MMAs, which wait for every scale warp)
+          mbar_arrive_expect_tx(&sfdata_bar[stage], kBytesSf);
+        }
         const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
                                        Cf::kABytes + 2 * Cf::kBBytes) +
                               16u * lane;
@@ -693,7 +715,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_bar[stage]);
+        if (lane == 0) {
+          // the first scale warp's arrival also expects the tiles' bytes
+          if (warp == kSfWarp0)
+            mbar_arrive_expect_tx(&full_bar[stage], kBytesA + kBytesB);
+          else
+            mbar_arrive(&full_bar[stage]);
+        }
         if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
         ++done;
         if (++stage == S) {
@@ -950,10 +978,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
-      // even CTA's producer A (with both CTAs' tile bytes) + the scale
-      // warps of both CTAs
-      mbar_init(&full_bar[s], 1 + 2 * kSfWarps);
-      mbar_init(&sfdata_bar[s], 1);         // own producer A
+      // the scale warps of both CTAs; on the even CTA the first one's
+      // arrival carries both CTAs' tile bytes
+      mbar_init(&full_bar[s], 2 * kSfWarps);
+      mbar_init(&sfdata_bar[s], 1);         // one arming arrival
       // even CTA: the MMA commit; odd CTA: the even producer A's forward
       mbar_init(&empty_bar[s], 1);
     }
@@ -962,6 +990,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(&drain_bar, 1);
     for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
     fence_mbar_init();
+    // arm the first scale fill of every stage
+    for (int s = 0; s < S; ++s)
+      mbar_arrive_expect_tx(&sfdata_bar[s], 3 * kSfRunBytes);
     fence_proxy_async_smem();
     prefetch_tmap(&tmA);
     prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
@@ -977,11 +1008,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_arrive_relaxed();
   cluster_wait();
   tc_fence_after();
-  // The producers' L2 cache policies (createpolicy is slow; its latency
-  // overlaps the wait for the previous grid).
-  uint64_t copy_policy = 0;
-  if ((warp == kProdAWarp || warp == kProdBWarp) && lane < 3)
-    copy_policy = (lane == 0) ? policy_evict_last() : policy_evict_normal();
   // Each role waits for the previous grid (griddepcontrol.wait) only after
   // its own setup, so the first pass through its code overlaps that wait.
   griddep_launch_dependents();
@@ -991,23 +1017,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
     // ------------------------------------------------------------ producers
-    // Warp 4 copies the operand tiles (lane 0: this CTA's A rows, lane 1:
-    // its B half, as one instruction) with their bytes counted on the even
-    // CTA's `full` barrier; warp 5 copies this CTA's three scale runs
-    // (lanes 0-2, one instruction) onto its own `sfdata` barrier.
-    const bool tiles = (warp == kProdAWarp);
-    const int nl = tiles ? 2 : 3;
-    if (lane < nl) {
-      const uint64_t pol = copy_policy;
-      const CUtensorMap* map =
-          (lane == 0) ? &tmA : (rank == 0 ? &tmB1 : &tmB2);
-      const uint8_t* sf_base =
-          (lane == 0) ? p.sfa : (lane == 1 ? p.sfb1 : p.sfb2);
-      const uint32_t dst_off =
-          tiles ? static_cast<uint32_t>(lane * Cf::kABytes)
-                : static_cast<uint32_t>(Cf::kABytes + Cf::kBBytes +
-                                        lane * kSfRunBytes);
-      const uint32_t mask = tiles ? 0x3u : 0x7u;
+    // As in the 1-SM kernel, lane 0 of warp 4 copies this CTA's A scale run,
+    // the first B scale run and its A rows, lane 0 of warp 5 the second B
+    // scale run and this CTA's B half (the B1 tile in CTA 0, B2 in CTA 1):
+    // a thread issues its copies one at a time, two warps side by side.
+    // Tile bytes land on the even CTA's `full` barrier, whose expected bytes
+    // (both CTAs' tiles) come with the even CTA's first scale warp's
+    // arrival; scale runs land on this CTA's `sfdata` barrier, re-armed by
+    // its first scale warp.
+    if (lane == 0) {
+      const bool a_side = (warp == kProdAWarp);
+      // A is read by every CTA of its row of tiles: keep it in L2 longer
+      const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
+      const uint32_t full_c = mapa_shared(smem_u32(&full_bar[0]), 0);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -1020,19 +1042,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (; ok && have; have = work_next(plan, it, w)) {
         const int m_tile = w.tile % plan.m_tiles;
         const int n_tile = w.tile / plan.m_tiles;
-        const int row = (lane == 0)
-                            ? m_tile * 2 * kBM + static_cast<int>(rank) * kBM
-                            : n_tile * BN;
+        const int a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
         // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
         // lie wholly past M (M in (256t, 256t + 128] for the last pair
         // tile) it copies the last block instead: its A rows are zero-filled
         // by the tensor map and its accumulator rows are never stored.
-        const int blk = (lane == 0)
-                            ? min(m_tile * 2 + static_cast<int>(rank),
-                                  (p.M + kBM - 1) / kBM - 1)
-                            : (n_tile * BN) / 128;
-        const uint8_t* sf_src =
-            sf_base + (size_t)blk * kblk64 * kSfAtomBytes;
+        const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
+                              (p.M + kBM - 1) / kBM - 1);
+        const uint8_t* sfa_src =
+            p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
+        const size_t sfb_off =
+            (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
                                  kErrProducer)) {
@@ -1040,30 +1060,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + stage * Cf::kStageBytes;
-          if (tiles) {
-            if (lane == 0) {
-              NVFP4DG_STAMP(0, issued);
-              if (leader) {
-                // The MMAs that read this stage in both CTAs are done: pass
-                // that on to the odd CTA (from the second fill on).
-                if (issued >= S)
-                  mbar_arrive_cluster(
-                      mapa_shared(smem_u32(&empty_bar[stage]), 1u));
-                mbar_arrive_expect_tx(&full_bar[stage],
-                                      2 * (Cf::kABytes + Cf::kBBytes));
-              }
-            }
-            __syncwarp(mask);
-            tma_load_2d_pair(st + dst_off, map,
-                             mapa_shared(smem_u32(&full_bar[stage]), 0),
-                             kb * kRowBytes, row, pol);
-            if (lane == 0) NVFP4DG_STAMP(1, issued);
-          } else {
-            if (lane == 0)
-              mbar_arrive_expect_tx(&sfdata_bar[stage], 3 * kSfRunBytes);
-            __syncwarp(mask);
-            bulk_load(st + dst_off, sf_src + (size_t)kb * kSfRunBytes,
+          uint8_t* sf_dst = st + Cf::kABytes + Cf::kBBytes;
+          const size_t run = (size_t)kb * kSfRunBytes;
+          const uint32_t full_s = full_c + 8u * static_cast<uint32_t>(stage);
+          if (a_side) {
+            NVFP4DG_STAMP(0, issued);
+            // The MMAs that read this stage in both CTAs are done: pass that
+            // on to the odd CTA (from the second fill on).
+            if (leader && issued >= S)
+              mbar_arrive_cluster(
+                  mapa_shared(smem_u32(&empty_bar[stage]), 1u));
+            bulk_load(sf_dst, sfa_src + run, kSfRunBytes, &sfdata_bar[stage],
+                      pol);
+            bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
+            tma_load_2d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, pol);
+            NVFP4DG_STAMP(1, issued);
+          } else {
+            bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
+                      kSfRunBytes, &sfdata_bar[stage], pol);
+            tma_load_2d_pair(st + Cf::kABytes, rank == 0 ? &tmB1 : &tmB2,
+                             full_s, kb * kRowBytes, n_tile * BN, pol);
           }
           ++issued;
           if (++stage == S) {
@@ -1073,16 +1090,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: the scale runs land on this CTA's own barrier; the A/B tiles
-      // of both CTAs land on the even CTA's `full` barrier, which its tile
-      // producer drains (the odd CTA cannot pass the final cluster barrier
-      // before that).
+      // of both CTAs land on the even CTA's `full` barrier, which its warp 4
+      // drains (the odd CTA cannot pass the final cluster barrier before
+      // that).
       for (int s = 0; s < S; ++s) {
         if (issued > s) {
           const uint32_t par =
               static_cast<uint32_t>(((issued - 1 - s) / S) & 1);
-          if (!tiles)
-            mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain, false);
-          else if (leader)
+          mbar_wait(&sfdata_bar[s], par, p.err, kErrDrain, false);
+          if (a_side && leader)
             mbar_wait_cluster(&full_bar[s], par, p.err, kErrDrain, false);
         }
       }
@@ -1110,7 +1126,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(6, done);
+        if (warp == kSfWarp0 && lane == 0) {
+          NVFP4DG_STAMP(6, done);
+          // arm the stage's next scale fill (see the 1-SM kernel)
+          mbar_arrive_expect_tx(&sfdata_bar[stage], 3 * kSfRunBytes);
+        }
         const uint32_t sf_s = smem_u32(smem + stage * Cf::kStageBytes +
                                        Cf::kABytes + Cf::kBBytes) +
                               16u * lane;
@@ -1158,8 +1178,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0)
-          mbar_arrive_cluster(mapa_shared(smem_u32(&full_bar[stage]), 0));
+        if (lane == 0) {
+          const uint32_t full_s = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          // the even CTA's first scale warp also expects both CTAs' tiles
+          if (leader && warp == kSfWarp0)
+            mbar_arrive_expect_tx_cluster(full_s,
+                                          2 * (Cf::kABytes + Cf::kBBytes));
+          else
+            mbar_arrive_cluster(full_s);
+        }
         if (warp == kSfWarp0 && lane == 0) NVFP4DG_STAMP(7, done);
         ++done;
         if (++stage == S) {
@@ -1456,12 +1483,16 @@ std::map<int, DevInfo> g_dev;
 
 struct MapKey {
   const void* ptr;
+  const void* ptr2;  // second tensor of a B1|B2 map, else nullptr
+  int rank;
   long long rows;
   long long row_bytes;
   int box_rows;
   int dev;
   bool operator<(const MapKey& o) const {
     if (ptr != o.ptr) return ptr < o.ptr;
+    if (ptr2 != o.ptr2) return ptr2 < o.ptr2;
+    if (rank != o.rank) return rank < o.rank;
     if (rows != o.rows) return rows < o.rows;
     if (row_bytes != o.row_bytes) return row_bytes < o.row_bytes;
     if (box_rows != o.box_rows) return box_rows < o.box_rows;
@@ -1512,9 +1543,13 @@ int device_info(int dev, DevInfo** out) {
   return NVFP4DG_OK;
 }
 
+// Tiled map of a K-major [rows][row_bytes] matrix, box {128 B, box_rows}
+// with the 128-byte swizzle.  rank 3 adds a unit outer dimension, so that
+// the 1-SM kernel issues every tile copy as the same 3-D instruction (see
+// b_pair_map).
 int tensor_map(const void* ptr, long long rows, long long row_bytes,
-               int box_rows, int dev, CUtensorMap* out) {
-  MapKey key{ptr, rows, row_bytes, box_rows, dev};
+               int box_rows, int dev, CUtensorMap* out, int rank = 2) {
+  MapKey key{ptr, nullptr, rank, rows, row_bytes, box_rows, dev};
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
     *out = it->second;
@@ -1523,13 +1558,14 @@ int tensor_map(const void* ptr, long long rows, long long row_bytes,
   int rc = get_encode();
   if (rc) return rc;
   CUtensorMap m;
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes),
-                              static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kRowBytes),
-                             static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_bytes),
+                              static_cast<cuuint64_t>(rows), 1};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes),
+                                 static_cast<cuuint64_t>(rows * row_bytes)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRowBytes),
+                             static_cast<cuuint32_t>(box_rows), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank,
                         const_cast<void*>(ptr), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1543,6 +1579,47 @@ int tensor_map(const void* ptr, long long rows, long long row_bytes,
   g_maps[key] = m;
   *out = m;
   return NVFP4DG_OK;
+}
+
+// One map over both weight matrices: a 3-D view [2][rows][row_bytes] whose
+// outer stride is the distance from B1 to B2, so that a single copy with box
+// {128 B, box_rows, 2} lands the B1 tile and then the B2 tile, exactly the
+// stacked layout the MMA reads.  Every coordinate stays inside B1 or B2.
+// Needs B2 above B1 at a multiple of 16 bytes; returns false (and the caller
+// keeps one map per matrix) otherwise or if the driver rejects the view.
+bool b_pair_map(const void* b1, const void* b2, long long rows,
+                long long row_bytes, int box_rows, int dev, CUtensorMap* out) {
+  const uintptr_t p1 = reinterpret_cast<uintptr_t>(b1);
+  const uintptr_t p2 = reinterpret_cast<uintptr_t>(b2);
+  if (p2 <= p1 || (p2 - p1) % 16 != 0 || (p2 - p1) >= (1ull << 40) ||
+      static_cast<long long>(p2 - p1) < rows * row_bytes)
+    return false;
+  MapKey key{b1, b2, 3, rows, row_bytes, box_rows, dev};
+  auto it = g_maps.find(key);
+  if (it != g_maps.end()) {
+    *out = it->second;
+    return true;
+  }
+  if (get_encode()) return false;
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_bytes),
+                              static_cast<cuuint64_t>(rows), 2};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes),
+                                 static_cast<cuuint64_t>(p2 - p1)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRowBytes),
+                             static_cast<cuuint32_t>(box_rows), 2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3,
+                        const_cast<void*>(b1), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return false;
+  if (g_maps.size() > 256) g_maps.clear();
+  g_maps[key] = m;
+  *out = m;
+  return true;
 }
 
 // ---------------------------------------------------------------- planning
@@ -1778,9 +1855,19 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   }
   CUtensorMap ta, tb1, tb2;
   int rc;
-  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta))) return rc;
-  if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1))) return rc;
-  if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2))) return rc;
+  // The pair kernel copies with 2-D maps; the 1-SM kernel with 3-D ones,
+  // both weight tiles of a K block in one copy when a single map can cover
+  // B1 and B2.
+  const int rank = PAIR ? 2 : 3;
+  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta, rank))) return rc;
+  const bool merged = !PAIR && !(flags & NVFP4DG_FLAG_NO_MERGED_B) &&
+                      b_pair_map(B1, B2, N, K / 2, BN, devid, &tb1);
+  if (merged) {
+    tb2 = tb1;
+  } else {
+    if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1, rank))) return rc;
+    if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2, rank))) return rc;
+  }
   KParams kp;
   kp.plan = plan;
   kp.M = M;
@@ -1795,6 +1882,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
                                               workspace_partials_offset(plan))
                    : nullptr;
   kp.err = dev.err;
+  kp.b_merged = merged ? 1 : 0;
   // Programmatic dependent launch lets this grid be scheduled while the
   // previous one in the stream finishes (the kernel waits for it before its
   // first global access); split-K plans run as 2-CTA clusters.

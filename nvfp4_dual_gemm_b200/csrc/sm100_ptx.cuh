@@ -146,23 +146,15 @@ __device__ __forceinline__ bool wait_count(const int* ptr, int target,
 // ---------------------------------------------------------------------------
 // L2 cache policies (createpolicy) and TMA / bulk copies
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint64_t policy_evict_normal() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;"
-               : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint64_t policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
-               : "=l"(p));
-  return p;
-}
+// The 64-bit cache-policy operands of the copies' .L2::cache_hint, as
+// constants: the values createpolicy.fractional.L2::<priority>.b64 with
+// fraction 1.0 returns on B200 (read back from the instruction; evict_first
+// and evict_last are also the CacheHintSm100 values published in CUTLASS's
+// cute/arch/copy_sm90_desc.hpp).  Creating them at run time puts that
+// instruction's latency on the first copy's path.
+constexpr uint64_t kPolicyEvictNormal = 0x16F0000000000000ull;
+constexpr uint64_t kPolicyEvictFirst = 0x12F0000000000000ull;
+constexpr uint64_t kPolicyEvictLast = 0x14F0000000000000ull;
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m))
@@ -171,14 +163,14 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
 
 // 2-D tiled TMA load global -> this CTA's shared memory; completion is
 // signalled as transaction bytes on `bar`.  c0 is the innermost coordinate.
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* m,
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* m,
                                             uint64_t* bar, int c0, int c1,
-                                            uint64_t policy) {
+                                            int c2, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
-      "tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(
           smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2),
       "r"(smem_u32(bar)), "l"(policy)
       : "memory");
 }
@@ -450,6 +442,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(
                    cluster_addr)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(
+    uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(
+          cluster_addr),
+      "r"(bytes)
+      : "memory");
 }
 
 // Waits on barriers that the peer CTA signals use the ordinary bounded wait.

@@ -30,7 +30,7 @@ import numpy as np
 from . import build as _build
 
 TRACE_LIB = os.path.join(_build.PKG_DIR, "libnvfp4dg_trace.so")
-CTAS, ROLES, SLOTS = 160, 8, 64
+CTAS, ROLES, SLOTS = 160, 10, 64
 
 
 def build_trace_lib(force: bool = False) -> str:
@@ -94,6 +94,17 @@ def summarise(buf: np.ndarray) -> dict:
         if has.any():
             out["cyc_entry_to_first_copy"] = float(
                 np.median(first[has] - buf[ok, 4, 61][has]))
+        # producer's prologue milestones (1-SM kernel): past __syncthreads,
+        # before and after the dependency wait
+        sync, pre, post = buf[ok, 1, 60], buf[ok, 1, 61], buf[ok, 1, 62]
+        if (sync > 0).any():
+            e = buf[ok, 4, 61]
+            out["cyc_entry_to_sync"] = float(np.median((sync - e)[sync > 0]))
+            out["cyc_sync_to_depwait"] = float(
+                np.median((pre - sync)[pre > 0]))
+            out["cyc_depwait"] = float(np.median((post - pre)[post > 0]))
+            out["cyc_depwait_to_first_copy"] = float(
+                np.median((first - post)[(post > 0) & (first > 0)]))
             out["cyc_epilogue_to_exit"] = float(
                 np.median(buf[ok, 4, 63][has] - epi_end[has]))
     return out

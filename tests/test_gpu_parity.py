@@ -362,3 +362,42 @@ def test_sharded_slices_equal_full_product(world):
     torch.cuda.synchronize()
     assert torch.equal(torch.cat(parts, dim=1), full)
     assert_close(full.cpu().numpy(), O.reference_output(p), "full")
+
+
+@pytest.mark.parametrize("order", ["adjacent", "b2_far_above", "b2_below"])
+@pytest.mark.parametrize("flags", [
+    0,
+    _lib.FLAG_BN64 | _lib.FLAG_NO_PAIR | _lib.FLAG_NO_SPLITK,
+    _lib.FLAG_BN128 | _lib.FLAG_NO_PAIR | _lib.FLAG_NO_SPLITK,
+    _lib.FLAG_SPLITK,
+    7 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR,
+])
+def test_weight_placement_and_merged_copy(order, flags):
+    # When B2 lies above B1, one copy brings both weight tiles of a K block
+    # through a single map over the two matrices; when it lies below, two
+    # copies do.  Both must give the same bits.
+    m, n, k = 256, 512, 2048
+    p = O.make_problem(m, n, k, seed=123)
+    d = to_device(p)
+    nb = n * k // 2
+    big = torch.zeros(4 * nb, dtype=torch.uint8, device="cuda")
+    if order == "adjacent":
+        b1, b2 = big[:nb], big[nb:2 * nb]
+    elif order == "b2_far_above":
+        b1, b2 = big[:nb], big[3 * nb - 4096:4 * nb - 4096]
+    else:
+        b2, b1 = big[:nb], big[2 * nb + 256:3 * nb + 256]
+    b1.copy_(d["b1"].reshape(-1))
+    b2.copy_(d["b2"].reshape(-1))
+    b1 = b1.view(n, k // 2)
+    b2 = b2.view(n, k // 2)
+    outs = []
+    for extra in (0, _lib.FLAG_NO_MERGED_B):
+        d["c"].fill_(float("nan"))
+        dg.dual_gemm(d["a"], b1, b2, d["sfa_blocked"], d["sfb1_blocked"],
+                     d["sfb2_blocked"], d["c"],
+                     flags=flags | extra | _lib.FLAG_SYNC_CHECK)
+        torch.cuda.synchronize()
+        outs.append(d["c"].cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
+    assert_close(outs[0], O.reference_output(p), f"{order} {flags:#x}")
