@@ -344,8 +344,8 @@ __device__ __forceinline__ bool split_group_all(bool pred) {
 
 // Epilogue of a cluster split-K tile, run once by the four epilogue warps
 // (part 0) and the four scale warps (part 1; idle once the main loop is
-// done): each warp owns TMEM lanes 32 (warp % 4) .. + 31.  Each CTA of the
-// pair holds the partial sums of half of K; CTA h finishes output columns
+// done): each warp owns TMEM lanes 32 (warp % 4) .. + 31.  Each of the two
+// CTAs holds the partial sums of half of K; CTA h finishes output columns
 // [h BN/2, (h+1) BN/2) in 16-column chunks j, part (j % 2) taking chunk j.
 // For each of its chunks a warp sends the peer's GEMM1 and GEMM2 partials of
 // chunk j into the peer's operand ring (idle once the peer's MMAs are done)
@@ -355,23 +355,23 @@ __device__ __forceinline__ bool split_group_all(bool pred) {
 // 16-byte group g of row r sits at (g * 128 + r) * 16 (GEMM1 chunk j: groups
 // 4j .. 4j+3, GEMM2 chunk j: groups 4 (BN/32 + j) ..), so a warp's 32 rows
 // are contiguous.
+// `own` is the half of K this CTA computed, which is also the half of the
+// columns it finishes; `xpeer` the cluster rank of the CTA that holds the
+// other half of K for the same 128 output rows; `grow0` the first of those
+// rows in C.  With `cluster_waited` set, the cluster barrier that publishes
+// every CTA's barrier initialisation has already been waited on.
 template <int BN>
 __device__ __forceinline__ void split_epilogue(
     const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
     uint64_t* ready_bar, uint64_t* recv_bar, int warp, int lane, int part,
-    bool& cluster_waited) {
+    int own, uint32_t xpeer, int grow0, int n_tile, bool& cluster_waited) {
   constexpr int kHalf = BN / 2;
   constexpr int kHalfChunks = kHalf / 16;
   constexpr uint32_t kChunkBytes = 2u * 128u * 16u * 4u;  // GEMM1 + GEMM2
-  const Plan& plan = p.plan;
-  const int own = static_cast<int>(blockIdx.x & 1);
-  const uint32_t peer = static_cast<uint32_t>(own ^ 1);
+  const int other = own ^ 1;
   const int row = 32 * (warp % 4) + lane;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16);
-  const int tile = static_cast<int>(blockIdx.x >> 1);
-  const int m_tile = tile % plan.m_tiles;
-  const int n_tile = tile / plan.m_tiles;
-  const int grow = m_tile * kBM + row;
+  const int grow = grow0 + row;
   const bool row_ok = grow < p.M;
   __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
 
@@ -380,18 +380,20 @@ __device__ __forceinline__ void split_epilogue(
   if (!split_group_all(ok)) return;
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(4, 0);
   tc_fence_after();
-  cluster_wait();  // the peer's barriers are initialised
-  cluster_waited = true;
+  if (!cluster_waited) {
+    cluster_wait();  // the peer's barriers are initialised
+    cluster_waited = true;
+  }
   if (part == 0 && threadIdx.x == 0) {
 #pragma unroll
     for (int c = 0; c < kHalfChunks; ++c)
       mbar_arrive_expect_tx(&recv_bar[c], kChunkBytes);
-    mbar_arrive_cluster(mapa_shared(smem_u32(ready_bar), peer));
+    mbar_arrive_cluster(mapa_shared(smem_u32(ready_bar), xpeer));
   }
   ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
   if (!split_group_all(ok)) return;
   const uint32_t xbuf = smem_u32(smem);
-  const uint32_t xdst = mapa_shared(xbuf, peer);
+  const uint32_t xdst = mapa_shared(xbuf, xpeer);
   // This warp's chunks j = part, part + 2 (at most two): all TMEM loads are
   // issued before one wait, then the stores go out.
   constexpr int kMine = (kHalfChunks + 1) / 2;
@@ -402,9 +404,8 @@ __device__ __forceinline__ void split_epilogue(
     if (c < kHalfChunks) {
 #pragma unroll
       for (int xy = 0; xy < 2; ++xy)
-        tc_ld_16cols(t_row + static_cast<uint32_t>(
-                                 xy * BN + static_cast<int>(peer) * kHalf +
-                                 16 * c),
+        tc_ld_16cols(t_row + static_cast<uint32_t>(xy * BN + other * kHalf +
+                                                   16 * c),
                      v[i][xy]);
     }
   }
@@ -413,7 +414,7 @@ __device__ __forceinline__ void split_epilogue(
   for (int i = 0; i < kMine; ++i) {
     const int c = part + 2 * i;
     if (c < kHalfChunks) {
-      const uint32_t cbar = mapa_shared(smem_u32(&recv_bar[c]), peer);
+      const uint32_t cbar = mapa_shared(smem_u32(&recv_bar[c]), xpeer);
 #pragma unroll
       for (int xy = 0; xy < 2; ++xy) {
         const int g0 = 4 * (xy * kHalfChunks + c);
@@ -526,6 +527,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmB1);
     prefetch_tmap(&tmB2);
   }
+  // Split-K clusters: every thread arrives on the cluster barrier once the
+  // barriers are initialised; the epilogue waits on it before its first
+  // remote operation, the other warps at teardown.
+  __syncwarp();
+  if (plan.split == 2) cluster_arrive_relaxed();
   if (warp == kMmaWarp) {
     tmem_alloc(&tmem_base_sh, kTmemCols);
     tmem_relinquish();
@@ -533,12 +539,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (threadIdx.x == 32 * kProdAWarp) NVFP4DG_STAMP(1, 60);
-  // Split-K clusters: every thread arrives on the cluster barrier once the
-  // barriers are initialised; the epilogue waits on it before its first
-  // remote operation, the other warps at teardown.
-  if (plan.split == 2) cluster_arrive_relaxed();
   // Whether this thread has waited on that arrival (warp-uniform).
   bool cluster_waited = false;
+  // Split-K: this CTA's half of K (= its cluster rank) and its tile.
+  const int split_own = static_cast<int>(blockIdx.x & 1);
+  const int split_m_tile = static_cast<int>(blockIdx.x >> 1) % plan.m_tiles;
+  const int split_n_tile = static_cast<int>(blockIdx.x >> 1) / plan.m_tiles;
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -733,7 +739,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                         warp, lane, 1, cluster_waited);
+                         warp, lane, 1, split_own, split_own ^ 1u,
+                         split_m_tile * kBM, split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
@@ -803,7 +810,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                       warp, lane, 0, cluster_waited);
+                       warp, lane, 0, split_own, split_own ^ 1u,
+                       split_m_tile * kBM, split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
     const int row = threadIdx.x;  // TMEM lane == tile row
@@ -945,7 +953,7 @@ struct PairCfg {
 };
 
 template <int BN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB1,
                           const __grid_constant__ CUtensorMap tmB2,
@@ -963,6 +971,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_empty_bar;  // even CTA: both drained
   __shared__ __align__(8) uint64_t drain_bar;
   __shared__ __align__(8) uint64_t fix_bar[kFixSlots];  // stream-K owner
+  __shared__ __align__(8) uint64_t ready_bar;  // split-K: partner may write
+  // split-K: the partner's partials of chunk j of this CTA's half landed
+  __shared__ __align__(8) uint64_t recv_bar[BN / 32];
   __shared__ uint32_t tmem_base_sh;
 
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -972,9 +983,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const Plan& plan = p.plan;
-  const uint32_t rank = cluster_ctarank();
-  const int unit = blockIdx.x >> 1;  // the pair's work-unit index
+  // Clusters of 2 CTAs (one pair), or of 4 for split-K (two pairs: ranks
+  // 2h and 2h + 1 take half h of K).  A pair is ranks (lead, lead + 1).
+  const uint32_t crank = cluster_ctarank();
+  const uint32_t rank = crank & 1u;   // position in the pair
+  const uint32_t lead = crank & ~1u;  // cluster rank of the pair's even CTA
+  const int unit = blockIdx.x >> 1;   // the pair's work-unit index
   const bool leader = (rank == 0);
+  // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
+  // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
+  const int split_own = static_cast<int>(crank >> 1);
+  const int split_m_tile = (unit >> 1) % plan.m_tiles;
+  const int split_n_tile = (unit >> 1) / plan.m_tiles;
+  const int split_grow0 =
+      split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+  bool cluster_waited = true;  // the start-up cluster barrier (below)
 
   if (warp == kProdAWarp && lane == 0) {
     for (int s = 0; s < S; ++s) {
@@ -989,6 +1012,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(&acc_empty_bar, 2 * kEpiWarps);
     mbar_init(&drain_bar, 1);
     for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
+    mbar_init(&ready_bar, 1);
+    for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
     fence_mbar_init();
     // arm the first scale fill of every stage
     for (int s = 0; s < S; ++s)
@@ -997,15 +1022,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
   }
+  // Every CTA's barriers initialised (published by the mbarrier-init fence)
+  // before any remote use: arrive now, wait after the TMEM allocation, so
+  // that the cluster-wide barrier completes meanwhile.
+  __syncwarp();
+  cluster_arrive_relaxed();
   if (warp == kMmaWarp) {
     tmem_alloc_pair(&tmem_base_sh, kTmemCols);
     tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();  // TMEM base and barrier inits visible within the CTA
-  // Barriers of both CTAs initialised (published by the mbarrier-init fence)
-  // before any remote use.
-  cluster_arrive_relaxed();
   cluster_wait();
   tc_fence_after();
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -1029,7 +1056,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const bool a_side = (warp == kProdAWarp);
       // A is read by every CTA of its row of tiles: keep it in L2 longer
       const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
-      const uint32_t full_c = mapa_shared(smem_u32(&full_bar[0]), 0);
+      const uint32_t full_c = mapa_shared(smem_u32(&full_bar[0]), lead);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
@@ -1069,7 +1096,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // on to the odd CTA (from the second fill on).
             if (leader && issued >= S)
               mbar_arrive_cluster(
-                  mapa_shared(smem_u32(&empty_bar[stage]), 1u));
+                  mapa_shared(smem_u32(&empty_bar[stage]), lead + 1u));
             bulk_load(sf_dst, sfa_src + run, kSfRunBytes, &sfdata_bar[stage],
                       pol);
             bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
@@ -1179,7 +1206,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          const uint32_t full_s = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          const uint32_t full_s =
+              mapa_shared(smem_u32(&full_bar[stage]), lead);
           // the even CTA's first scale warp also expects both CTAs' tiles
           if (leader && warp == kSfWarp0)
             mbar_arrive_expect_tx_cluster(full_s,
@@ -1195,12 +1223,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
     }
+    // Split-K: the scale warps help finish the tile.
+    if (plan.split == 2)
+      split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
+                         warp, lane, 1, split_own, crank ^ 2u, split_grow0,
+                         split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
       constexpr uint32_t kIdesc = idesc_nvf4(256, 2 * BN);
       constexpr uint32_t kSfbStep = (BN == 128) ? 8u : 4u;
-      const uint32_t peer = 1u;
+      const uint32_t peer = lead + 1u;
       const uint64_t a_desc0 = smem_desc(smem_u32(smem), 16, 1024,
                                          SmemLayout::kSwizzle128B);
       const uint64_t b_desc0 = smem_desc(smem_u32(smem) + Cf::kABytes, 16,
@@ -1245,7 +1278,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
           // The stage is free in both CTAs once these MMAs complete; the
           // odd CTA learns it from the even producer A (one commit here).
-          tc_commit_pair(mapa_shared(smem_u32(&empty_bar[stage]), 0));
+          tc_commit_pair(mapa_shared(smem_u32(&empty_bar[stage]), lead));
           NVFP4DG_STAMP(3, consumed);
           ++consumed;
           if (++stage == S) {
@@ -1255,19 +1288,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         const uint32_t ab = smem_u32(&acc_full_bar);
-        tc_commit_pair(mapa_shared(ab, 0));
+        tc_commit_pair(mapa_shared(ab, lead));
         tc_commit_pair(mapa_shared(ab, peer));
         acc_phase ^= 1u;
       }
-      tc_commit_pair(mapa_shared(smem_u32(&drain_bar), 0));
+      tc_commit_pair(mapa_shared(smem_u32(&drain_bar), lead));
       mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
     }
     __syncwarp();
+  } else if (plan.split == 2) {
+    // ------------------------------------------------------------ epilogue
+    split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
+                       warp, lane, 0, split_own, crank ^ 2u, split_grow0,
+                       split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
     const int row = threadIdx.x;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), 0);
+    const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), lead);
     uint32_t acc_phase = 0;
     int unit_i = 0;
     WorkIter it;
@@ -1655,12 +1693,13 @@ Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
   return p;
 }
 
-// Cluster split-K: one tile per pair of CTAs, each CTA half of K.
-Plan plan_split(int M, int N, int K, int bn) {
+// Cluster split-K: each tile's K range in two halves on two work units (two
+// CTAs, or two 2-SM pairs in a cluster of four) that exchange partial sums.
+Plan plan_split(int M, int N, int K, int bn, int ctas = 1) {
   Plan p{};
   p.bn = bn;
-  p.ctas = 1;
-  p.m_tiles = (M + kBM - 1) / kBM;
+  p.ctas = ctas;
+  p.m_tiles = (M + kBM * ctas - 1) / (kBM * ctas);
   p.n_tiles = N / bn;
   p.kblocks = K / 256;
   p.num_tiles = p.m_tiles * p.n_tiles;
@@ -1671,10 +1710,11 @@ Plan plan_split(int M, int N, int K, int bn) {
   return p;
 }
 
-bool split_fits(int M, int N, int K, int bn, int sms) {
+bool split_fits(int M, int N, int K, int bn, int sms, int ctas = 1) {
   if (N % bn != 0 || K / 256 < 2) return false;
-  const long long tiles = (long long)((M + kBM - 1) / kBM) * (N / bn);
-  return 2 * tiles <= sms;
+  const long long tiles =
+      (long long)((M + kBM * ctas - 1) / (kBM * ctas)) * (N / bn);
+  return 2 * ctas * tiles <= sms;
 }
 
 // Estimated SM cycles of the busiest work unit, from pipeline traces on B200
@@ -1695,9 +1735,15 @@ double plan_cost(const Plan& p) {
   const double epi = (p.bn == 128) ? 3900.0 : 2100.0;
   const double tear = pair ? 2100.0 : 500.0;
   const double start = 2300.0;
-  if (p.split == 2)
-    return 3200.0 + ((p.kblocks + 1) / 2) * (p.bn == 128 ? 830.0 : 715.0) +
-           (p.bn == 128 ? 5100.0 : 2800.0) + 1600.0;
+  if (p.split == 2) {
+    // 2-SM pairs stream 38 KB per K block and SM where single CTAs stream
+    // 54 KB (BN = 128) for the same MMAs; with ~128 SMs sharing L2 that
+    // sets the block period
+    const double blk = pair ? (p.bn == 128 ? 640.0 : 600.0)
+                            : (p.bn == 128 ? 830.0 : 715.0);
+    return (pair ? 3400.0 : 3200.0) + ((p.kblocks + 1) / 2) * blk +
+           (p.bn == 128 ? 5100.0 : 2800.0) + (pair ? 2100.0 : 1600.0);
+  }
   double cost = start + tear;
   double tiles = 0;
   if (p.dp_tiles > 0) {
@@ -1748,21 +1794,24 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
   Plan best{};
   double best_cost = 1e300;
   if (flags & NVFP4DG_FLAG_SPLITK) {
+    // forced: 2-SM pairs when PAIR is also given, else single CTAs
+    const int ctas = (flags & NVFP4DG_FLAG_PAIR) ? 2 : 1;
     for (int i = 0; i < nb; ++i)
-      if (split_fits(M, N, K, bns[i], forced > 0 ? forced : sms))
-        return plan_split(M, N, K, bns[i]);
+      if (split_fits(M, N, K, bns[i], forced > 0 ? forced : sms, ctas))
+        return plan_split(M, N, K, bns[i], ctas);
     return best;  // grid == 0: not possible (rejected by check_problem)
   }
-  if (!(flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_PAIR |
-                 NVFP4DG_FLAG_FORCE_STREAMK)) &&
+  if (!(flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_FORCE_STREAMK)) &&
       forced == 0) {
-    for (int i = 0; i < nb; ++i) {
-      if (!split_fits(M, N, K, bns[i], sms)) continue;
-      Plan p = plan_split(M, N, K, bns[i]);
-      const double cost = plan_cost(p);
-      if (cost < best_cost) {
-        best_cost = cost;
-        best = p;
+    for (int c = 0; c < nc; ++c) {
+      for (int i = 0; i < nb; ++i) {
+        if (!split_fits(M, N, K, bns[i], sms, ctas_opts[c])) continue;
+        Plan p = plan_split(M, N, K, bns[i], ctas_opts[c]);
+        const double cost = plan_cost(p);
+        if (cost < best_cost) {
+          best_cost = cost;
+          best = p;
+        }
       }
     }
   }
@@ -1820,10 +1869,9 @@ int check_problem(const void* A, const void* B1, const void* B2,
   if ((flags & NVFP4DG_FLAG_PAIR) && (flags & NVFP4DG_FLAG_NO_PAIR))
     return fail(NVFP4DG_ERR_INVALID, "PAIR and NO_PAIR flags are exclusive");
   if ((flags & NVFP4DG_FLAG_SPLITK) &&
-      (flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_PAIR |
-                NVFP4DG_FLAG_FORCE_STREAMK)))
+      (flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_FORCE_STREAMK)))
     return fail(NVFP4DG_ERR_INVALID,
-                "SPLITK excludes NO_SPLITK, PAIR and FORCE_STREAMK");
+                "SPLITK excludes NO_SPLITK and FORCE_STREAMK");
   if (M == 0 || N == 0) return NVFP4DG_OK;
   const void* ptrs[7] = {A, B1, B2, SFA, SFB1, SFB2, C};
   const char* names[7] = {"A", "B1", "B2", "SFA", "SFB1", "SFB2", "C"};
@@ -1885,7 +1933,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.b_merged = merged ? 1 : 0;
   // Programmatic dependent launch lets this grid be scheduled while the
   // previous one in the stream finishes (the kernel waits for it before its
-  // first global access); split-K plans run as 2-CTA clusters.
+  // first global access); clusters as set below.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid * plan.ctas, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
@@ -1898,9 +1946,12 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
     ++na;
   }
-  if (!PAIR && plan.split == 2) {
+  // clusters: a 2-SM pair (2), a split-K pair of CTAs (2) or of 2-SM pairs
+  // (4)
+  const int cluster = (PAIR ? 2 : 1) * (plan.split == 2 ? 2 : 1);
+  if (cluster > 1) {
     attrs[na].id = cudaLaunchAttributeClusterDimension;
-    attrs[na].val.clusterDim.x = 2;
+    attrs[na].val.clusterDim.x = cluster;
     attrs[na].val.clusterDim.y = 1;
     attrs[na].val.clusterDim.z = 1;
     ++na;
@@ -1955,7 +2006,7 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   const Plan plan = choose_plan(M, N, K, flags, dev->sms);
   if (plan.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
-                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
+                "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
   const size_t need = static_cast<size_t>(workspace_bytes(plan));
   if (own_ws && need > 0) {
     WsEntry& ent = g_ws[{devid, stream_ptr}];
@@ -2204,7 +2255,7 @@ int run_host_impl(const void* A, const void* B1, const void* B2,
       const int w = std::min(rows, N - j * rows);
       if (choose_plan(M, w, K, flags, dev->sms).grid == 0)
         return fail(NVFP4DG_ERR_UNSUPPORTED,
-                    "cluster split-K needs 2 x tiles <= SMs and K >= 512 "
+                    "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512 "
                     "(slab of " + std::to_string(w) + " columns)");
     }
   }
@@ -2360,7 +2411,7 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
   const Plan plan = choose_plan(M, N, K, flags, dev->sms);
   if (plan.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
-                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
+                "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
   const size_t need = static_cast<size_t>(workspace_bytes(plan));
   if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
     return fail(NVFP4DG_ERR_WORKSPACE,
@@ -2432,7 +2483,7 @@ int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,
   const Plan p = choose_plan(M, N, K, flags, num_sms);
   if (p.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
-                "cluster split-K needs 2 x tiles <= SMs and K >= 512");
+                "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
   if (split_out) *split_out = p.split;
   if (bn_out) *bn_out = p.bn;
   if (ctas_out) *ctas_out = p.ctas;

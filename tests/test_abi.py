@@ -184,20 +184,42 @@ def test_cluster_split_k_covers_every_block_once(m, n, k):
         assert [(a, b) for a, b, _, _ in sorted(segs)] == [(0, h), (h, k // 256)]
 
 
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 7168), (256, 512, 2048),
+                                   (200, 256, 768), (333, 192, 1024),
+                                   (128, 64, 512), (512, 2048, 1024)])
+def test_pair_cluster_split_k_covers_every_block_once(m, n, k):
+    # 2-SM pairs in clusters of four: unit 2t + h is pair h of tile t
+    pl, seen = cover(m, n, k, flags=dg.FLAG_SPLITK | dg.FLAG_PAIR)
+    assert pl["split"] == 2 and pl["ctas"] == 2 and pl["sk_tiles"] == 0
+    assert pl["grid"] == 2 * len(seen) and 2 * pl["grid"] <= 148
+    h = (k // 256 + 1) // 2
+    for segs in seen.values():
+        assert [(a, b) for a, b, _, _ in sorted(segs)] == [(0, h), (h, k // 256)]
+
+
 def test_cluster_split_k_choice_and_limits():
-    # decode shape: 64 tiles of 128 columns -> 128 CTAs in 64 clusters
+    # decode shape: 32 pair tiles of 256 x 128 -> 128 CTAs in 32 clusters of
+    # four (two 2-SM pairs, one per half of K)
     pl = dg.plan(256, 4096, 7168)
-    assert pl["split"] == 2 and pl["bn"] == 128 and pl["grid"] == 128
+    assert pl["split"] == 2 and pl["bn"] == 128 and pl["ctas"] == 2
+    assert pl["grid"] * pl["ctas"] == 128
+    assert dg.plan(256, 4096, 7168, dg.FLAG_NO_PAIR)["ctas"] == 1
     assert dg.plan(256, 4096, 7168, dg.FLAG_NO_SPLITK)["split"] == 0
     # too many tiles for 2 CTAs each, or a single K block: not possible
     for shape in ((4096, 14336, 4096), (256, 4096, 256)):
-        with pytest.raises(RuntimeError):
-            dg.plan(*shape, dg.FLAG_SPLITK)
+        for extra in (0, dg.FLAG_PAIR):
+            with pytest.raises(RuntimeError):
+                dg.plan(*shape, dg.FLAG_SPLITK | extra)
         assert dg.plan(*shape)["split"] == 0
+    # 384 rows: 3 single-CTA row tiles but 2 pair tiles of 256 (4 SMs each),
+    # so 20 column tiles fit single CTAs (120 SMs) but not pairs (160)
+    assert dg.plan(384, 2560, 1024, dg.FLAG_SPLITK)["ctas"] == 1
+    with pytest.raises(RuntimeError):
+        dg.plan(384, 2560, 1024, dg.FLAG_SPLITK | dg.FLAG_PAIR)
     # exclusive flags are rejected before any GPU work
     lib = _lib.load()
     ptr = ctypes.c_void_p(16)
-    for bad in (dg.FLAG_PAIR, dg.FLAG_NO_SPLITK, dg.FLAG_FORCE_STREAMK):
+    for bad in (dg.FLAG_NO_SPLITK, dg.FLAG_FORCE_STREAMK):
         rc = lib.nvfp4_dual_gemm_run(ptr, ptr, ptr, ptr, ptr, ptr, ptr, 256,
                                      512, 2048, 1, dg.FLAG_SPLITK | bad, None)
         assert rc == _lib.ERR_INVALID and "SPLITK" in _lib.last_error()

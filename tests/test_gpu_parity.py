@@ -137,12 +137,18 @@ def test_ragged_m_and_small_shapes(m, n, k, pair):
                                       (256, 512, 2048, 64),
                                       (200, 256, 768, 128),
                                       (333, 192, 1024, 64),
-                                      (128, 128, 512, 128)])
-def test_cluster_split_k(m, n, k, bn):
+                                      (128, 128, 512, 128),
+                                      (256, 4096, 7168, 128)])
+@pytest.mark.parametrize("pair", [0, _lib.FLAG_PAIR])
+def test_cluster_split_k(m, n, k, bn, pair):
+    # single CTAs in clusters of two, or 2-SM pairs in clusters of four (the
+    # odd CTA of a pair past M for the ragged shapes); K halves exchange
+    # partial sums through distributed shared memory
     p = O.make_problem(m, n, k, seed=m + 7 * n + k)
-    flags = _lib.FLAG_SPLITK | (_lib.FLAG_BN64 if bn == 64 else
-                                _lib.FLAG_BN128) | _lib.FLAG_SYNC_CHECK
-    assert dg.plan(m, n, k, flags)["split"] == 2
+    flags = _lib.FLAG_SPLITK | pair | (_lib.FLAG_BN64 if bn == 64 else
+                                       _lib.FLAG_BN128) | _lib.FLAG_SYNC_CHECK
+    pl = dg.plan(m, n, k, flags)
+    assert pl["split"] == 2 and pl["ctas"] == (2 if pair else 1)
     ref = O.reference_output(p)
     d = to_device(p)
     for _ in range(2):  # twice: no state may leak between launches
