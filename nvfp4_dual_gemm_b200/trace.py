@@ -95,9 +95,10 @@ def summarise(buf: np.ndarray) -> dict:
             out["cyc_entry_to_first_copy"] = float(
                 np.median(first[has] - buf[ok, 4, 61][has]))
         # producer's prologue milestones (1-SM kernel): past __syncthreads,
-        # before and after the dependency wait
+        # before and after the dependency wait (slots 60-62 of role 1, which
+        # the per-block stamps reach when a CTA runs 60 or more K blocks)
         sync, pre, post = buf[ok, 1, 60], buf[ok, 1, 61], buf[ok, 1, 62]
-        if (sync > 0).any():
+        if (sync > 0).any() and out.get("kblocks", 0) < 60:
             e = buf[ok, 4, 61]
             out["cyc_entry_to_sync"] = float(np.median((sync - e)[sync > 0]))
             out["cyc_sync_to_depwait"] = float(
