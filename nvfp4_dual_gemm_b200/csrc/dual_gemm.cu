@@ -128,6 +128,19 @@ __device__ __forceinline__ void epi_bar() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// Start-up barriers: the producer warps (4, 5) meet warp 0 once it has
+// initialised the mbarriers (kBarInit: warp 0 arrives, the producers wait),
+// and every other warp meets the others once TMEM is allocated (kBarStart);
+// the producers never wait for the TMEM allocation.
+constexpr int kBarInit = 5;
+constexpr int kBarStart = 6;
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
 // Barrier `ID` over 128 threads (four warps) that also ANDs a predicate:
 // every thread gets the same answer, so a group that must later meet at the
 // same named barrier either continues together or leaves together.
@@ -503,7 +516,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x % 32;
   const Plan& plan = p.plan;
 
-  if (warp == kProdAWarp && lane == 0) {
+  const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
+  // Warp 0 (an epilogue warp, idle until the first tile is computed)
+  // initialises the mbarriers while the producers work out their first item.
+  if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; ++s) {
       // the scale warps; the first one's arrival carries the tiles' bytes
       mbar_init(&full_bar[s], kSfWarps);
@@ -532,13 +548,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // remote operation, the other warps at teardown.
   __syncwarp();
   if (plan.split == 2) cluster_arrive_relaxed();
-  if (warp == kMmaWarp) {
-    tmem_alloc(&tmem_base_sh, kTmemCols);
-    tmem_relinquish();
+  uint32_t tmem = 0;
+  if (!producer) {
+    if (warp == 0) named_bar_arrive(kBarInit, 96);
+    if (warp == kMmaWarp) {
+      tmem_alloc(&tmem_base_sh, kTmemCols);
+      tmem_relinquish();
+    }
+    tc_fence_before();
+    named_bar_sync(kBarStart, kThreads - 64);
+    tc_fence_after();
+    tmem = tmem_base_sh;
   }
-  tc_fence_before();
-  __syncthreads();
-  if (threadIdx.x == 32 * kProdAWarp) NVFP4DG_STAMP(1, 60);
   // Whether this thread has waited on that arrival (warp-uniform).
   bool cluster_waited = false;
   // Split-K: this CTA's half of K (= its cluster rank) and its tile.
@@ -551,8 +572,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   // its own setup, so the first pass through its code overlaps that wait.
   griddep_launch_dependents();
   NVFP4DG_STAMP_NS(62);
-  tc_fence_after();
-  const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;  // scale atoms per 128-row block
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
@@ -570,28 +589,34 @@ __global__ void __launch_bounds__(kThreads, 1)
     // chain of waits and tcgen05 instructions sets the pace.  Scale runs go
     // first and land on their own barrier, so the scale warps move them into
     // TMEM while the tiles are in flight.
+    // First item and its addresses before meeting warp 0 (parameters only).
+    const bool a_side = (warp == kProdAWarp);
+    // A is read by every CTA of its row of tiles: keep it in L2 longer
+    const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
+    WorkIter it;
+    work_begin(plan, blockIdx.x, it);
+    Work w;
+    bool have = work_next(plan, it, w);
+    int m_tile = 0, n_tile = 0;
+    const uint8_t* sfa_src = nullptr;
+    size_t sfb_off = 0;
+    auto place = [&] {
+      m_tile = w.tile % plan.m_tiles;
+      n_tile = w.tile / plan.m_tiles;
+      sfa_src = p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
+      sfb_off = (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+    };
+    if (have) place();
+    if (a_side && lane == 0) NVFP4DG_STAMP(1, 61);
+    named_bar_sync(kBarInit, 96);  // the mbarriers are initialised
     if (lane == 0) {
-      const bool a_side = (warp == kProdAWarp);
-      // A is read by every CTA of its row of tiles: keep it in L2 longer
-      const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      WorkIter it;
-      work_begin(plan, blockIdx.x, it);
-      Work w;
-      bool have = work_next(plan, it, w);
-      if (a_side) NVFP4DG_STAMP(1, 61);
       griddep_wait();  // global memory only after the previous grid
       if (a_side) NVFP4DG_STAMP(1, 62);
-      for (; ok && have; have = work_next(plan, it, w)) {
-        const int m_tile = w.tile % plan.m_tiles;
-        const int n_tile = w.tile / plan.m_tiles;
-        const uint8_t* sfa_src =
-            p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
-        const size_t sfb_off =
-            (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+      while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (a_side) NVFP4DG_STAMP(9, issued);
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
@@ -626,6 +651,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        if (!ok) break;
+        have = work_next(plan, it, w);
+        if (have) place();
       }
       // Never leave with copies in flight: wait (bounded) until every stage
       // has completed the fill that holds this thread's last copies.
@@ -999,7 +1027,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
   bool cluster_waited = true;  // the start-up cluster barrier (below)
 
-  if (warp == kProdAWarp && lane == 0) {
+  const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
+  // Warp 0 initialises the mbarriers while the producers work out their
+  // first item (as in the 1-SM kernel).
+  if (warp == 0 && lane == 0) {
     for (int s = 0; s < S; ++s) {
       // the scale warps of both CTAs; on the even CTA the first one's
       // arrival carries both CTAs' tile bytes
@@ -1027,19 +1058,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   // that the cluster-wide barrier completes meanwhile.
   __syncwarp();
   cluster_arrive_relaxed();
-  if (warp == kMmaWarp) {
-    tmem_alloc_pair(&tmem_base_sh, kTmemCols);
-    tmem_relinquish_pair();
+  uint32_t tmem = 0;
+  if (!producer) {
+    if (warp == 0) named_bar_arrive(kBarInit, 96);
+    if (warp == kMmaWarp) {
+      tmem_alloc_pair(&tmem_base_sh, kTmemCols);
+      tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    named_bar_sync(kBarStart, kThreads - 64);  // TMEM base, barrier inits
+    cluster_wait();
+    tc_fence_after();
+    tmem = tmem_base_sh;
   }
-  tc_fence_before();
-  __syncthreads();  // TMEM base and barrier inits visible within the CTA
-  cluster_wait();
-  tc_fence_after();
   // Each role waits for the previous grid (griddepcontrol.wait) only after
   // its own setup, so the first pass through its code overlaps that wait.
   griddep_launch_dependents();
   NVFP4DG_STAMP_NS(62);
-  const uint32_t tmem = tmem_base_sh;
   const int kblk64 = p.K / 64;
 
   if (warp == kProdAWarp || warp == kProdBWarp) {
@@ -1052,34 +1087,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (both CTAs' tiles) come with the even CTA's first scale warp's
     // arrival; scale runs land on this CTA's `sfdata` barrier, re-armed by
     // its first scale warp.
+    // First item and its addresses before meeting warp 0 (parameters only).
+    const bool a_side = (warp == kProdAWarp);
+    // A is read by every CTA of its row of tiles: keep it in L2 longer
+    const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
+    WorkIter it;
+    work_begin(plan, unit, it);
+    Work w;
+    bool have = work_next(plan, it, w);
+    int n_tile = 0, a_row = 0;
+    const uint8_t* sfa_src = nullptr;
+    size_t sfb_off = 0;
+    auto place = [&] {
+      const int m_tile = w.tile % plan.m_tiles;
+      n_tile = w.tile / plan.m_tiles;
+      a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+      // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
+      // lie wholly past M (M in (256t, 256t + 128] for the last pair tile)
+      // it copies the last block instead: its A rows are zero-filled by the
+      // tensor map and its accumulator rows are never stored.
+      const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
+                            (p.M + kBM - 1) / kBM - 1);
+      sfa_src = p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
+      sfb_off = (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+    };
+    if (have) place();
+    named_bar_sync(kBarInit, 96);  // this CTA's mbarriers are initialised
+    cluster_wait();                // and every other CTA's
     if (lane == 0) {
-      const bool a_side = (warp == kProdAWarp);
-      // A is read by every CTA of its row of tiles: keep it in L2 longer
-      const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
       const uint32_t full_c = mapa_shared(smem_u32(&full_bar[0]), lead);
       int stage = 0;
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      WorkIter it;
-      work_begin(plan, unit, it);
-      Work w;
-      bool have = work_next(plan, it, w);
       griddep_wait();  // global memory only after the previous grid
-      for (; ok && have; have = work_next(plan, it, w)) {
-        const int m_tile = w.tile % plan.m_tiles;
-        const int n_tile = w.tile / plan.m_tiles;
-        const int a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
-        // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
-        // lie wholly past M (M in (256t, 256t + 128] for the last pair
-        // tile) it copies the last block instead: its A rows are zero-filled
-        // by the tensor map and its accumulator rows are never stored.
-        const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
-                              (p.M + kBM - 1) / kBM - 1);
-        const uint8_t* sfa_src =
-            p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
-        const size_t sfb_off =
-            (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+      while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
                                  kErrProducer)) {
@@ -1115,6 +1157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1u;
           }
         }
+        if (!ok) break;
+        have = work_next(plan, it, w);
+        if (have) place();
       }
       // Drain: the scale runs land on this CTA's own barrier; the A/B tiles
       // of both CTAs land on the even CTA's `full` barrier, which its warp 4
