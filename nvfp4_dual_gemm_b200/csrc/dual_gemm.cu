@@ -564,8 +564,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool cluster_waited = false;
   // Split-K: this CTA's half of K (= its cluster rank) and its tile.
   const int split_own = static_cast<int>(blockIdx.x & 1);
-  const int split_m_tile = static_cast<int>(blockIdx.x >> 1) % plan.m_tiles;
-  const int split_n_tile = static_cast<int>(blockIdx.x >> 1) / plan.m_tiles;
+  int split_m_tile, split_n_tile;
+  tile_mn(plan, static_cast<int>(blockIdx.x >> 1), split_m_tile, split_n_tile);
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -591,22 +591,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     // TMEM while the tiles are in flight.
     // First item and its addresses before meeting warp 0 (parameters only).
     const bool a_side = (warp == kProdAWarp);
+    if (a_side && lane == 0) NVFP4DG_STAMP(1, 56);
     // A is read by every CTA of its row of tiles: keep it in L2 longer
     const uint64_t pol = a_side ? kPolicyEvictLast : kPolicyEvictNormal;
     WorkIter it;
     work_begin(plan, blockIdx.x, it);
+    if (a_side && lane == 0) NVFP4DG_STAMP(1, 57);
     Work w;
     bool have = work_next(plan, it, w);
+    if (a_side && lane == 0) NVFP4DG_STAMP(1, 58);
     int m_tile = 0, n_tile = 0;
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
     auto place = [&] {
-      m_tile = w.tile % plan.m_tiles;
-      n_tile = w.tile / plan.m_tiles;
+      tile_mn(plan, w.tile, m_tile, n_tile);
       sfa_src = p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
       sfb_off = (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
     };
     if (have) place();
+    if (a_side && lane == 0) NVFP4DG_STAMP(1, 59);
     if (a_side && lane == 0) NVFP4DG_STAMP(1, 61);
     named_bar_sync(kBarInit, 96);  // the mbarriers are initialised
     if (lane == 0) {
@@ -619,7 +622,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (a_side) NVFP4DG_STAMP(9, issued);
-          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
+          // a stage's first fill needs no wait: it is free from the start
+          if (issued >= S &&
+              !mbar_wait(&empty_bar[stage], phase ^ 1u, p.err, kErrProducer)) {
             ok = false;
             break;
           }
@@ -686,7 +691,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; ok && have; have = work_next(plan, it, w)) {
       // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
-      const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
+      int m_tile, n_tile;
+      tile_mn(plan, w.tile, m_tile, n_tile);
+      const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got = mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
         if (!__all_sync(0xffffffffu, got)) {
@@ -856,8 +863,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
       tc_fence_after();
-      const int m_tile = w.tile % plan.m_tiles;
-      const int n_tile = w.tile / plan.m_tiles;
+      int m_tile, n_tile;
+      tile_mn(plan, w.tile, m_tile, n_tile);
       const int grow = m_tile * kBM + row;
       const bool row_ok = grow < p.M;
       __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
@@ -1021,8 +1028,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
   // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
   const int split_own = static_cast<int>(crank >> 1);
-  const int split_m_tile = (unit >> 1) % plan.m_tiles;
-  const int split_n_tile = (unit >> 1) / plan.m_tiles;
+  int split_m_tile, split_n_tile;
+  tile_mn(plan, unit >> 1, split_m_tile, split_n_tile);
   const int split_grow0 =
       split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
   bool cluster_waited = true;  // the start-up cluster barrier (below)
@@ -1099,8 +1106,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
     auto place = [&] {
-      const int m_tile = w.tile % plan.m_tiles;
-      n_tile = w.tile / plan.m_tiles;
+      int m_tile;
+      tile_mn(plan, w.tile, m_tile, n_tile);
       a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
       // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
       // lie wholly past M (M in (256t, 256t + 128] for the last pair tile)
@@ -1123,7 +1130,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       griddep_wait();  // global memory only after the previous grid
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
-          if (!mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
+          if (issued >= S &&
+              !mbar_wait_cluster(&empty_bar[stage], phase ^ 1u, p.err,
                                  kErrProducer)) {
             ok = false;
             break;
@@ -1190,7 +1198,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool have = work_next(plan, it, w);
     griddep_wait();  // global memory only after the previous grid
     for (; ok && have; have = work_next(plan, it, w)) {
-      const int half = (BN == 64) ? ((w.tile / plan.m_tiles) & 1) : 0;
+      int m_tile, n_tile;
+      tile_mn(plan, w.tile, m_tile, n_tile);
+      const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got =
             mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
@@ -1364,8 +1374,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit_i);
       tc_fence_after();
-      const int m_tile = w.tile % plan.m_tiles;
-      const int n_tile = w.tile / plan.m_tiles;
+      int m_tile, n_tile;
+      tile_mn(plan, w.tile, m_tile, n_tile);
       const int grow = m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
       const bool row_ok = grow < p.M;
       __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
@@ -1727,6 +1737,7 @@ Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
     p.grid = std::min(T, unit_cap);
     p.dp_tiles = T;
     p.sk_iters = 0;
+    set_tile_div(p);
     return p;
   }
   const int waves = T / unit_cap;
@@ -1735,6 +1746,7 @@ Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
   p.grid = (int)std::min<long long>(unit_cap, sk_total);
   if (p.dp_tiles > 0 && p.grid < unit_cap) p.grid = unit_cap;
   p.sk_iters = sk_total;
+  set_tile_div(p);
   return p;
 }
 
@@ -1752,6 +1764,7 @@ Plan plan_split(int M, int N, int K, int bn, int ctas = 1) {
   p.dp_tiles = p.num_tiles;
   p.sk_iters = 0;
   p.split = 2;
+  set_tile_div(p);
   return p;
 }
 

@@ -42,7 +42,38 @@ struct Plan {
   long long sk_iters;  // (num_tiles - dp_tiles) * kblocks
   int split;        // 2: the two CTAs of a cluster split each tile's K range
                     // (unit b = CTA b: tile b / 2, K half b % 2); else 0
+  // tile / m_tiles as (umulhi(tile, mt_mul) + tile) >> mt_shift (set by
+  // set_tile_div; a division by a run-time value is a long dependent chain
+  // on the producers' way to their first copy)
+  uint32_t mt_mul;
+  int mt_shift;
 };
+
+// Division by d >= 1 through a multiply-high: shift = ceil(log2 d),
+// mul = floor(2^32 (2^shift - d) / d) + 1; exact for every n < 2^31
+// (Granlund and Montgomery, "Division by invariant integers using
+// multiplication", 1994, round-up variant).
+inline void set_tile_div(Plan& p) {
+  const unsigned long long d = static_cast<unsigned long long>(p.m_tiles);
+  int shift = 0;
+  while ((1ull << shift) < d) ++shift;
+  p.mt_shift = shift;
+  p.mt_mul = static_cast<uint32_t>(((1ull << 32) * ((1ull << shift) - d)) / d +
+                                   1ull);
+}
+
+// (m_tile, n_tile) of linear tile index `tile` (m fastest).
+NVFP4DG_HD void tile_mn(const Plan& p, int tile, int& m_tile, int& n_tile) {
+  const uint32_t t = static_cast<uint32_t>(tile);
+#if defined(__CUDA_ARCH__)
+  const uint32_t hi = __umulhi(t, p.mt_mul);
+#else
+  const uint32_t hi = static_cast<uint32_t>(
+      (static_cast<unsigned long long>(t) * p.mt_mul) >> 32);
+#endif
+  n_tile = static_cast<int>((hi + t) >> p.mt_shift);
+  m_tile = tile - n_tile * p.m_tiles;
+}
 
 struct Work {
   int tile;  // linear tile index; m fastest: m = tile % m_tiles

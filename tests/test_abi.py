@@ -367,3 +367,19 @@ def test_stream_k_small_grid_search():
     flags = _lib.FLAG_FORCE_STREAMK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN128
     pl = dg.plan(256, 512, 7168, flags)
     assert pl["sk_tiles"] == 8 and pl["grid"] < 148
+
+
+def test_tile_division_by_multiply_high():
+    # Restatement of set_tile_div / tile_mn (schedule.h): the quotient of
+    # every tile index by every row-tile count the planner can produce.
+    import numpy as np
+    n = np.arange(1 << 17, dtype=np.uint64)
+    for d in list(range(1, 1025)) + [4095, 4096, 8191, 16384]:
+        shift = 0
+        while (1 << shift) < d:
+            shift += 1
+        mul = ((1 << 32) * ((1 << shift) - d)) // d + 1
+        assert 0 < mul < (1 << 32) or d == 1
+        hi = (n * np.uint64(mul)) >> np.uint64(32)
+        q = (hi + n) >> np.uint64(shift)
+        assert np.array_equal(q, n // np.uint64(d)), d
