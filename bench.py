@@ -515,6 +515,81 @@ def run_reference(args, world, rank):
     return line
 
 
+PLUMBING = {
+    "quantize": dict(rows=8192, K=7168, dtype="bfloat16",
+                     name="activation quantiser: 8192 x 7168 bf16 rows -> "
+                          "NVFP4 codes + blocked scales"),
+    "scales": dict(rows=14336, K=7168,
+                   name="scale layout converter: plain -> blocked, "
+                        "14336 x 448 scales"),
+}
+
+
+def run_plumbing(args):
+    """Time one of the kernels beside the dual GEMM (SURVEY-style 'next'
+    rows): the activation quantiser or the scale layout converter, in a
+    CUDA graph over rotating buffers larger than 2 x L2; one JSON line with
+    GB/s against the measured HBM copy bandwidth."""
+    import nvfp4_dual_gemm_b200 as dg
+    from nvfp4_dual_gemm_b200 import _lib
+
+    torch.cuda.set_device(0)
+    cfg = PLUMBING[args.plumbing]
+    rows, k = cfg["rows"], cfg["K"]
+    lib = _lib.load()
+    stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
+    blocked = ((rows + 127) // 128) * (k // 64) * 512
+    if args.plumbing == "quantize":
+        dt = getattr(torch, cfg["dtype"])
+        per = rows * k * 2 + rows * k // 2 + blocked
+        nsets = max(2, -(-2 * L2_BYTES // per))
+        xs = [torch.randn((rows, k), device="cuda").to(dt) for _ in range(nsets)]
+        codes = [torch.empty((rows, k // 2), dtype=torch.uint8, device="cuda")
+                 for _ in range(nsets)]
+        blks = [torch.empty((blocked,), dtype=torch.uint8, device="cuda")
+                for _ in range(nsets)]
+
+        def step(i):
+            j = i % nsets
+            rc = lib.nvfp4_quantize_rows(
+                xs[j].data_ptr(), _lib.DTYPE_BF16, rows, k, k,
+                codes[j].data_ptr(), None, blks[j].data_ptr(), stream())
+            assert rc == 0, _lib.last_error()
+    else:
+        per = rows * (k // 16) + blocked
+        nsets = max(2, -(-2 * L2_BYTES // per))
+        sfs = [torch.randint(0, 256, (rows, k // 16), dtype=torch.uint8,
+                             device="cuda") for _ in range(nsets)]
+        blks = [torch.empty((blocked,), dtype=torch.uint8, device="cuda")
+                for _ in range(nsets)]
+
+        def step(i):
+            j = i % nsets
+            rc = lib.nvfp4_scales_to_blocked(sfs[j].data_ptr(), rows, k,
+                                             k // 16, blks[j].data_ptr(),
+                                             stream())
+            assert rc == 0, _lib.last_error()
+    ms, clocks = time_graph(step, args.steps, args.warmup, 1)
+    us = ms * 1e3 / args.steps
+    gbs = per / (us * 1e-6) / 1e9
+    peaks = load_peaks()
+    return {
+        "metric": cfg["name"], "value": round(gbs, 1), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "us_per_call": round(us, 3),
+        "higher_is_better": True, "data": "synthetic",
+        "config": {"workload": args.plumbing, "rows": rows, "K": k,
+                   "bytes_per_call": per,
+                   "l2": f"{nsets} rotating buffer sets (> 2 x 126 MB L2)",
+                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peaks['source']} HBM copy GB/s"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawTextHelpFormatter)
@@ -529,9 +604,15 @@ def main():
     ap.add_argument("--shapes", action="store_true",
                     help="also time C2/C3/C4 and report their geomean")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--plumbing", choices=sorted(PLUMBING),
+                    help="time the activation quantiser or the scale layout "
+                         "converter instead of the dual GEMM (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.plumbing:
+        print(json.dumps(run_plumbing(args)), flush=True)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

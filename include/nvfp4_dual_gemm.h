@@ -138,6 +138,43 @@ NVFP4DG_API int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void
 NVFP4DG_API int nvfp4_quantize(const float* X, int rows, int K, void* codes,
                    void* sf_plain, void* sf_blocked, void* stream);
 
+/* Element types of nvfp4_quantize_rows's input. */
+#define NVFP4DG_DTYPE_F32 0
+#define NVFP4DG_DTYPE_F16 1
+#define NVFP4DG_DTYPE_BF16 2
+
+/*
+ * Activation quantiser (the step before the dual GEMM in an FFN): X is
+ * [rows, K] of `dtype` with a row pitch of `ldx` elements (>= K); writes the
+ * e2m1 codes [rows, K/2], the blocked scales (ceil(rows/128) * (K/64) * 512
+ * bytes, padding rows zero — every byte of the buffer is written) and, when
+ * `sf_plain` is not NULL, the plain scales [rows, K/16].  Same arithmetic
+ * as nvfp4_quantize.  K % 64 == 0; X, its row pitch, codes and sf_blocked
+ * 16-byte aligned, sf_plain 4-byte aligned.  The reference has no device
+ * quantiser: its harness quantises on the host (submission.py:1154).
+ */
+NVFP4DG_API int nvfp4_quantize_rows(const void* X, int dtype, int rows, int K,
+                                    long long ldx, void* codes,
+                                    void* sf_plain, void* sf_blocked,
+                                    void* stream);
+
+/*
+ * Scale layout conversion on the device between the plain layout
+ * [rows, K/16] (row pitch `ld` bytes >= K/16) and the blocked layout
+ * described at the top of this file (ceil(rows/128) * (K/64) * 512 bytes).
+ * to_blocked writes every byte of the blocked buffer (padding rows zero);
+ * from_blocked writes the rows x K/16 plain bytes.  K % 64 == 0; plain
+ * scales and `ld` 4-byte aligned, blocked scales 16-byte aligned.  The
+ * reference's harness builds the blocked copies on the host
+ * (submission.py:1154, the `*_blocked` fields of `data`).
+ */
+NVFP4DG_API int nvfp4_scales_to_blocked(const void* plain, int rows, int K,
+                                        long long ld, void* blocked,
+                                        void* stream);
+NVFP4DG_API int nvfp4_scales_from_blocked(const void* blocked, int rows, int K,
+                                          void* plain, long long ld,
+                                          void* stream);
+
 /*
  * Read and clear the device error word of `device` (synchronizes that
  * device).  *word_out = 0 when no kernel reported a timeout; otherwise bits

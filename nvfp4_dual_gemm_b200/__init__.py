@@ -14,6 +14,8 @@ from .api import (  # noqa: F401
     plan,
     plan_work,
     quantize_nvfp4,
+    scales_from_blocked,
+    scales_to_blocked,
     workspace_size,
 )
 from .shard import (  # noqa: F401

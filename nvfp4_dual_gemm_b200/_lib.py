@@ -36,6 +36,11 @@ FLAG_NO_SPLITK = 1 << 21
 FLAG_NO_PDL = 1 << 22
 FLAG_NO_MERGED_B = 1 << 23
 
+# Input element types of nvfp4_quantize_rows.
+DTYPE_F32 = 0
+DTYPE_F16 = 1
+DTYPE_BF16 = 2
+
 # Most weight slabs nvfp4_dual_gemm_run_host uses.
 MAX_HOST_SLABS = 16
 
@@ -56,6 +61,12 @@ SIGNATURES = {
     "nvfp4_dual_gemm_run_noalloc": (_i, [_vp] * 7 + [_i, _i, _i, _i, _u,
                                                      _vp]),
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "nvfp4_quantize_rows": (_i, [_vp, _i, _i, _i, ctypes.c_longlong, _vp, _vp,
+                                 _vp, _vp]),
+    "nvfp4_scales_to_blocked": (_i, [_vp, _i, _i, ctypes.c_longlong, _vp,
+                                     _vp]),
+    "nvfp4_scales_from_blocked": (_i, [_vp, _i, _i, _vp, ctypes.c_longlong,
+                                       _vp]),
     "nvfp4_dual_gemm_device_status": (_i, [_i, ctypes.POINTER(ctypes.c_uint)]),
     "nvfp4_dual_gemm_plan": (_i, [_i, _i, _i, _u, _i, _ip, _ip, _ip, _ip,
                                   _ip, _ip]),

@@ -32,6 +32,8 @@ __all__ = [
     "dual_gemm_host",
     "host_staging_size",
     "quantize_nvfp4",
+    "scales_to_blocked",
+    "scales_from_blocked",
     "generate_input",
     "workspace_size",
     "plan",
@@ -260,26 +262,84 @@ def plan_work(M: int, N: int, K: int, cta: int, flags: int = 0,
     return [tuple(buf[4 * i:4 * i + 4]) for i in range(n)]
 
 
-def quantize_nvfp4(x: torch.Tensor):
-    """fp32 CUDA tensor [rows, K] -> (codes [rows, K/2] uint8,
-    plain scales [rows, K/16] float8_e4m3fn, blocked scales uint8), computed
-    by the library's quantiser kernel on the current stream."""
-    if x.dtype != torch.float32 or not x.is_cuda or x.dim() != 2:
-        raise ValueError("x must be a 2-D float32 CUDA tensor")
-    x = x.contiguous()
+_QUANT_DTYPES = {torch.float32: _lib.DTYPE_F32, torch.float16: _lib.DTYPE_F16,
+                 torch.bfloat16: _lib.DTYPE_BF16}
+
+
+def quantize_nvfp4(x: torch.Tensor, plain: bool = True):
+    """Activation quantiser: a [rows, K] CUDA tensor of float32, float16 or
+    bfloat16 (rows may be strided: stride(1) == 1, the row pitch a multiple
+    of 16 bytes) -> (codes [rows, K/2] uint8, plain scales [rows, K/16]
+    float8_e4m3fn or None when ``plain`` is False, blocked scales uint8), by
+    the library's quantiser kernel on the current stream."""
+    if x.dtype not in _QUANT_DTYPES or not x.is_cuda or x.dim() != 2:
+        raise ValueError("x must be a 2-D float32 / float16 / bfloat16 CUDA "
+                         "tensor")
+    if x.stride(1) != 1 or (x.stride(0) * x.element_size()) % 16 != 0:
+        x = x.contiguous()
     rows, k = x.shape
     if k % 64 != 0:
         raise ValueError("K must be a multiple of 64")
     codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=x.device)
-    sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=x.device)
+    sf = (torch.empty((rows, k // 16), dtype=torch.uint8, device=x.device)
+          if plain else None)
     blk = torch.empty((_blocked_bytes(rows, k),), dtype=torch.uint8,
                       device=x.device)
     lib = _lib.load()
     with torch.cuda.device(x.device):
-        rc = lib.nvfp4_quantize(_ptr(x), rows, k, _ptr(codes), _ptr(sf),
-                                _ptr(blk), _stream(x.device))
-    _lib.check(rc, "nvfp4_quantize")
-    return codes, sf.view(torch.float8_e4m3fn), blk
+        rc = lib.nvfp4_quantize_rows(
+            _ptr(x), _QUANT_DTYPES[x.dtype], rows, k, max(x.stride(0), k),
+            _ptr(codes), None if sf is None else _ptr(sf), _ptr(blk),
+            _stream(x.device))
+    _lib.check(rc, "nvfp4_quantize_rows")
+    return codes, (None if sf is None else sf.view(torch.float8_e4m3fn)), blk
+
+
+def _byte_view(t: torch.Tensor) -> torch.Tensor:
+    return t.view(torch.uint8) if t.element_size() == 1 else t
+
+
+def scales_to_blocked(sf: torch.Tensor) -> torch.Tensor:
+    """Plain scales [rows, K/16] (1-byte CUDA tensor, rows may be strided:
+    stride(1) == 1, row pitch a multiple of 4 bytes) -> the blocked layout
+    the dual GEMM reads (uint8, padding rows zero), on the current stream."""
+    if not sf.is_cuda or sf.dim() != 2 or sf.element_size() != 1:
+        raise ValueError("sf must be a 2-D 1-byte CUDA tensor")
+    sf = _byte_view(sf)
+    if sf.stride(1) != 1 or sf.stride(0) % 4 != 0:
+        sf = sf.contiguous()
+    rows, kb = sf.shape
+    k = kb * 16
+    if k % 64 != 0:
+        raise ValueError("K / 16 must be a multiple of 4")
+    out = torch.empty((_blocked_bytes(rows, k),), dtype=torch.uint8,
+                      device=sf.device)
+    lib = _lib.load()
+    with torch.cuda.device(sf.device):
+        rc = lib.nvfp4_scales_to_blocked(_ptr(sf), rows, k,
+                                         max(sf.stride(0), kb), _ptr(out),
+                                         _stream(sf.device))
+    _lib.check(rc, "nvfp4_scales_to_blocked")
+    return out
+
+
+def scales_from_blocked(blocked: torch.Tensor, rows: int, k: int) -> torch.Tensor:
+    """Blocked scales (1-byte CUDA tensor) -> plain [rows, K/16] uint8, on
+    the current stream."""
+    if not blocked.is_cuda or blocked.element_size() != 1:
+        raise ValueError("blocked must be a 1-byte CUDA tensor")
+    blocked = _byte_view(blocked).contiguous()
+    if k % 64 != 0:
+        raise ValueError("K must be a multiple of 64")
+    if blocked.numel() < _blocked_bytes(rows, k):
+        raise ValueError("blocked holds fewer bytes than the layout needs")
+    out = torch.empty((rows, k // 16), dtype=torch.uint8, device=blocked.device)
+    lib = _lib.load()
+    with torch.cuda.device(blocked.device):
+        rc = lib.nvfp4_scales_from_blocked(_ptr(blocked), rows, k, _ptr(out),
+                                           k // 16, _stream(blocked.device))
+    _lib.check(rc, "nvfp4_scales_from_blocked")
+    return out
 
 
 def generate_input(m: int, n: int, k: int, l: int = 1, seed: int = 0,

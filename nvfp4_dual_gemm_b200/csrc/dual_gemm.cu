@@ -14,6 +14,7 @@
 // the scale copies and two MMAs per K step from one thread
 // (nvfp4_dual_gemm.cu:77-317); the scheduling here is in schedule.h.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -1485,48 +1486,175 @@ __device__ __forceinline__ uint32_t e2m1x8(const float* v) {
   return r;
 }
 
-__global__ void quantize_kernel(const float* __restrict__ X, int rows, int K,
-                                uint8_t* __restrict__ codes,
-                                uint8_t* __restrict__ sf_plain,
-                                uint8_t* __restrict__ sf_blocked) {
-  const int kb16 = K / 16;
-  const long long nblk = static_cast<long long>(rows) * kb16;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nblk;
-       i += (long long)gridDim.x * blockDim.x) {
-    const int r = static_cast<int>(i / kb16);
-    const int j = static_cast<int>(i - (long long)r * kb16);
-    const float4* src =
-        reinterpret_cast<const float4*>(X + (size_t)r * K + (size_t)j * 16);
-    float v[16];
+// Activation quantiser: rows of fp32 / fp16 / bf16 -> e2m1 codes and e4m3
+// block scales, written straight into the blocked layout the dual GEMM
+// reads.  One lane per (row, 64-element group): it reads 64 contiguous
+// elements (16-byte loads), writes 32 bytes of codes and the group's four
+// scales as one 32-bit word, so a warp (32 consecutive rows, one group)
+// writes 32 words of one blocked atom (row r's 16-byte atom row at
+// (r % 32) * 16, quarter (r % 128) / 32 at +4 within it).  Lanes of the
+// padding rows up to a multiple of 128 write zero scales, so no memset of
+// the blocked buffer is needed.  Arithmetic as the oracle's quantiser:
+// scale = e4m3(amax / 6) RN saturating, codes = e2m1(x / scale) RN
+// saturating (an IEEE division, as the oracle's), zero codes for a zero
+// scale.
+template <typename T>
+struct In16 {
+  // 16 consecutive elements at p (16-byte aligned) as fp32
+  static __device__ __forceinline__ void load(const T* p, float (&v)[16]);
+};
+template <>
+struct In16<float> {
+  static __device__ __forceinline__ void load(const float* p, float (&v)[16]) {
+    const float4* s = reinterpret_cast<const float4*>(p);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const float4 t = src[q];
+      const float4 t = __ldg(s + q);
       v[4 * q] = t.x;
       v[4 * q + 1] = t.y;
       v[4 * q + 2] = t.z;
       v[4 * q + 3] = t.w;
     }
-    float amax = 0.f;
+  }
+};
+template <>
+struct In16<__half> {
+  static __device__ __forceinline__ void load(const __half* p, float (&v)[16]) {
+    const uint4* s = reinterpret_cast<const uint4*>(p);
 #pragma unroll
-    for (int q = 0; q < 16; ++q) amax = fmaxf(amax, fabsf(v[q]));
-    const __nv_fp8_storage_t sb =
-        __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
-    const __half_raw hr = __nv_cvt_fp8_to_halfraw(sb, __NV_E4M3);
-    const float sd = __half2float(__half(hr));
-    uint32_t w0 = 0, w1 = 0;
-    if (sd > 0.f) {
-      float q[16];
+    for (int q = 0; q < 2; ++q) {
+      const uint4 t = __ldg(s + q);
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
 #pragma unroll
-      for (int t = 0; t < 16; ++t) q[t] = v[t] / sd;
-      w0 = e2m1x8(q);
-      w1 = e2m1x8(q + 8);
+      for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        v[8 * q + 2 * i] = f.x;
+        v[8 * q + 2 * i + 1] = f.y;
+      }
     }
-    *reinterpret_cast<uint2*>(codes + (size_t)r * (K / 2) + (size_t)j * 8) =
-        make_uint2(w0, w1);
-    if (sf_plain) sf_plain[(size_t)r * kb16 + j] = sb;
-    const size_t atom = (size_t)(r / 128) * (K / 64) + (j / 4);
-    sf_blocked[atom * kSfAtomBytes + (r % 32) * 16 + ((r % 128) / 32) * 4 +
-               (j % 4)] = sb;
+  }
+};
+template <>
+struct In16<__nv_bfloat16> {
+  static __device__ __forceinline__ void load(const __nv_bfloat16* p,
+                                              float (&v)[16]) {
+    const uint4* s = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint4 t = __ldg(s + q);
+      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[8 * q + 2 * i] = __uint_as_float(w[i] << 16);
+        v[8 * q + 2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    }
+  }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    quantize_rows_kernel(const T* __restrict__ X, int rows, int K, long long ldx,
+                         uint8_t* __restrict__ codes,
+                         uint8_t* __restrict__ sf_plain,
+                         uint8_t* __restrict__ sf_blocked) {
+  const int groups = K / 64;
+  const long long units = (long long)((rows + 127) / 128) * 4 * groups;
+  const int lane = threadIdx.x & 31;
+  for (long long u = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+       u < units; u += (long long)gridDim.x * (blockDim.x / 32)) {
+    const int g = static_cast<int>(u % groups);  // consecutive warps: along K
+    const int r = static_cast<int>(u / groups) * 32 + lane;
+    uint32_t sfw = 0;
+    if (r < rows) {
+      const T* src = X + (size_t)r * ldx + (size_t)g * 64;
+      uint8_t* dst = codes + (size_t)r * (K / 2) + (size_t)g * 32;
+#pragma unroll 1
+      for (int b = 0; b < 4; ++b) {
+        float v[16];
+        In16<T>::load(src + 16 * b, v);
+        float amax = 0.f;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) amax = fmaxf(amax, fabsf(v[q]));
+        const __nv_fp8_storage_t sb =
+            __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+        const float sd =
+            __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
+        uint32_t w0 = 0, w1 = 0;
+        if (sd > 0.f) {
+          float q[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) q[t] = v[t] / sd;
+          w0 = e2m1x8(q);
+          w1 = e2m1x8(q + 8);
+        }
+        *reinterpret_cast<uint2*>(dst + 8 * b) = make_uint2(w0, w1);
+        sfw |= static_cast<uint32_t>(sb) << (8 * b);
+      }
+      if (sf_plain)
+        *reinterpret_cast<uint32_t*>(sf_plain + (size_t)r * (K / 16) +
+                                     (size_t)g * 4) = sfw;
+    }
+    *reinterpret_cast<uint32_t*>(
+        sf_blocked + ((size_t)(r / 128) * groups + g) * kSfAtomBytes +
+        (r % 32) * 16 + ((r % 128) / 32) * 4) = sfw;
+  }
+}
+
+// Scale layout converter (plain [rows, K/16] <-> blocked).  One CTA moves
+// a 128-row block x 32 four-scale groups (16 KiB) through shared memory:
+// the plain side is read / written row by row (consecutive threads,
+// consecutive 4-byte words of a row), the blocked side as whole 512-byte
+// atoms (the 32 atoms of a row block and 32 consecutive groups are
+// contiguous), so both sides are coalesced.  Padding rows of the blocked
+// buffer are written as zero.
+constexpr int kCvtGroups = 32;
+
+__global__ void __launch_bounds__(256)
+    scales_to_blocked_kernel(const uint8_t* __restrict__ plain, int rows,
+                             int groups, long long ld,
+                             uint8_t* __restrict__ blocked) {
+  __shared__ uint32_t tile[128][kCvtGroups + 1];
+  const int rb = blockIdx.y;
+  const int g0 = blockIdx.x * kCvtGroups;
+  const int ng = min(kCvtGroups, groups - g0);
+  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+    const int r = i / ng, gg = i - r * ng;
+    const int row = rb * 128 + r;
+    tile[r][gg] = row < rows ? *reinterpret_cast<const uint32_t*>(
+                                   plain + (size_t)row * ld + 4 * (g0 + gg))
+                             : 0u;
+  }
+  __syncthreads();
+  uint32_t* out = reinterpret_cast<uint32_t*>(blocked) +
+                  ((size_t)rb * groups + g0) * (kSfAtomBytes / 4);
+  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+    const int gg = i >> 7, w = i & 127;  // word w of atom gg: row (w/4)+32(w%4)
+    out[i] = tile[(w >> 2) + 32 * (w & 3)][gg];
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    scales_from_blocked_kernel(const uint8_t* __restrict__ blocked, int rows,
+                               int groups, long long ld,
+                               uint8_t* __restrict__ plain) {
+  __shared__ uint32_t tile[128][kCvtGroups + 1];
+  const int rb = blockIdx.y;
+  const int g0 = blockIdx.x * kCvtGroups;
+  const int ng = min(kCvtGroups, groups - g0);
+  const uint32_t* in = reinterpret_cast<const uint32_t*>(blocked) +
+                       ((size_t)rb * groups + g0) * (kSfAtomBytes / 4);
+  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+    const int gg = i >> 7, w = i & 127;
+    tile[(w >> 2) + 32 * (w & 3)][gg] = in[i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+    const int r = i / ng, gg = i - r * ng;
+    const int row = rb * 128 + r;
+    if (row < rows)
+      *reinterpret_cast<uint32_t*>(plain + (size_t)row * ld + 4 * (g0 + gg)) =
+          tile[r][gg];
   }
 }
 
@@ -2579,30 +2707,99 @@ int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, int num_sms,
   return n;
 }
 
-int nvfp4_quantize(const float* X, int rows, int K, void* codes,
-                   void* sf_plain, void* sf_blocked, void* stream_ptr) {
+int nvfp4_quantize_rows(const void* X, int dtype, int rows, int K,
+                        long long ldx, void* codes, void* sf_plain,
+                        void* sf_blocked, void* stream_ptr) {
+  g_last_error.clear();
+  if (rows < 0 || K < 0 || K % 64 != 0)
+    return fail(NVFP4DG_ERR_INVALID, "rows >= 0 and K % 64 == 0 required");
+  if (dtype != NVFP4DG_DTYPE_F32 && dtype != NVFP4DG_DTYPE_F16 &&
+      dtype != NVFP4DG_DTYPE_BF16)
+    return fail(NVFP4DG_ERR_INVALID, "dtype must be F32, F16 or BF16");
+  if (rows == 0 || K == 0) return NVFP4DG_OK;
+  if (ldx < K)
+    return fail(NVFP4DG_ERR_INVALID, "ldx must be at least K");
+  if (!X || !codes || !sf_blocked)
+    return fail(NVFP4DG_ERR_INVALID, "X, codes and sf_blocked are required");
+  const size_t esize = dtype == NVFP4DG_DTYPE_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(X) % 16 || (ldx * esize) % 16 ||
+      reinterpret_cast<uintptr_t>(codes) % 16 ||
+      reinterpret_cast<uintptr_t>(sf_blocked) % 16 ||
+      reinterpret_cast<uintptr_t>(sf_plain) % 4)
+    return fail(NVFP4DG_ERR_ALIGN,
+                "X, its row pitch, codes and sf_blocked must be 16-byte "
+                "aligned, sf_plain 4-byte aligned");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long units = (long long)((rows + 127) / 128) * 4 * (K / 64);
+  const int threads = 256;
+  const long long want = (units + threads / 32 - 1) / (threads / 32);
+  const int blocks = (int)std::min<long long>(want, (long long)sms * 8);
+  uint8_t* c8 = static_cast<uint8_t*>(codes);
+  uint8_t* p8 = static_cast<uint8_t*>(sf_plain);
+  uint8_t* b8 = static_cast<uint8_t*>(sf_blocked);
+  if (dtype == NVFP4DG_DTYPE_F32)
+    quantize_rows_kernel<float><<<blocks, threads, 0, stream>>>(
+        static_cast<const float*>(X), rows, K, ldx, c8, p8, b8);
+  else if (dtype == NVFP4DG_DTYPE_F16)
+    quantize_rows_kernel<__half><<<blocks, threads, 0, stream>>>(
+        static_cast<const __half*>(X), rows, K, ldx, c8, p8, b8);
+  else
+    quantize_rows_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(X), rows, K, ldx, c8, p8, b8);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "quantize_rows_kernel launch");
+  return NVFP4DG_OK;
+}
+
+int convert_scales(const void* src, void* dst, int rows, int K, long long ld,
+                   bool to_blocked, void* stream_ptr) {
   g_last_error.clear();
   if (rows < 0 || K < 0 || K % 64 != 0)
     return fail(NVFP4DG_ERR_INVALID, "rows >= 0 and K % 64 == 0 required");
   if (rows == 0 || K == 0) return NVFP4DG_OK;
-  if (!X || !codes || !sf_blocked)
-    return fail(NVFP4DG_ERR_INVALID, "X, codes and sf_blocked are required");
-  if (reinterpret_cast<uintptr_t>(X) % 16 || reinterpret_cast<uintptr_t>(codes) % 8)
-    return fail(NVFP4DG_ERR_ALIGN, "X must be 16-byte and codes 8-byte aligned");
+  if (ld < K / 16)
+    return fail(NVFP4DG_ERR_INVALID, "ld must be at least K / 16 bytes");
+  if (!src || !dst) return fail(NVFP4DG_ERR_INVALID, "NULL buffer");
+  const void* plain = to_blocked ? src : dst;
+  const void* blk = to_blocked ? dst : src;
+  if (reinterpret_cast<uintptr_t>(plain) % 4 || ld % 4 ||
+      reinterpret_cast<uintptr_t>(blk) % 16)
+    return fail(NVFP4DG_ERR_ALIGN,
+                "plain scales and their row pitch must be 4-byte aligned, "
+                "blocked scales 16-byte aligned");
+  const int groups = K / 64;
+  const dim3 grid((groups + kCvtGroups - 1) / kCvtGroups, (rows + 127) / 128);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const size_t blocked = (size_t)((rows + 127) / 128) * (K / 64) * kSfAtomBytes;
-  cudaError_t e = cudaMemsetAsync(sf_blocked, 0, blocked, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(sf_blocked)");
-  const long long nblk = (long long)rows * (K / 16);
-  const int threads = 256;
-  const long long want = (nblk + threads - 1) / threads;
-  const int blocks = (int)std::min<long long>(want, 148LL * 16);
-  quantize_kernel<<<blocks, threads, 0, stream>>>(
-      X, rows, K, static_cast<uint8_t*>(codes),
-      static_cast<uint8_t*>(sf_plain), static_cast<uint8_t*>(sf_blocked));
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "quantize_kernel launch");
+  if (to_blocked)
+    scales_to_blocked_kernel<<<grid, 256, 0, stream>>>(
+        static_cast<const uint8_t*>(src), rows, groups, ld,
+        static_cast<uint8_t*>(dst));
+  else
+    scales_from_blocked_kernel<<<grid, 256, 0, stream>>>(
+        static_cast<const uint8_t*>(src), rows, groups, ld,
+        static_cast<uint8_t*>(dst));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "scale layout kernel launch");
   return NVFP4DG_OK;
+}
+
+int nvfp4_scales_to_blocked(const void* plain, int rows, int K, long long ld,
+                            void* blocked, void* stream) {
+  return convert_scales(plain, blocked, rows, K, ld, true, stream);
+}
+
+int nvfp4_scales_from_blocked(const void* blocked, int rows, int K,
+                              void* plain, long long ld, void* stream) {
+  return convert_scales(blocked, plain, rows, K, ld, false, stream);
+}
+
+int nvfp4_quantize(const float* X, int rows, int K, void* codes,
+                   void* sf_plain, void* sf_blocked, void* stream_ptr) {
+  return nvfp4_quantize_rows(X, NVFP4DG_DTYPE_F32, rows, K, K, codes, sf_plain,
+                             sf_blocked, stream_ptr);
 }
 
 int nvfp4_dual_gemm_device_status(int device, unsigned* word_out) {

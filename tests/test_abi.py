@@ -383,3 +383,31 @@ def test_tile_division_by_multiply_high():
         hi = (n * np.uint64(mul)) >> np.uint64(32)
         q = (hi + n) >> np.uint64(shift)
         assert np.array_equal(q, n // np.uint64(d)), d
+
+
+def test_quantize_rows_rejects_bad_arguments_without_gpu():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    q = lib.nvfp4_quantize_rows
+    assert q(p, 7, 4, 64, 64, p, None, p, None) == _lib.ERR_INVALID   # dtype
+    assert q(p, _lib.DTYPE_F16, 4, 100, 100, p, None, p, None) == _lib.ERR_INVALID
+    assert q(p, _lib.DTYPE_F16, 4, 64, 32, p, None, p, None) == _lib.ERR_INVALID
+    assert q(p, _lib.DTYPE_F16, 4, 64, 68, p, None, p, None) == _lib.ERR_ALIGN
+    assert q(ctypes.c_void_p(8), _lib.DTYPE_F32, 4, 64, 64, p, None, p,
+             None) == _lib.ERR_ALIGN
+    assert q(p, _lib.DTYPE_BF16, 4, 64, 64, None, None, p, None) == \
+        _lib.ERR_INVALID
+    assert q(None, _lib.DTYPE_F32, 0, 64, 64, None, None, None, None) == _lib.OK
+
+
+def test_scale_converter_rejects_bad_arguments_without_gpu():
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    to, back = lib.nvfp4_scales_to_blocked, lib.nvfp4_scales_from_blocked
+    assert to(p, 4, 100, 8, p, None) == _lib.ERR_INVALID     # K % 64
+    assert to(p, 4, 128, 4, p, None) == _lib.ERR_INVALID     # ld < K/16
+    assert to(p, 4, 128, 10, p, None) == _lib.ERR_ALIGN      # ld % 4
+    assert to(p, 4, 128, 8, ctypes.c_void_p(260), None) == _lib.ERR_ALIGN
+    assert back(ctypes.c_void_p(260), 4, 128, p, 8, None) == _lib.ERR_ALIGN
+    assert to(None, 4, 128, 8, p, None) == _lib.ERR_INVALID
+    assert to(None, 0, 128, 8, None, None) == _lib.OK

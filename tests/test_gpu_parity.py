@@ -407,3 +407,49 @@ def test_weight_placement_and_merged_copy(order, flags):
         outs.append(d["c"].cpu().numpy())
     assert np.array_equal(outs[0].view(np.uint16), outs[1].view(np.uint16))
     assert_close(outs[0], O.reference_output(p), f"{order} {flags:#x}")
+
+
+@pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
+@pytest.mark.parametrize("rows,k,pitch", [(300, 1024, 0), (1, 64, 0),
+                                          (129, 7168, 0), (77, 512, 640)])
+def test_activation_quantizer_dtypes_and_pitch(dtype, rows, k, pitch):
+    # fp32 / fp16 / bf16 rows (optionally inside a wider row pitch) quantised
+    # on the GPU: bit-exact against the oracle applied to the same values
+    # widened to fp32; the padding rows of the blocked buffer are zero.
+    rng = np.random.default_rng(rows + k)
+    x = (rng.standard_normal((rows, max(k, pitch))) *
+         rng.choice([1e-3, 1.0, 30.0], size=(rows, 1))).astype(np.float32)
+    x[0, :16] = 0.0
+    tdt = getattr(torch, dtype)
+    xt = torch.from_numpy(x).to(tdt).cuda()[:, :k]
+    x32 = xt.float().cpu().numpy()
+    codes, sf = O.quantize(x32)
+    gc, gsf, gblk = dg.quantize_nvfp4(xt)
+    torch.cuda.synchronize()
+    assert np.array_equal(gc.cpu().numpy(), codes)
+    assert np.array_equal(gsf.view(torch.uint8).cpu().numpy(), sf)
+    assert np.array_equal(gblk.cpu().numpy(), O.to_blocked(sf))
+    # without the plain scales
+    gc2, none, gblk2 = dg.quantize_nvfp4(xt, plain=False)
+    torch.cuda.synchronize()
+    assert none is None
+    assert np.array_equal(gblk2.cpu().numpy(), gblk.cpu().numpy())
+
+
+@pytest.mark.parametrize("rows,k,pitch", [(300, 1024, 0), (1, 64, 0),
+                                          (128, 7168, 0), (129, 4160, 0),
+                                          (77, 512, 48)])
+def test_scale_layout_converter(rows, k, pitch):
+    # plain -> blocked and back on the device, against the oracle's layout
+    # functions; a pitched plain buffer (a slice of wider rows) included
+    rng = np.random.default_rng(rows * 7 + k)
+    kb = k // 16
+    wide = rng.integers(0, 256, size=(rows, max(kb, pitch)), dtype=np.uint8)
+    sf = torch.from_numpy(wide).cuda()[:, :kb]
+    blk = dg.scales_to_blocked(sf)
+    torch.cuda.synchronize()
+    want = O.to_blocked(wide[:, :kb])
+    assert np.array_equal(blk.cpu().numpy(), want)
+    back = dg.scales_from_blocked(blk, rows, k)
+    torch.cuda.synchronize()
+    assert np.array_equal(back.cpu().numpy(), wide[:, :kb])
