@@ -522,6 +522,9 @@ PLUMBING = {
     "scales": dict(rows=14336, K=7168,
                    name="scale layout converter: plain -> blocked, "
                         "14336 x 448 scales"),
+    "nvfp4_out": dict(rows=256, K=7168, N=4096,
+                      name="dual GEMM with NVFP4 output (C2 256x4096x7168): "
+                           "fused quantising epilogue vs fp16 C + quantiser"),
 }
 
 
@@ -539,6 +542,8 @@ def run_plumbing(args):
     lib = _lib.load()
     stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
     blocked = ((rows + 127) // 128) * (k // 64) * 512
+    if args.plumbing == "nvfp4_out":
+        return run_nvfp4_out(args, cfg)
     if args.plumbing == "quantize":
         dt = getattr(torch, cfg["dtype"])
         per = rows * k * 2 + rows * k // 2 + blocked
@@ -585,6 +590,62 @@ def run_plumbing(args):
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "peak_source": f"{peaks['source']} HBM copy GB/s"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
+def run_nvfp4_out(args, cfg):
+    """The dual GEMM emitting NVFP4 (codes + blocked scales of fp16(h)) for
+    the next GEMM: the fused epilogue (one launch) against the unfused
+    sequence (fp16 C, then the activation quantiser over C), both graph-timed
+    over the same rotating input sets."""
+    import nvfp4_dual_gemm_b200 as dg
+    from nvfp4_dual_gemm_b200 import _lib
+
+    lib = _lib.load()
+    m, n, k = cfg["rows"], cfg["N"], cfg["K"]
+    wl = WORKLOADS["c2"]
+    sets, nsets = make_sets(dg, m, n, k, wl, 0)
+    cq = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
+    sfc = torch.empty((((m + 127) // 128) * (n // 64) * 512,),
+                      dtype=torch.uint8, device="cuda")
+
+    def fused(i):
+        d = sets[i % nsets]
+        dg.dual_gemm_nvfp4(d[0], d[1], d[2], d[6], d[7], d[8], cq, sfc)
+
+    def unfused(i):
+        d = sets[i % nsets]
+        dg.dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9])
+        rc = lib.nvfp4_quantize_rows(
+            d[9].data_ptr(), _lib.DTYPE_F16, m, n, n, cq.data_ptr(), None,
+            sfc.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        assert rc == 0, _lib.last_error()
+
+    ms_f, clocks = time_graph(fused, args.steps, args.warmup, 1)
+    ms_u, _ = time_graph(unfused, args.steps, args.warmup, 1)
+    us_f = ms_f * 1e3 / args.steps
+    us_u = ms_u * 1e3 / args.steps
+    tflops = algo_flops(m, n, k) / (us_f * 1e-6) / 1e12
+    peaks = load_peaks()
+    # bytes: the inputs plus the NVFP4 output (codes + scales) instead of C
+    byts = algo_bytes(m, n, k) - 2 * m * n + m * n // 2 + sfc.numel()
+    gbs = byts / (us_f * 1e-6) / 1e9
+    return {
+        "metric": cfg["name"], "value": round(tflops, 3), "unit": "TFLOP/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_f / args.steps, "us_per_call": round(us_f, 3),
+        "unfused_us_per_call": round(us_u, 3),
+        "higher_is_better": True, "data": "synthetic: seeded randn -> NVFP4",
+        "config": {"workload": "nvfp4_out", "M": m, "N": n, "K": k,
+                   "plan": dg.plan(m, n, k),
+                   "l2": f"{nsets} rotating input sets (> 2 x 126 MB L2)",
+                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "algorithmic_bytes": byts,
                      "peak_source": f"{peaks['source']} HBM copy GB/s"},
         "gpu_launches": args.steps, "clocks": clocks,
     }

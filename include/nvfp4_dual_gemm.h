@@ -125,6 +125,28 @@ NVFP4DG_API int nvfp4_dual_gemm_run_ws(const void* A, const void* B1, const void
                            void* stream);
 
 /*
+ * The dual GEMM with its result emitted in NVFP4 for the next GEMM of the
+ * FFN (the down projection, whose K is this N): each 16-column block of a
+ * row of the fp16 result h = fp16(silu(A B1^T) * (A B2^T)) is quantised as
+ * nvfp4_quantize_rows quantises fp16 rows — scale = e4m3(amax / 6), codes =
+ * e2m1(h / scale), round to nearest even, saturating — so the output equals
+ * quantising nvfp4_dual_gemm_run's C bit for bit.  Writes
+ *   Cq : M * N/2 bytes, row m at Cq + m * N/2 (element 2i in the low nibble)
+ *   SFC: ceil(M/128) * (N/64) * 512 bytes, the blocked layout above with
+ *        rows = M, K = N; scales of the padding rows up to a multiple of 128
+ *        are written as 0, so every byte of the buffer is written.
+ * The fp16 C is never materialised.  Same inputs, preconditions, flags and
+ * library-owned workspace as nvfp4_dual_gemm_run; Cq and SFC 16-byte
+ * aligned.  The reference writes only the fp16 C (nvfp4_dual_gemm.cu:126-193
+ * epilogue); its harness would quantise that C on the host for a following
+ * NVFP4 GEMM (submission.py:1154 builds such inputs).
+ */
+NVFP4DG_API int nvfp4_dual_gemm_run_nvfp4_out(
+    const void* A, const void* B1, const void* B2, const void* SFA,
+    const void* SFB1, const void* SFB2, void* Cq, void* SFC, int M, int N,
+    int K, int L, unsigned flags, void* stream);
+
+/*
  * Quantise fp32 rows to NVFP4 on the GPU: X is [rows, K] fp32 row-major;
  * writes codes [rows, K/2] (low nibble = even element), the plain scales
  * [rows, K/16] and the blocked scales (ceil(rows/128) * (K/64) * 512 bytes;

@@ -9,6 +9,7 @@ from .api import (  # noqa: F401
     custom_kernel,
     dual_gemm,
     dual_gemm_host,
+    dual_gemm_nvfp4,
     generate_input,
     host_staging_size,
     plan,

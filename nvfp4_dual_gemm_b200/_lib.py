@@ -60,6 +60,8 @@ SIGNATURES = {
                                                 _vp]),
     "nvfp4_dual_gemm_run_noalloc": (_i, [_vp] * 7 + [_i, _i, _i, _i, _u,
                                                      _vp]),
+    "nvfp4_dual_gemm_run_nvfp4_out": (_i, [_vp] * 8 + [_i, _i, _i, _i, _u,
+                                                       _vp]),
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "nvfp4_quantize_rows": (_i, [_vp, _i, _i, _i, ctypes.c_longlong, _vp, _vp,
                                  _vp, _vp]),

@@ -93,6 +93,19 @@ def _check_blocked(name: str, t: torch.Tensor, rows: int, k: int,
 def _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda: bool):
     """Shape, dtype and placement checks shared by both entry points;
     returns (M, N, K)."""
+    M, N, K = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda)
+    if C.dtype != torch.float16:
+        raise ValueError(f"C must be float16, got {C.dtype}")
+    where = "CUDA" if cuda else "CPU"
+    placed = C.is_cuda if cuda else C.device.type == "cpu"
+    if not placed or not C.is_contiguous():
+        raise ValueError(f"C must be a contiguous {where} tensor")
+    if C.numel() != M * N or C.size(0) != M:
+        raise ValueError(f"C has shape {tuple(C.shape)}, expected [{M}, {N}(, 1)]")
+    return M, N, K
+
+
+def _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda: bool):
     for name, t in (("A", A), ("B1", B1), ("B2", B2)):
         _check_bytes(name, t, cuda)
     M = A.size(0)
@@ -108,14 +121,6 @@ def _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda: bool):
     _check_blocked("SFA", SFA, M, K, cuda)
     _check_blocked("SFB1", SFB1, N, K, cuda)
     _check_blocked("SFB2", SFB2, N, K, cuda)
-    if C.dtype != torch.float16:
-        raise ValueError(f"C must be float16, got {C.dtype}")
-    where = "CUDA" if cuda else "CPU"
-    placed = C.is_cuda if cuda else C.device.type == "cpu"
-    if not placed or not C.is_contiguous():
-        raise ValueError(f"C must be a contiguous {where} tensor")
-    if C.numel() != M * N or C.size(0) != M:
-        raise ValueError(f"C has shape {tuple(C.shape)}, expected [{M}, {N}(, 1)]")
     return M, N, K
 
 
@@ -150,6 +155,37 @@ def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
                 workspace.numel() * workspace.element_size(), stream)
     _lib.check(rc, "nvfp4_dual_gemm_run")
     return C
+
+
+def dual_gemm_nvfp4(A, B1, B2, SFA, SFB1, SFB2, Cq=None, SFC=None, *,
+                    flags: int = 0):
+    """The dual GEMM with its result in NVFP4, for the next GEMM of an FFN:
+    returns (Cq, SFC), the e2m1 codes [M, N/2] (uint8, element 2i in the low
+    nibble) and the blocked e4m3 scales of h = fp16(silu(A B1^T) * (A B2^T)),
+    equal bit for bit to ``quantize_nvfp4`` of :func:`dual_gemm`'s C.  The
+    fp16 C is never written (``nvfp4_dual_gemm_run_nvfp4_out``).  ``Cq`` /
+    ``SFC`` are allocated on A's device when not given."""
+    M, N, K = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda=True)
+    dev = A.device
+    if Cq is None:
+        Cq = torch.empty((M, N // 2), dtype=torch.uint8, device=dev)
+    if SFC is None:
+        SFC = torch.empty(max(_blocked_bytes(M, N), 1), dtype=torch.uint8,
+                          device=dev)
+    _check_bytes("Cq", Cq, True)
+    _rows_dense("Cq", Cq, M, N // 2)
+    _check_blocked("SFC", SFC, M, N, True)
+    for name, t in (("B1", B1), ("B2", B2), ("SFA", SFA), ("SFB1", SFB1),
+                    ("SFB2", SFB2), ("Cq", Cq), ("SFC", SFC)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, A on {dev}")
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.nvfp4_dual_gemm_run_nvfp4_out(
+            _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
+            _ptr(Cq), _ptr(SFC), M, N, K, 1, flags, _stream(dev))
+    _lib.check(rc, "nvfp4_dual_gemm_run_nvfp4_out")
+    return Cq, SFC
 
 
 def host_staging_size(M: int, N: int, K: int) -> int:

@@ -71,6 +71,12 @@ struct KParams {
   const uint8_t* sfb1;
   const uint8_t* sfb2;
   __half* C;
+  // NVFP4 output (nvfp4_dual_gemm_run_nvfp4_out): when cq is not null, C is
+  // not written; instead each 16-column block of a row of fp16(silu * y) is
+  // quantised to e2m1 codes (cq, [M, N/2]) and one e4m3 scale in the
+  // blocked layout (sfc, ceil(M/128) * (N/64) * 512 bytes)
+  uint8_t* cq;
+  uint8_t* sfc;
   float* partials;
   int* counters;
   unsigned* err;
@@ -168,6 +174,72 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// One 16-element block -> NVFP4: returns the e4m3 scale byte
+// e4m3(amax / 6) (round to nearest even, saturating at 448) and sets w0/w1
+// to the eight bytes of e2m1 codes of q = RN(v / scale) rounded to the e2m1
+// grid (nearest, ties to the even code, saturating at 6, sign kept), all-zero
+// codes when the scale is 0.  The activation quantiser and the NVFP4-output
+// epilogue both use it, so the fused output equals quantising the fp16
+// result.
+//
+// No division: the e2m1 code of q only depends on how q compares with the
+// grid midpoints t in {0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5}, and
+// RN(v / s) < t  <=>  v < t * s  (and = <=> =) for every fp32 v and e4m3
+// scale s.  t * s has at most 7 significant bits, so it is exact; and with
+// s = b 2^e, 1 <= b < 2, t = a 2^f, 1 <= a < 2, the fp32 neighbours of
+// t * s lie more than s * ulp(t) / 2 away from it (their spacing is at least
+// 2^(e+f-23) > b 2^(e+f-24)), so no v other than t * s has a quotient that
+// rounds onto t.  Ties at 0.25, 1.25, 2.5, 5 go down (strict >), those at
+// 0.75, 1.75, 3.5 up (>=, written as > the float just below).  With an
+// IEEE division per element instead, the NVFP4-output epilogue took 18.5
+// instead of 15.2 us on the 256 x 4096 x 7168 problem.
+__device__ __forceinline__ uint8_t quant_block16(const float* v, uint32_t& w0,
+                                                 uint32_t& w1) {
+  float amax = 0.f;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) amax = fmaxf(amax, fabsf(v[q]));
+  const __nv_fp8_storage_t sb =
+      __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+  const float sd =
+      __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
+  w0 = 0;
+  w1 = 0;
+  if (sd > 0.f) {
+    auto below = [](float x) { return __uint_as_float(__float_as_uint(x) - 1u); };
+    const float t0 = 0.25f * sd, t1 = below(0.75f * sd), t2 = 1.25f * sd,
+                t3 = below(1.75f * sd), t4 = 2.5f * sd, t5 = below(3.5f * sd),
+                t6 = 5.0f * sd;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      // the number of midpoints below |v| (t0 < t1 < ... < t6), by a
+      // three-level binary search
+      const float a = fabsf(v[i]);
+      const bool b2 = a > t3;
+      const bool b1 = a > (b2 ? t5 : t1);
+      const bool b0 = a > (b2 ? (b1 ? t6 : t4) : (b1 ? t2 : t0));
+      const uint32_t m = (b2 ? 4u : 0u) | (b1 ? 2u : 0u) | (b0 ? 1u : 0u);
+      const uint32_t code = m | ((__float_as_uint(v[i]) >> 28) & 8u);
+      if (i < 8)
+        w0 |= code << (4 * i);
+      else
+        w1 |= code << (4 * (i - 8));
+    }
+  }
+  return static_cast<uint8_t>(sb);
+}
+
+// Where the epilogue of one tile row writes its outputs: fp16 C, or NVFP4
+// codes and blocked scales (KParams::cq).  `col0` is the tile's first column.
+struct OutRow {
+  __half* c;    // fp16: row `grow` of C at column col0
+  uint8_t* q;   // NVFP4: the row's codes at column col0
+  uint8_t* sf;  // NVFP4: the row's scale byte in atom 0 of its row block
+  int col0;
+  bool row_ok;  // grow < M: values / codes are stored
+  bool sf_ok;   // grow < M rounded up to 128: scale bytes are stored (the
+                // padding rows' scales are 0, their accumulators being 0)
+};
+
 // 32 outputs of one row -> 64 contiguous bytes of C.
 // fp16(silu(x) * y) of 16 columns -> 32 bytes at dst (16-byte aligned).
 __device__ __forceinline__ void store_row16(__half* dst, const float (&x)[16],
@@ -203,6 +275,64 @@ __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
     v.w = pack_half2(silu_mul(x[8 * q + 6], y[8 * q + 6]),
                      silu_mul(x[8 * q + 7], y[8 * q + 7]));
     d[q] = v;
+  }
+}
+
+__device__ __forceinline__ OutRow out_row(const KParams& p, int grow,
+                                          int col0) {
+  OutRow o;
+  o.col0 = col0;
+  o.row_ok = grow < p.M;
+  if (p.cq != nullptr) {
+    o.c = nullptr;
+    o.q = p.cq + (size_t)grow * (p.N / 2) + col0 / 2;
+    o.sf = p.sfc + (size_t)(grow / 128) * (p.N / 64) * kSfAtomBytes +
+           (grow % 32) * 16 + ((grow % 128) / 32) * 4;
+    o.sf_ok = grow < (p.M + 127) / 128 * 128;
+  } else {
+    o.c = p.C + (size_t)grow * p.N + col0;
+    o.q = nullptr;
+    o.sf = nullptr;
+    o.sf_ok = false;
+  }
+  return o;
+}
+
+// NVFP4 output of tile columns [cc, cc + 16) of one row: fp16(silu(x) * y)
+// quantised as one block.
+__device__ __forceinline__ void quant_store16(const OutRow& o, int cc,
+                                              const float* x,
+                                              const float* y) {
+  float h[16];  // the values the fp16 output would hold
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    h[i] = __half2float(__float2half_rn(silu_mul(x[i], y[i])));
+  uint32_t w0, w1;
+  const uint8_t sb = quant_block16(h, w0, w1);
+  const int col = o.col0 + cc;
+  if (o.row_ok) *reinterpret_cast<uint2*>(o.q + cc / 2) = make_uint2(w0, w1);
+  if (o.sf_ok) o.sf[(col / 64) * kSfAtomBytes + (col / 16) % 4] = sb;
+}
+
+// Outputs of tile columns [cc, cc + 16) / [cc, cc + 32) of one row.
+__device__ __forceinline__ void emit16(const OutRow& o, int cc,
+                                       const float (&x)[16],
+                                       const float (&y)[16]) {
+  if (o.q == nullptr) {
+    if (o.row_ok) store_row16(o.c + cc, x, y);
+  } else {
+    quant_store16(o, cc, x, y);
+  }
+}
+
+__device__ __forceinline__ void emit32(const OutRow& o, int cc,
+                                       const float (&x)[32],
+                                       const float (&y)[32]) {
+  if (o.q == nullptr) {
+    if (o.row_ok) store_row32(o.c + cc, x, y);
+  } else {
+    quant_store16(o, cc, x, y);
+    quant_store16(o, cc + 16, x + 16, y + 16);
   }
 }
 
@@ -264,7 +394,7 @@ template <int BN, typename SlotPtr, typename ArriveEmpty>
 __device__ __forceinline__ void sk_owner_fixup(
     uint8_t* stage, uint64_t* fix_bar, int b_first, int b_last,
     SlotPtr slot_ptr, ArriveEmpty arrive_empty, uint32_t t_row, int row,
-    bool row_ok, __half* crow, unsigned* err) {
+    const OutRow& out, unsigned* err) {
   const int nb = b_last - b_first;
   const int n_items = (BN / 32) * nb;
   uint64_t pol = 0;
@@ -329,7 +459,7 @@ __device__ __forceinline__ void sk_owner_fixup(
         issue(i + kFixSlots);
       }
     }
-    if (row_ok) store_row32(crow + 32 * c, x, y);
+    emit32(out, 32 * c, x, y);
     if (threadIdx.x == 0) NVFP4DG_STAMP(4, 41 + c);
   }
   // After a timeout, copies may still be in flight: let them land (bounded)
@@ -386,8 +516,7 @@ __device__ __forceinline__ void split_epilogue(
   const int row = 32 * (warp % 4) + lane;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16);
   const int grow = grow0 + row;
-  const bool row_ok = grow < p.M;
-  __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+  const OutRow out = out_row(p, grow, n_tile * BN);
 
   griddep_wait();  // global memory only after the previous grid
   bool ok = mbar_wait(acc_full_bar, 0, p.err, kErrEpilogue);
@@ -475,7 +604,7 @@ __device__ __forceinline__ void split_epilogue(
     }
     // after an expired wait the values are stale but every access stays in
     // bounds; the error word reports it
-    if (row_ok) store_row16(crow + own * kHalf + 16 * c, ox[i], oy[i]);
+    emit16(out, own * kHalf + 16 * c, ox[i], oy[i]);
   }
   split_group_all(all_ok);  // every participant finishes the tile together
   tc_fence_before();
@@ -867,8 +996,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_tile, n_tile;
       tile_mn(plan, w.tile, m_tile, n_tile);
       const int grow = m_tile * kBM + row;
-      const bool row_ok = grow < p.M;
-      __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+      const OutRow out = out_row(p, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -881,7 +1009,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             mbar_arrive(&acc_empty_bar);
           }
-          if (row_ok) store_row32(crow + 32 * c, x, y);
+          emit32(out, 32 * c, x, y);
         }
       } else {
         // A stream-K tile shared by CTAs b_first..b_last.  Its first K
@@ -932,7 +1060,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tc_fence_before();
                 mbar_arrive(&acc_empty_bar);
               },
-              t_row, row, row_ok, crow, p.err);
+              t_row, row, out, p.err);
         }
       }
       if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit);
@@ -1378,8 +1506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int m_tile, n_tile;
       tile_mn(plan, w.tile, m_tile, n_tile);
       const int grow = m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
-      const bool row_ok = grow < p.M;
-      __half* crow = p.C + (size_t)grow * p.N + (size_t)n_tile * BN;
+      const OutRow out = out_row(p, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -1393,7 +1520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc_empty_c);
           }
-          if (row_ok) store_row32(crow + 32 * c, x, y);
+          emit32(out, 32 * c, x, y);
         }
       } else {
         // Stream-K tile shared by units b_first..b_last: as in the 1-SM
@@ -1446,7 +1573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(acc_empty_c);
               },
-              t_row, row, row_ok, crow, p.err);
+              t_row, row, out, p.err);
         }
       }
       if (threadIdx.x == 0) NVFP4DG_STAMP(5, unit_i);
@@ -1469,23 +1596,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 // NVFP4 quantiser (fp32 rows -> e2m1 codes + e4m3 block scales)
 // ===========================================================================
-// Eight fp32 values -> four bytes of e2m1 pairs (round to nearest even,
-// saturating at +-6).  cvt...e2m1x2 puts its first source operand in the high
-// nibble, so the odd element goes first and element 2i lands in the low nibble.
-__device__ __forceinline__ uint32_t e2m1x8(const float* v) {
-  uint32_t r;
-  asm("{\n\t.reg .b8 q0, q1, q2, q3;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 q0, %2, %1;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 q1, %4, %3;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 q2, %6, %5;\n\t"
-      "cvt.rn.satfinite.e2m1x2.f32 q3, %8, %7;\n\t"
-      "mov.b32 %0, {q0, q1, q2, q3};\n\t}"
-      : "=r"(r)
-      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]),
-        "f"(v[6]), "f"(v[7]));
-  return r;
-}
-
 // Activation quantiser: rows of fp32 / fp16 / bf16 -> e2m1 codes and e4m3
 // block scales, written straight into the blocked layout the dual GEMM
 // reads.  One lane per (row, 64-element group): it reads 64 contiguous
@@ -1573,21 +1683,8 @@ __global__ void __launch_bounds__(256)
       for (int b = 0; b < 4; ++b) {
         float v[16];
         In16<T>::load(src + 16 * b, v);
-        float amax = 0.f;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) amax = fmaxf(amax, fabsf(v[q]));
-        const __nv_fp8_storage_t sb =
-            __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
-        const float sd =
-            __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
-        uint32_t w0 = 0, w1 = 0;
-        if (sd > 0.f) {
-          float q[16];
-#pragma unroll
-          for (int t = 0; t < 16; ++t) q[t] = v[t] / sd;
-          w0 = e2m1x8(q);
-          w1 = e2m1x8(q + 8);
-        }
+        uint32_t w0, w1;
+        const uint8_t sb = quant_block16(v, w0, w1);
         *reinterpret_cast<uint2*>(dst + 8 * b) = make_uint2(w0, w1);
         sfw |= static_cast<uint32_t>(sb) << (8 * b);
       }
@@ -2076,7 +2173,8 @@ template <int BN, bool PAIR>
 int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
            const void* B1, const void* B2, const void* SFA, const void* SFB1,
            const void* SFB2, void* C, int M, int N, int K, void* ws,
-           unsigned flags, cudaStream_t stream) {
+           unsigned flags, cudaStream_t stream, void* cq = nullptr,
+           void* sfc = nullptr) {
   constexpr int kSmem = PAIR ? PairCfg<BN>::kSmemBytes : Cfg<BN>::kSmemBytes;
   auto kernel = PAIR ? dual_gemm_pair_kernel<BN> : dual_gemm_kernel<BN>;
   bool& attr = PAIR ? (BN == 64 ? dev.attr64p : dev.attr128p)
@@ -2111,6 +2209,8 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.sfb1 = static_cast<const uint8_t*>(SFB1);
   kp.sfb2 = static_cast<const uint8_t*>(SFB2);
   kp.C = static_cast<__half*>(C);
+  kp.cq = static_cast<uint8_t*>(cq);
+  kp.sfc = static_cast<uint8_t*>(sfc);
   kp.counters = static_cast<int*>(ws);
   kp.partials = ws ? reinterpret_cast<float*>(static_cast<uint8_t*>(ws) +
                                               workspace_partials_offset(plan))
@@ -2169,20 +2269,37 @@ int read_status(int dev, unsigned* word) {
   return rc;
 }
 
+// `cq` / `sfc` not null: NVFP4 output (codes and blocked scales) instead of
+// the fp16 C, which is then unused (nvfp4_dual_gemm_run_nvfp4_out).
 int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
              const void* SFB1, const void* SFB2, void* C, int M, int N, int K,
              int L, unsigned flags, void* ws, size_t ws_bytes, bool own_ws,
-             void* stream_ptr) {
+             void* stream_ptr, void* cq = nullptr, void* sfc = nullptr) {
   g_last_error.clear();
-  int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags);
+  const bool q_out = cq != nullptr || sfc != nullptr;
+  int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, q_out ? cq : C, M, N, K,
+                         L, flags);
   if (rc) return rc;
+  if (q_out && M > 0 && N > 0) {
+    if (sfc == nullptr) return fail(NVFP4DG_ERR_INVALID, "SFC is NULL");
+    if (reinterpret_cast<uintptr_t>(sfc) % 16 != 0)
+      return fail(NVFP4DG_ERR_ALIGN, "SFC is not 16-byte aligned");
+  }
   if (M == 0 || N == 0) return NVFP4DG_OK;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   if (K == 0) {  // empty sums: silu(0) * 0 = 0
-    cudaError_t e =
-        cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
+    cudaError_t e;
+    if (q_out) {
+      e = cudaMemsetAsync(cq, 0, (size_t)M * (N / 2), stream);
+      if (e == cudaSuccess)
+        e = cudaMemsetAsync(sfc, 0, (size_t)(M + 127) / 128 * (N / 64) * 512,
+                            stream);
+    } else {
+      e = cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
+    }
     return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "cudaMemsetAsync");
   }
+  if (q_out) C = nullptr;
   std::lock_guard<std::mutex> lock(g_mu);
   int devid = 0;
   cudaError_t e = cudaGetDevice(&devid);
@@ -2226,16 +2343,16 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   }
   if (plan.ctas == 2 && plan.bn == 128)
     rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, flags, stream);
+                           N, K, ws, flags, stream, cq, sfc);
   else if (plan.ctas == 2)
     rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                          N, K, ws, flags, stream);
+                          N, K, ws, flags, stream, cq, sfc);
   else if (plan.bn == 128)
     rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, flags, stream);
+                            M, N, K, ws, flags, stream, cq, sfc);
   else
     rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                           M, N, K, ws, flags, stream);
+                           M, N, K, ws, flags, stream, cq, sfc);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;
@@ -2536,6 +2653,19 @@ int nvfp4_dual_gemm_run(const void* A, const void* B1, const void* B2,
                         void* stream) {
   return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, nullptr, 0,
                   true, stream);
+}
+
+int nvfp4_dual_gemm_run_nvfp4_out(const void* A, const void* B1,
+                                  const void* B2, const void* SFA,
+                                  const void* SFB1, const void* SFB2,
+                                  void* Cq, void* SFC, int M, int N, int K,
+                                  int L, unsigned flags, void* stream) {
+  if (Cq == nullptr && M > 0 && N > 0) {
+    g_last_error.clear();
+    return fail(NVFP4DG_ERR_INVALID, "Cq is NULL");
+  }
+  return run_impl(A, B1, B2, SFA, SFB1, SFB2, nullptr, M, N, K, L, flags,
+                  nullptr, 0, true, stream, Cq, SFC);
 }
 
 size_t nvfp4_dual_gemm_host_staging_size(int M, int N, int K, int L) {

@@ -151,3 +151,53 @@ def test_make_problem_is_deterministic():
 def test_check_close_rejects_nan(bad):
     ok, n, _ = O.check_close(np.array([bad], np.float16), np.array([1], np.float16))
     assert not ok and n == 1
+
+
+def _threshold_codes(v, sd):
+    """The division-free e2m1 encoding the CUDA quantiser uses
+    (quant_block16 in csrc/dual_gemm.cu): locate |v| among the exact
+    products t * sd of the grid midpoints by binary search, ties at
+    0.75 / 1.75 / 3.5 going up (> the float just below)."""
+    v = np.asarray(v, dtype=np.float32)
+    sd = np.float32(sd)
+    below = lambda x: (np.float32(x).view(np.uint32) - np.uint32(1)).view(
+        np.float32)
+    ts = [np.float32(0.25) * sd, below(np.float32(0.75) * sd),
+          np.float32(1.25) * sd, below(np.float32(1.75) * sd),
+          np.float32(2.5) * sd, below(np.float32(3.5) * sd),
+          np.float32(5.0) * sd]
+    a = np.abs(v)
+    assert all(x < y for x, y in zip(ts, ts[1:]))
+    # the kernel's three-level binary search over the increasing midpoints
+    b2 = a > ts[3]
+    b1 = a > np.where(b2, ts[5], ts[1])
+    b0 = a > np.where(b2, np.where(b1, ts[6], ts[4]),
+                      np.where(b1, ts[2], ts[0]))
+    m = (4 * b2 + 2 * b1 + b0).astype(np.uint8)
+    return (m | np.where(np.signbit(v), 8, 0)).astype(np.uint8)
+
+
+def test_division_free_e2m1_encoding_equals_division():
+    # For every positive e4m3 scale: values on and around each midpoint
+    # t * sd (a few float32 steps either side), around the grid points, and
+    # random fp16-representable values (the fused epilogue quantises fp16
+    # results), signed.  The kernel's comparison form must give the code of
+    # e2m1(RN(v / sd)) exactly.
+    rng = np.random.default_rng(0)
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    grid = O.E2M1_VALUES[:8]
+    for b in range(1, 0x7F):
+        sd = O.e4m3_decode(np.uint8(b))
+        centres = np.concatenate([mids, grid, [6.0, 7.0, 100.0]]) * sd
+        steps = np.arange(-4, 5, dtype=np.int64)
+        near = (centres.astype(np.float32).view(np.int32)[:, None] +
+                steps[None, :]).astype(np.int32).view(np.float32).ravel()
+        rand = (rng.standard_normal(512).astype(np.float32) * 3 * sd)
+        rand = rand.astype(np.float16).astype(np.float32)
+        v = np.concatenate([near, rand, [0.0, np.inf]]).astype(np.float32)
+        v = np.concatenate([v, -v])
+        with np.errstate(over="ignore", invalid="ignore"):
+            want = O.e2m1_encode(v / sd)
+        got = _threshold_codes(v, sd)
+        bad = np.flatnonzero(got != want)
+        assert bad.size == 0, (b, v[bad[:4]], got[bad[:4]], want[bad[:4]])
