@@ -13,15 +13,22 @@
  * layout the reference kernel reads (nvfp4_dual_gemm.cu:226-243: atom index
  * rowblock * (K/64) + kblock64, 512 bytes per atom).
  *
- * Buffer sizes the caller provides (L = 1):
+ * Buffer sizes the caller provides per batch (L problems of one shape, one
+ * after another in memory; L = 1 for a single problem):
  *   A    : M * K/2 bytes        row m at A  + m * K/2
  *   B1,B2: N * K/2 bytes        row n at B1 + n * K/2
  *   SFA  : ceil(M/128) * (K/64) * 512 bytes   (blocked, rows padded to 128)
  *   SFB1, SFB2: ceil(N/128) * (K/64) * 512 bytes
  *   C    : M * N fp16, row-major (row m at C + m * N)
+ * Batch l of each tensor starts l times its per-batch size after batch 0:
+ * the layout of the reference's [rows, cols, L] tensors, which are
+ * [L, rows, cols] tensors viewed through permute(1, 2, 0).  The reference
+ * kernel reads batch 0 only (its L dimension is ignored); here every batch
+ * is computed, all batches' tiles scheduled in one launch.
  *
  * Preconditions (checked, an error code is returned otherwise):
- *   M >= 0, N >= 0, K >= 0; N % 64 == 0; K % 256 == 0; L == 1;
+ *   M >= 0, N >= 0, K >= 0; N % 64 == 0; K % 256 == 0; L >= 1 (L == 1 for
+ *   nvfp4_dual_gemm_run_noalloc and the host-buffer entry point);
  *   A, B1, B2, SFA, SFB1, SFB2, C 16-byte aligned.
  * M needs no alignment: rows past M are read as zeros and never written.
  *
@@ -48,7 +55,7 @@ extern "C" {
 
 /* Status codes. */
 #define NVFP4DG_OK 0
-#define NVFP4DG_ERR_INVALID 1     /* bad shape / null pointer / L != 1      */
+#define NVFP4DG_ERR_INVALID 1     /* bad shape / null pointer / bad L       */
 #define NVFP4DG_ERR_ALIGN 2       /* pointer not 16-byte aligned            */
 #define NVFP4DG_ERR_WORKSPACE 3   /* workspace missing or too small         */
 #define NVFP4DG_ERR_CUDA 4        /* CUDA runtime / driver call failed      */

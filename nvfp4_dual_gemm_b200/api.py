@@ -60,19 +60,31 @@ def _check_bytes(name: str, t: torch.Tensor, cuda: bool = True) -> None:
                          "tensor")
 
 
-def _rows_dense(name: str, t: torch.Tensor, rows: int, row_bytes: int) -> None:
+def _batches(t: torch.Tensor) -> int:
+    """L of a [rows, cols] or [rows, cols, L] operand."""
+    return t.size(2) if t.dim() == 3 else 1
+
+
+def _rows_dense(name: str, t: torch.Tensor, rows: int, row_bytes: int,
+                L: int = 1) -> None:
+    """[rows, row_bytes] or [rows, row_bytes, L]: rows dense and K-major; a
+    batch (L > 1) stored batch after batch (``t.movedim(-1, 0)`` contiguous,
+    the layout of a [L, rows, row_bytes] tensor viewed through
+    ``permute(1, 2, 0)``, as the reference's harness builds its tensors)."""
     if t.dim() not in (2, 3):
         raise ValueError(f"{name} must be [rows, K/2] or [rows, K/2, L]")
-    if t.dim() == 3 and t.size(2) != 1:
-        raise ValueError(f"{name}: L must be 1 (batched problems are not "
-                         "supported)")
+    if _batches(t) != L:
+        raise ValueError(f"{name} holds {_batches(t)} batches, A holds {L}")
     if t.size(0) != rows or t.size(1) != row_bytes:
         raise ValueError(f"{name} has shape {tuple(t.shape)}, expected "
-                         f"[{rows}, {row_bytes}(, 1)]")
+                         f"[{rows}, {row_bytes}(, {L})]")
     if rows > 1 and row_bytes > 0 and t.stride(0) != row_bytes:
         raise ValueError(f"{name} rows must be dense (stride(0) == K/2)")
     if row_bytes > 1 and t.stride(1) != 1:
         raise ValueError(f"{name} must be K-major (stride(1) == 1)")
+    if L > 1 and rows * row_bytes > 0 and t.stride(2) != rows * row_bytes:
+        raise ValueError(f"{name}: the batches must follow one another "
+                         f"(stride(2) == {rows * row_bytes})")
 
 
 def _blocked_bytes(rows: int, k: int) -> int:
@@ -80,29 +92,45 @@ def _blocked_bytes(rows: int, k: int) -> int:
 
 
 def _check_blocked(name: str, t: torch.Tensor, rows: int, k: int,
-                   cuda: bool = True) -> None:
+                   cuda: bool = True, L: int = 1) -> None:
+    """Blocked scales: contiguous bytes, or for a batch (L > 1) a tensor whose
+    last dimension is the batch, stored batch after batch; each batch holds
+    the blocked layout of its rows."""
     _check_bytes(name, t, cuda)
     need = _blocked_bytes(rows, k)
-    if not t.is_contiguous():
-        raise ValueError(f"{name} must be contiguous")
-    if t.numel() < need:
+    dense = t.is_contiguous() or (
+        L > 1 and t.dim() >= 2 and t.size(-1) == L and
+        t.movedim(-1, 0).is_contiguous())
+    if not dense:
+        raise ValueError(f"{name} must be contiguous (batch after batch)")
+    if L > 1 and not t.is_contiguous() and t.numel() != L * need:
+        raise ValueError(f"{name} holds {t.numel()} bytes, {L} batches of the "
+                         f"blocked layout need {L * need}")
+    if t.numel() < L * need:
         raise ValueError(f"{name} holds {t.numel()} bytes, the blocked layout "
-                         f"needs {need}")
+                         f"needs {L * need}")
 
 
 def _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda: bool):
     """Shape, dtype and placement checks shared by both entry points;
     returns (M, N, K)."""
-    M, N, K = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda)
+    M, N, K, L = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda)
     if C.dtype != torch.float16:
         raise ValueError(f"C must be float16, got {C.dtype}")
     where = "CUDA" if cuda else "CPU"
     placed = C.is_cuda if cuda else C.device.type == "cpu"
-    if not placed or not C.is_contiguous():
-        raise ValueError(f"C must be a contiguous {where} tensor")
-    if C.numel() != M * N or C.size(0) != M:
-        raise ValueError(f"C has shape {tuple(C.shape)}, expected [{M}, {N}(, 1)]")
-    return M, N, K
+    batch_major = C.is_contiguous() or (
+        L > 1 and C.dim() == 3 and C.movedim(-1, 0).is_contiguous())
+    if not placed or not batch_major:
+        raise ValueError(f"C must be a contiguous {where} tensor "
+                         "(batch after batch)")
+    if C.numel() != L * M * N or C.size(0) != M or \
+            (C.dim() == 3 and C.size(2) != L):
+        raise ValueError(f"C has shape {tuple(C.shape)}, expected "
+                         f"[{M}, {N}(, {L})]")
+    if L > 1 and C.dim() != 3:
+        raise ValueError(f"C must be [{M}, {N}, {L}] for a batch")
+    return M, N, K, L
 
 
 def _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda: bool):
@@ -111,17 +139,20 @@ def _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda: bool):
     M = A.size(0)
     N = B1.size(0)
     K = 2 * A.size(1) if A.dim() >= 2 else 0
-    _rows_dense("A", A, M, K // 2)
-    _rows_dense("B1", B1, N, K // 2)
-    _rows_dense("B2", B2, N, K // 2)
+    L = _batches(A)
+    if L < 1:
+        raise ValueError("L must be >= 1")
+    _rows_dense("A", A, M, K // 2, L)
+    _rows_dense("B1", B1, N, K // 2, L)
+    _rows_dense("B2", B2, N, K // 2, L)
     if N % 64 != 0:
         raise ValueError(f"N = {N} must be a multiple of 64")
     if K % 256 != 0:
         raise ValueError(f"K = {K} must be a multiple of 256")
-    _check_blocked("SFA", SFA, M, K, cuda)
-    _check_blocked("SFB1", SFB1, N, K, cuda)
-    _check_blocked("SFB2", SFB2, N, K, cuda)
-    return M, N, K
+    _check_blocked("SFA", SFA, M, K, cuda, L)
+    _check_blocked("SFB1", SFB1, N, K, cuda, L)
+    _check_blocked("SFB2", SFB2, N, K, cuda, L)
+    return M, N, K, L
 
 
 def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
@@ -132,7 +163,7 @@ def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
     ``workspace`` (a zero-initialised uint8 CUDA tensor of at least
     :func:`workspace_size` bytes) the caller owns the split-K scratch;
     otherwise the library keeps one per (device, stream)."""
-    M, N, K = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=True)
+    M, N, K, L = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=True)
     dev = C.device
     for name, t in (("A", A), ("B1", B1), ("B2", B2), ("SFA", SFA),
                     ("SFB1", SFB1), ("SFB2", SFB2)):
@@ -144,14 +175,14 @@ def dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
         if workspace is None:
             rc = lib.nvfp4_dual_gemm_run(
                 _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
-                _ptr(C), M, N, K, 1, flags, stream)
+                _ptr(C), M, N, K, L, flags, stream)
         else:
             if workspace.device != dev or not workspace.is_contiguous():
                 raise ValueError("workspace must be a contiguous tensor on "
                                  "C's device")
             rc = lib.nvfp4_dual_gemm_run_ws(
                 _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
-                _ptr(C), M, N, K, 1, flags, _ptr(workspace),
+                _ptr(C), M, N, K, L, flags, _ptr(workspace),
                 workspace.numel() * workspace.element_size(), stream)
     _lib.check(rc, "nvfp4_dual_gemm_run")
     return C
@@ -164,17 +195,22 @@ def dual_gemm_nvfp4(A, B1, B2, SFA, SFB1, SFB2, Cq=None, SFC=None, *,
     nibble) and the blocked e4m3 scales of h = fp16(silu(A B1^T) * (A B2^T)),
     equal bit for bit to ``quantize_nvfp4`` of :func:`dual_gemm`'s C.  The
     fp16 C is never written (``nvfp4_dual_gemm_run_nvfp4_out``).  ``Cq`` /
-    ``SFC`` are allocated on A's device when not given."""
-    M, N, K = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda=True)
+    ``SFC`` are allocated on A's device when not given.  For a batch (A of
+    shape [M, K/2, L]) Cq is [M, N/2, L] stored batch after batch and SFC
+    holds L blocked layouts one after another."""
+    M, N, K, L = _check_inputs(A, B1, B2, SFA, SFB1, SFB2, cuda=True)
     dev = A.device
     if Cq is None:
-        Cq = torch.empty((M, N // 2), dtype=torch.uint8, device=dev)
+        Cq = (torch.empty((M, N // 2), dtype=torch.uint8, device=dev)
+              if L == 1 else
+              torch.empty((L, M, N // 2), dtype=torch.uint8,
+                          device=dev).permute(1, 2, 0))
     if SFC is None:
-        SFC = torch.empty(max(_blocked_bytes(M, N), 1), dtype=torch.uint8,
+        SFC = torch.empty(max(L * _blocked_bytes(M, N), 1), dtype=torch.uint8,
                           device=dev)
     _check_bytes("Cq", Cq, True)
-    _rows_dense("Cq", Cq, M, N // 2)
-    _check_blocked("SFC", SFC, M, N, True)
+    _rows_dense("Cq", Cq, M, N // 2, L)
+    _check_blocked("SFC", SFC, M, N, True, L)
     for name, t in (("B1", B1), ("B2", B2), ("SFA", SFA), ("SFB1", SFB1),
                     ("SFB2", SFB2), ("Cq", Cq), ("SFC", SFC)):
         if t.device != dev:
@@ -183,7 +219,7 @@ def dual_gemm_nvfp4(A, B1, B2, SFA, SFB1, SFB2, Cq=None, SFC=None, *,
     with torch.cuda.device(dev):
         rc = lib.nvfp4_dual_gemm_run_nvfp4_out(
             _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
-            _ptr(Cq), _ptr(SFC), M, N, K, 1, flags, _stream(dev))
+            _ptr(Cq), _ptr(SFC), M, N, K, L, flags, _stream(dev))
     _lib.check(rc, "nvfp4_dual_gemm_run_nvfp4_out")
     return Cq, SFC
 
@@ -217,7 +253,9 @@ def dual_gemm_host(A, B1, B2, SFA, SFB1, SFB2, C, *, flags: int = 0,
     uint8 CUDA tensor of at least :func:`host_staging_size` bytes, is the
     device buffer the inputs go through; by default the library keeps one per
     (device, stream)."""
-    M, N, K = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=False)
+    M, N, K, L = _check_problem(A, B1, B2, SFA, SFB1, SFB2, C, cuda=False)
+    if L != 1:
+        raise ValueError("dual_gemm_host takes unbatched problems (L = 1)")
     dev = torch.device("cuda", torch.cuda.current_device()
                        if device is None else torch.device(device).index or 0)
     lib = _lib.load()
@@ -258,13 +296,15 @@ def custom_kernel(data):
 
 
 def workspace_size(M: int, N: int, K: int, flags: int = 0,
-                   device: torch.device | int | None = None) -> int:
-    """Bytes of caller-owned workspace :func:`dual_gemm` needs (0 = none)."""
+                   device: torch.device | int | None = None,
+                   L: int = 1) -> int:
+    """Bytes of caller-owned workspace :func:`dual_gemm` needs (0 = none)
+    for L problems of shape M x N x K."""
     lib = _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device()
                        if device is None else torch.device(device).index or 0)
     with torch.cuda.device(dev):
-        n = lib.nvfp4_dual_gemm_workspace_size(M, N, K, 1, flags)
+        n = lib.nvfp4_dual_gemm_workspace_size(M, N, K, L, flags)
     msg = _lib.last_error()
     if n == 0 and msg:
         raise RuntimeError(msg)
@@ -383,11 +423,14 @@ def generate_input(m: int, n: int, k: int, l: int = 1, seed: int = 0,
                    device="cuda"):
     """Seeded synthetic ``data`` tuple for :func:`custom_kernel`: randn fp32
     activations / weights (times a_scale / w_scale) quantised to NVFP4 on the
-    GPU.  Tensors: a/b1/b2 float4_e2m1fn_x2 [rows, K/2, 1], plain scales
-    float8_e4m3fn [rows, K/16, 1], blocked scales float8_e4m3fn (flat),
-    c float16 [m, n, 1]."""
-    if l != 1:
-        raise ValueError("only L = 1 is supported")
+    GPU.  Tensors: a/b1/b2 float4_e2m1fn_x2 [rows, K/2, l], plain scales
+    float8_e4m3fn [rows, K/16, l], blocked scales float8_e4m3fn (flat, l
+    blocked layouts one after another), c float16 [m, n, l]; for l > 1 each
+    [rows, cols, l] tensor is a [l, rows, cols] tensor viewed through
+    ``permute(1, 2, 0)`` (batch after batch in memory).  Batch 0 is the same
+    for every l."""
+    if l < 1:
+        raise ValueError("l must be >= 1")
     dev = torch.device(device)
     gen = torch.Generator(device=dev)
     out = []
@@ -395,16 +438,23 @@ def generate_input(m: int, n: int, k: int, l: int = 1, seed: int = 0,
     blocked = []
     for idx, (rows, scale) in enumerate(((m, a_scale), (n, w_scale),
                                          (n, w_scale))):
-        gen.manual_seed(seed * 1000003 + idx)
-        x = torch.randn((rows, k), generator=gen, device=dev,
-                        dtype=torch.float32)
-        if scale != 1.0:
-            x.mul_(scale)
-        codes, sf, blk = quantize_nvfp4(x)
-        del x
-        out.append(codes.view(torch.float4_e2m1fn_x2).unsqueeze(-1))
-        plain.append(sf.unsqueeze(-1))
-        blocked.append(blk.view(torch.float8_e4m3fn))
-    c = torch.empty((m, n, 1), dtype=torch.float16, device=dev)
+        codes_l, sf_l, blk_l = [], [], []
+        for b in range(l):
+            gen.manual_seed(seed * 1000003 + idx + 7919 * b)
+            x = torch.randn((rows, k), generator=gen, device=dev,
+                            dtype=torch.float32)
+            if scale != 1.0:
+                x.mul_(scale)
+            codes, sf, blk = quantize_nvfp4(x)
+            del x
+            codes_l.append(codes)
+            sf_l.append(sf)
+            blk_l.append(blk)
+        codes = torch.stack(codes_l).permute(1, 2, 0)
+        out.append(codes.view(torch.float4_e2m1fn_x2))
+        plain.append(torch.stack(sf_l).permute(1, 2, 0))
+        blocked.append(torch.cat(blk_l).view(torch.float8_e4m3fn))
+    c = torch.empty((l, m, n), dtype=torch.float16,
+                    device=dev).permute(1, 2, 0)
     return (out[0], out[1], out[2], plain[0], plain[1], plain[2],
             blocked[0], blocked[1], blocked[2], c)

@@ -67,6 +67,12 @@ struct Cfg {
 struct KParams {
   Plan plan;
   int M, N, K;
+  // batch l of a batched problem (plan.L > 1): its blocked scales start
+  // l * sfa_batch / l * sfb_batch bytes into SFA / SFB1 / SFB2, its rows of
+  // C (or of Cq / SFC) l * M * N elements (l * M * N/2 / l * sfc_batch
+  // bytes) into C (Cq / SFC); A, B1, B2 are addressed by the tensor maps'
+  // third coordinate
+  long long sfa_batch, sfb_batch, sfc_batch;
   const uint8_t* sfa;
   const uint8_t* sfb1;
   const uint8_t* sfb2;
@@ -278,19 +284,21 @@ __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
   }
 }
 
-__device__ __forceinline__ OutRow out_row(const KParams& p, int grow,
+__device__ __forceinline__ OutRow out_row(const KParams& p, int l, int grow,
                                           int col0) {
   OutRow o;
   o.col0 = col0;
   o.row_ok = grow < p.M;
+  const size_t mn = (size_t)l * p.M * p.N;  // elements before batch l
   if (p.cq != nullptr) {
     o.c = nullptr;
-    o.q = p.cq + (size_t)grow * (p.N / 2) + col0 / 2;
-    o.sf = p.sfc + (size_t)(grow / 128) * (p.N / 64) * kSfAtomBytes +
+    o.q = p.cq + mn / 2 + (size_t)grow * (p.N / 2) + col0 / 2;
+    o.sf = p.sfc + (size_t)l * p.sfc_batch +
+           (size_t)(grow / 128) * (p.N / 64) * kSfAtomBytes +
            (grow % 32) * 16 + ((grow % 128) / 32) * 4;
     o.sf_ok = grow < (p.M + 127) / 128 * 128;
   } else {
-    o.c = p.C + (size_t)grow * p.N + col0;
+    o.c = p.C + mn + (size_t)grow * p.N + col0;
     o.q = nullptr;
     o.sf = nullptr;
     o.sf_ok = false;
@@ -508,7 +516,8 @@ template <int BN>
 __device__ __forceinline__ void split_epilogue(
     const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
     uint64_t* ready_bar, uint64_t* recv_bar, int warp, int lane, int part,
-    int own, uint32_t xpeer, int grow0, int n_tile, bool& cluster_waited) {
+    int own, uint32_t xpeer, int l, int grow0, int n_tile,
+    bool& cluster_waited) {
   constexpr int kHalf = BN / 2;
   constexpr int kHalfChunks = kHalf / 16;
   constexpr uint32_t kChunkBytes = 2u * 128u * 16u * 4u;  // GEMM1 + GEMM2
@@ -516,7 +525,7 @@ __device__ __forceinline__ void split_epilogue(
   const int row = 32 * (warp % 4) + lane;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16);
   const int grow = grow0 + row;
-  const OutRow out = out_row(p, grow, n_tile * BN);
+  const OutRow out = out_row(p, l, grow, n_tile * BN);
 
   griddep_wait();  // global memory only after the previous grid
   bool ok = mbar_wait(acc_full_bar, 0, p.err, kErrEpilogue);
@@ -694,8 +703,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool cluster_waited = false;
   // Split-K: this CTA's half of K (= its cluster rank) and its tile.
   const int split_own = static_cast<int>(blockIdx.x & 1);
-  int split_m_tile, split_n_tile;
-  tile_mn(plan, static_cast<int>(blockIdx.x >> 1), split_m_tile, split_n_tile);
+  int split_l, split_m_tile, split_n_tile;
+  tile_lmn(plan, static_cast<int>(blockIdx.x >> 1), split_l, split_m_tile,
+           split_n_tile);
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -730,13 +740,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     Work w;
     bool have = work_next(plan, it, w);
     if (a_side && lane == 0) NVFP4DG_STAMP(1, 58);
-    int m_tile = 0, n_tile = 0;
+    int l = 0, m_tile = 0, n_tile = 0;
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
     auto place = [&] {
-      tile_mn(plan, w.tile, m_tile, n_tile);
-      sfa_src = p.sfa + (size_t)m_tile * kblk64 * kSfAtomBytes;
-      sfb_off = (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+      tile_lmn(plan, w.tile, l, m_tile, n_tile);
+      sfa_src = p.sfa + (size_t)l * p.sfa_batch +
+                (size_t)m_tile * kblk64 * kSfAtomBytes;
+      sfb_off = (size_t)l * p.sfb_batch +
+                (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
     };
     if (have) place();
     if (a_side && lane == 0) NVFP4DG_STAMP(1, 59);
@@ -768,15 +780,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
             tma_load_3d(st, &tmA, &full_bar[stage], kb * kRowBytes,
-                        m_tile * kBM, 0, pol);
+                        m_tile * kBM, l, pol);
           } else {
             bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
+            // (the merged map's third coordinate picks B1 / B2; it is only
+            // used for unbatched problems, otherwise it is the batch)
             tma_load_3d(st + Cf::kABytes, &tmB1, &full_bar[stage],
-                        kb * kRowBytes, n_tile * BN, 0, pol);
+                        kb * kRowBytes, n_tile * BN, l, pol);
             if (!p.b_merged)
               tma_load_3d(st + Cf::kABytes + Cf::kBBytes, &tmB2,
-                          &full_bar[stage], kb * kRowBytes, n_tile * BN, 0,
+                          &full_bar[stage], kb * kRowBytes, n_tile * BN, l,
                           pol);
           }
           if (a_side) NVFP4DG_STAMP(1, issued);
@@ -821,8 +835,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; ok && have; have = work_next(plan, it, w)) {
       // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
-      int m_tile, n_tile;
-      tile_mn(plan, w.tile, m_tile, n_tile);
+      int l_, m_tile, n_tile;
+      tile_lmn(plan, w.tile, l_, m_tile, n_tile);
       const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got = mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
@@ -904,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                         warp, lane, 1, split_own, split_own ^ 1u,
+                         warp, lane, 1, split_own, split_own ^ 1u, split_l,
                          split_m_tile * kBM, split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -975,7 +989,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                       warp, lane, 0, split_own, split_own ^ 1u,
+                       warp, lane, 0, split_own, split_own ^ 1u, split_l,
                        split_m_tile * kBM, split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
@@ -993,10 +1007,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
       tc_fence_after();
-      int m_tile, n_tile;
-      tile_mn(plan, w.tile, m_tile, n_tile);
+      int l, m_tile, n_tile;
+      tile_lmn(plan, w.tile, l, m_tile, n_tile);
       const int grow = m_tile * kBM + row;
-      const OutRow out = out_row(p, grow, n_tile * BN);
+      const OutRow out = out_row(p, l, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -1157,8 +1171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
   // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
   const int split_own = static_cast<int>(crank >> 1);
-  int split_m_tile, split_n_tile;
-  tile_mn(plan, unit >> 1, split_m_tile, split_n_tile);
+  int split_l, split_m_tile, split_n_tile;
+  tile_lmn(plan, unit >> 1, split_l, split_m_tile, split_n_tile);
   const int split_grow0 =
       split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
   bool cluster_waited = true;  // the start-up cluster barrier (below)
@@ -1231,12 +1245,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     work_begin(plan, unit, it);
     Work w;
     bool have = work_next(plan, it, w);
-    int n_tile = 0, a_row = 0;
+    int l = 0, n_tile = 0, a_row = 0;
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
     auto place = [&] {
       int m_tile;
-      tile_mn(plan, w.tile, m_tile, n_tile);
+      tile_lmn(plan, w.tile, l, m_tile, n_tile);
       a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
       // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
       // lie wholly past M (M in (256t, 256t + 128] for the last pair tile)
@@ -1244,8 +1258,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // tensor map and its accumulator rows are never stored.
       const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
                             (p.M + kBM - 1) / kBM - 1);
-      sfa_src = p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
-      sfb_off = (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+      sfa_src = p.sfa + (size_t)l * p.sfa_batch +
+                (size_t)a_blk * kblk64 * kSfAtomBytes;
+      sfb_off = (size_t)l * p.sfb_batch +
+                (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
     };
     if (have) place();
     named_bar_sync(kBarInit, 96);  // this CTA's mbarriers are initialised
@@ -1280,13 +1296,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                       pol);
             bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
-            tma_load_2d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, pol);
+            // unbatched problems use 2-D maps, batched ones 3-D maps whose
+            // third coordinate is the batch
+            if (plan.L == 1)
+              tma_load_2d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, pol);
+            else
+              tma_load_3d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, l,
+                               pol);
             NVFP4DG_STAMP(1, issued);
           } else {
             bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
-            tma_load_2d_pair(st + Cf::kABytes, rank == 0 ? &tmB1 : &tmB2,
-                             full_s, kb * kRowBytes, n_tile * BN, pol);
+            if (plan.L == 1)
+              tma_load_2d_pair(st + Cf::kABytes, rank == 0 ? &tmB1 : &tmB2,
+                               full_s, kb * kRowBytes, n_tile * BN, pol);
+            else
+              tma_load_3d_pair(st + Cf::kABytes, rank == 0 ? &tmB1 : &tmB2,
+                               full_s, kb * kRowBytes, n_tile * BN, l, pol);
           }
           ++issued;
           if (++stage == S) {
@@ -1327,8 +1353,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool have = work_next(plan, it, w);
     griddep_wait();  // global memory only after the previous grid
     for (; ok && have; have = work_next(plan, it, w)) {
-      int m_tile, n_tile;
-      tile_mn(plan, w.tile, m_tile, n_tile);
+      int l_, m_tile, n_tile;
+      tile_lmn(plan, w.tile, l_, m_tile, n_tile);
       const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got =
@@ -1410,8 +1436,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                         warp, lane, 1, split_own, crank ^ 2u, split_grow0,
-                         split_n_tile, cluster_waited);
+                         warp, lane, 1, split_own, crank ^ 2u, split_l,
+                         split_grow0, split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
@@ -1483,8 +1509,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                       warp, lane, 0, split_own, crank ^ 2u, split_grow0,
-                       split_n_tile, cluster_waited);
+                       warp, lane, 0, split_own, crank ^ 2u, split_l,
+                       split_grow0, split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
     const int row = threadIdx.x;
@@ -1503,10 +1529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit_i);
       tc_fence_after();
-      int m_tile, n_tile;
-      tile_mn(plan, w.tile, m_tile, n_tile);
+      int l, m_tile, n_tile;
+      tile_lmn(plan, w.tile, l, m_tile, n_tile);
       const int grow = m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
-      const OutRow out = out_row(p, grow, n_tile * BN);
+      const OutRow out = out_row(p, l, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -1679,10 +1705,14 @@ __global__ void __launch_bounds__(256)
     if (r < rows) {
       const T* src = X + (size_t)r * ldx + (size_t)g * 64;
       uint8_t* dst = codes + (size_t)r * (K / 2) + (size_t)g * 32;
-#pragma unroll 1
+      // all four 16-element loads of the group before any arithmetic, so
+      // that each lane keeps its whole 64-element run in flight
+      float vv[4][16];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) In16<T>::load(src + 16 * b, vv[b]);
+#pragma unroll
       for (int b = 0; b < 4; ++b) {
-        float v[16];
-        In16<T>::load(src + 16 * b, v);
+        const float* v = vv[b];
         uint32_t w0, w1;
         const uint8_t sb = quant_block16(v, w0, w1);
         *reinterpret_cast<uint2*>(dst + 8 * b) = make_uint2(w0, w1);
@@ -1799,6 +1829,11 @@ struct DevInfo {
 };
 std::map<int, DevInfo> g_dev;
 
+// Bytes of a blocked scale tensor of `rows` rows and K / 16 scales a row.
+long long blocked_scale_bytes(long long rows, long long K) {
+  return (rows + 127) / 128 * (K / 64) * 512;
+}
+
 struct MapKey {
   const void* ptr;
   const void* ptr2;  // second tensor of a B1|B2 map, else nullptr
@@ -1807,6 +1842,7 @@ struct MapKey {
   long long row_bytes;
   int box_rows;
   int dev;
+  int layers;  // batch count (third dimension of a per-matrix map)
   bool operator<(const MapKey& o) const {
     if (ptr != o.ptr) return ptr < o.ptr;
     if (ptr2 != o.ptr2) return ptr2 < o.ptr2;
@@ -1814,6 +1850,7 @@ struct MapKey {
     if (rows != o.rows) return rows < o.rows;
     if (row_bytes != o.row_bytes) return row_bytes < o.row_bytes;
     if (box_rows != o.box_rows) return box_rows < o.box_rows;
+    if (layers != o.layers) return layers < o.layers;
     return dev < o.dev;
   }
 };
@@ -1865,9 +1902,12 @@ int device_info(int dev, DevInfo** out) {
 // with the 128-byte swizzle.  rank 3 adds a unit outer dimension, so that
 // the 1-SM kernel issues every tile copy as the same 3-D instruction (see
 // b_pair_map).
+// `layers` > 1: a batch of `layers` matrices of `rows` rows, one after the
+// other (the third dimension, stride rows * row_bytes; needs rank 3).
 int tensor_map(const void* ptr, long long rows, long long row_bytes,
-               int box_rows, int dev, CUtensorMap* out, int rank = 2) {
-  MapKey key{ptr, nullptr, rank, rows, row_bytes, box_rows, dev};
+               int box_rows, int dev, CUtensorMap* out, int rank = 2,
+               int layers = 1) {
+  MapKey key{ptr, nullptr, rank, rows, row_bytes, box_rows, dev, layers};
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
     *out = it->second;
@@ -1877,7 +1917,8 @@ int tensor_map(const void* ptr, long long rows, long long row_bytes,
   if (rc) return rc;
   CUtensorMap m;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_bytes),
-                              static_cast<cuuint64_t>(rows), 1};
+                              static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(layers)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_bytes),
                                  static_cast<cuuint64_t>(rows * row_bytes)};
   const cuuint32_t box[3] = {static_cast<cuuint32_t>(kRowBytes),
@@ -1912,7 +1953,7 @@ bool b_pair_map(const void* b1, const void* b2, long long rows,
   if (p2 <= p1 || (p2 - p1) % 16 != 0 || (p2 - p1) >= (1ull << 40) ||
       static_cast<long long>(p2 - p1) < rows * row_bytes)
     return false;
-  MapKey key{b1, b2, 3, rows, row_bytes, box_rows, dev};
+  MapKey key{b1, b2, 3, rows, row_bytes, box_rows, dev, 1};
   auto it = g_maps.find(key);
   if (it != g_maps.end()) {
     *out = it->second;
@@ -1949,14 +1990,15 @@ bool b_pair_map(const void* b1, const void* b2, long long rows,
 // epilogue of a tile takes ~34 cycles per output column (not overlapped);
 // a split tile costs its fp32 partial round trip through L2.
 Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
-              bool streamk, bool force_sk) {
+              bool streamk, bool force_sk, int L = 1) {
   Plan p{};
   p.bn = bn;
   p.ctas = ctas;
+  p.L = L;
   p.m_tiles = (M + kBM * ctas - 1) / (kBM * ctas);
   p.n_tiles = N / bn;
   p.kblocks = K / 256;
-  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.num_tiles = L * p.m_tiles * p.n_tiles;
   const int T = p.num_tiles;
   if (!streamk || (T % unit_cap == 0 && !force_sk)) {
     p.grid = std::min(T, unit_cap);
@@ -1977,14 +2019,15 @@ Plan plan_for(int M, int N, int K, int bn, int ctas, int unit_cap,
 
 // Cluster split-K: each tile's K range in two halves on two work units (two
 // CTAs, or two 2-SM pairs in a cluster of four) that exchange partial sums.
-Plan plan_split(int M, int N, int K, int bn, int ctas = 1) {
+Plan plan_split(int M, int N, int K, int bn, int ctas = 1, int L = 1) {
   Plan p{};
   p.bn = bn;
   p.ctas = ctas;
+  p.L = L;
   p.m_tiles = (M + kBM * ctas - 1) / (kBM * ctas);
   p.n_tiles = N / bn;
   p.kblocks = K / 256;
-  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.num_tiles = L * p.m_tiles * p.n_tiles;
   p.grid = 2 * p.num_tiles;
   p.dp_tiles = p.num_tiles;
   p.sk_iters = 0;
@@ -1993,10 +2036,11 @@ Plan plan_split(int M, int N, int K, int bn, int ctas = 1) {
   return p;
 }
 
-bool split_fits(int M, int N, int K, int bn, int sms, int ctas = 1) {
+bool split_fits(int M, int N, int K, int bn, int sms, int ctas = 1,
+                int L = 1) {
   if (N % bn != 0 || K / 256 < 2) return false;
   const long long tiles =
-      (long long)((M + kBM * ctas - 1) / (kBM * ctas)) * (N / bn);
+      (long long)L * ((M + kBM * ctas - 1) / (kBM * ctas)) * (N / bn);
   return 2 * ctas * tiles <= sms;
 }
 
@@ -2056,7 +2100,9 @@ double plan_cost(const Plan& p) {
   return cost;
 }
 
-Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
+// `L` independent problems of one shape (a batch) share one launch: their
+// tiles are numbered batch by batch and scheduled together.
+Plan choose_plan(int M, int N, int K, unsigned flags, int sms, int L = 1) {
   const int forced = static_cast<int>(flags & NVFP4DG_FLAG_GRID_MASK);
   const bool streamk = (flags & NVFP4DG_FLAG_NO_STREAMK) == 0;
   const bool force_sk = (flags & NVFP4DG_FLAG_FORCE_STREAMK) != 0;
@@ -2080,16 +2126,16 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
     // forced: 2-SM pairs when PAIR is also given, else single CTAs
     const int ctas = (flags & NVFP4DG_FLAG_PAIR) ? 2 : 1;
     for (int i = 0; i < nb; ++i)
-      if (split_fits(M, N, K, bns[i], forced > 0 ? forced : sms, ctas))
-        return plan_split(M, N, K, bns[i], ctas);
+      if (split_fits(M, N, K, bns[i], forced > 0 ? forced : sms, ctas, L))
+        return plan_split(M, N, K, bns[i], ctas, L);
     return best;  // grid == 0: not possible (rejected by check_problem)
   }
   if (!(flags & (NVFP4DG_FLAG_NO_SPLITK | NVFP4DG_FLAG_FORCE_STREAMK)) &&
       forced == 0) {
     for (int c = 0; c < nc; ++c) {
       for (int i = 0; i < nb; ++i) {
-        if (!split_fits(M, N, K, bns[i], sms, ctas_opts[c])) continue;
-        Plan p = plan_split(M, N, K, bns[i], ctas_opts[c]);
+        if (!split_fits(M, N, K, bns[i], sms, ctas_opts[c], L)) continue;
+        Plan p = plan_split(M, N, K, bns[i], ctas_opts[c], L);
         const double cost = plan_cost(p);
         if (cost < best_cost) {
           best_cost = cost;
@@ -2110,13 +2156,15 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
         int ncap = 0;
         caps[ncap++] = cap;
         if (sk == 1 && forced == 0) {
-          const long long tiles =
-              (long long)((M + kBM * ctas - 1) / (kBM * ctas)) * (N / bns[i]);
+          const long long tiles = (long long)L *
+                                  ((M + kBM * ctas - 1) / (kBM * ctas)) *
+                                  (N / bns[i]);
           for (int f : {2, 3, 4, 6, 8})
             if (tiles * f < cap) caps[ncap++] = static_cast<int>(tiles * f);
         }
         for (int j = 0; j < ncap; ++j) {
-          Plan p = plan_for(M, N, K, bns[i], ctas, caps[j], sk == 1, force_sk);
+          Plan p = plan_for(M, N, K, bns[i], ctas, caps[j], sk == 1, force_sk,
+                            L);
           const double cost = plan_cost(p);
           if (cost < best_cost) {
             best_cost = cost;
@@ -2132,12 +2180,16 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms) {
 int check_problem(const void* A, const void* B1, const void* B2,
                   const void* SFA, const void* SFB1, const void* SFB2,
                   const void* C, int M, int N, int K, int L, unsigned flags,
-                  bool device_ptrs = true) {
+                  bool device_ptrs = true, bool allow_batch = false) {
   if (M < 0 || N < 0 || K < 0)
     return fail(NVFP4DG_ERR_INVALID, "M, N, K must be non-negative");
-  if (L != 1)
+  if (L < 1 || (L != 1 && !allow_batch))
     return fail(NVFP4DG_ERR_INVALID,
-                "L must be 1 (batched problems are not supported)");
+                allow_batch ? "L must be >= 1"
+                            : "L must be 1 for this entry point (batched "
+                              "problems go through nvfp4_dual_gemm_run)");
+  if ((long long)L * ((M + 255) / 256) * (N / 64) >= (1ll << 30))
+    return fail(NVFP4DG_ERR_INVALID, "too many tiles (L * M * N too large)");
   if (N % 64 != 0)
     return fail(NVFP4DG_ERR_INVALID, "N must be a multiple of 64");
   if (K % 256 != 0)
@@ -2189,22 +2241,28 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   int rc;
   // The pair kernel copies with 2-D maps; the 1-SM kernel with 3-D ones,
   // both weight tiles of a K block in one copy when a single map can cover
-  // B1 and B2.
-  const int rank = PAIR ? 2 : 3;
-  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta, rank))) return rc;
-  const bool merged = !PAIR && !(flags & NVFP4DG_FLAG_NO_MERGED_B) &&
+  // B1 and B2.  Batched problems (L > 1) use 3-D maps in both kernels, the
+  // batch being the third coordinate, and separate B1 / B2 maps.
+  const int L = plan.L;
+  const int rank = (PAIR && L == 1) ? 2 : 3;
+  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta, rank, L))) return rc;
+  const bool merged = !PAIR && L == 1 &&
+                      !(flags & NVFP4DG_FLAG_NO_MERGED_B) &&
                       b_pair_map(B1, B2, N, K / 2, BN, devid, &tb1);
   if (merged) {
     tb2 = tb1;
   } else {
-    if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1, rank))) return rc;
-    if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2, rank))) return rc;
+    if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1, rank, L))) return rc;
+    if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2, rank, L))) return rc;
   }
   KParams kp;
   kp.plan = plan;
   kp.M = M;
   kp.N = N;
   kp.K = K;
+  kp.sfa_batch = blocked_scale_bytes(M, K);
+  kp.sfb_batch = blocked_scale_bytes(N, K);
+  kp.sfc_batch = blocked_scale_bytes(M, N);
   kp.sfa = static_cast<const uint8_t*>(SFA);
   kp.sfb1 = static_cast<const uint8_t*>(SFB1);
   kp.sfb2 = static_cast<const uint8_t*>(SFB2);
@@ -2278,7 +2336,7 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   g_last_error.clear();
   const bool q_out = cq != nullptr || sfc != nullptr;
   int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, q_out ? cq : C, M, N, K,
-                         L, flags);
+                         L, flags, true, /*allow_batch=*/true);
   if (rc) return rc;
   if (q_out && M > 0 && N > 0) {
     if (sfc == nullptr) return fail(NVFP4DG_ERR_INVALID, "SFC is NULL");
@@ -2290,12 +2348,12 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   if (K == 0) {  // empty sums: silu(0) * 0 = 0
     cudaError_t e;
     if (q_out) {
-      e = cudaMemsetAsync(cq, 0, (size_t)M * (N / 2), stream);
+      e = cudaMemsetAsync(cq, 0, (size_t)L * M * (N / 2), stream);
       if (e == cudaSuccess)
-        e = cudaMemsetAsync(sfc, 0, (size_t)(M + 127) / 128 * (N / 64) * 512,
+        e = cudaMemsetAsync(sfc, 0, (size_t)L * blocked_scale_bytes(M, N),
                             stream);
     } else {
-      e = cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
+      e = cudaMemsetAsync(C, 0, (size_t)L * M * N * sizeof(__half), stream);
     }
     return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "cudaMemsetAsync");
   }
@@ -2306,7 +2364,7 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   DevInfo* dev = nullptr;
   if ((rc = device_info(devid, &dev))) return rc;
-  const Plan plan = choose_plan(M, N, K, flags, dev->sms);
+  const Plan plan = choose_plan(M, N, K, flags, dev->sms, L);
   if (plan.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
                 "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
@@ -2779,14 +2837,14 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
 size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
                                       unsigned flags) {
   g_last_error.clear();
-  if (M <= 0 || N <= 0 || K <= 0 || L != 1 || N % 64 || K % 256) return 0;
+  if (M <= 0 || N <= 0 || K <= 0 || L < 1 || N % 64 || K % 256) return 0;
   int devid = 0;
   if (cudaGetDevice(&devid) != cudaSuccess) return 0;
   std::lock_guard<std::mutex> lock(g_mu);
   DevInfo* dev = nullptr;
   if (device_info(devid, &dev)) return 0;
   return static_cast<size_t>(
-      workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+      workspace_bytes(choose_plan(M, N, K, flags, dev->sms, L)));
 }
 
 int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,

@@ -34,7 +34,7 @@ struct Plan {
   int m_tiles;      // ceil(M / (128 * ctas))
   int n_tiles;      // N / BN
   int kblocks;      // K / 256
-  int num_tiles;    // m_tiles * n_tiles
+  int num_tiles;    // L * m_tiles * n_tiles
   int grid;         // persistent work units (CTAs, or CTA pairs)
   int dp_tiles;     // whole tiles handed out round-robin (multiple of grid)
   int bn;           // tile width per GEMM (64 or 128)
@@ -47,32 +47,61 @@ struct Plan {
   // on the producers' way to their first copy)
   uint32_t mt_mul;
   int mt_shift;
+  int L;            // batch count (independent problems of one shape)
+  // (tile / m_tiles) / n_tiles, the batch of a tile, likewise (L > 1)
+  uint32_t nt_mul;
+  int nt_shift;
 };
 
 // Division by d >= 1 through a multiply-high: shift = ceil(log2 d),
 // mul = floor(2^32 (2^shift - d) / d) + 1; exact for every n < 2^31
 // (Granlund and Montgomery, "Division by invariant integers using
 // multiplication", 1994, round-up variant).
-inline void set_tile_div(Plan& p) {
-  const unsigned long long d = static_cast<unsigned long long>(p.m_tiles);
+inline void set_div(unsigned long long d, uint32_t& mul, int& shift_out) {
   int shift = 0;
   while ((1ull << shift) < d) ++shift;
-  p.mt_shift = shift;
-  p.mt_mul = static_cast<uint32_t>(((1ull << 32) * ((1ull << shift) - d)) / d +
-                                   1ull);
+  shift_out = shift;
+  mul = static_cast<uint32_t>(((1ull << 32) * ((1ull << shift) - d)) / d +
+                              1ull);
 }
 
-// (m_tile, n_tile) of linear tile index `tile` (m fastest).
-NVFP4DG_HD void tile_mn(const Plan& p, int tile, int& m_tile, int& n_tile) {
-  const uint32_t t = static_cast<uint32_t>(tile);
+inline void set_tile_div(Plan& p) {
+  if (p.L < 1) p.L = 1;
+  set_div(static_cast<unsigned long long>(p.m_tiles), p.mt_mul, p.mt_shift);
+  set_div(static_cast<unsigned long long>(p.n_tiles), p.nt_mul, p.nt_shift);
+}
+
+NVFP4DG_HD uint32_t div_by(uint32_t t, uint32_t mul, int shift) {
 #if defined(__CUDA_ARCH__)
-  const uint32_t hi = __umulhi(t, p.mt_mul);
+  const uint32_t hi = __umulhi(t, mul);
 #else
-  const uint32_t hi = static_cast<uint32_t>(
-      (static_cast<unsigned long long>(t) * p.mt_mul) >> 32);
+  const uint32_t hi =
+      static_cast<uint32_t>((static_cast<unsigned long long>(t) * mul) >> 32);
 #endif
-  n_tile = static_cast<int>((hi + t) >> p.mt_shift);
-  m_tile = tile - n_tile * p.m_tiles;
+  return (hi + t) >> shift;
+}
+
+// (batch, m_tile, n_tile) of linear tile index `tile`: m fastest, then n,
+// then the batch.
+NVFP4DG_HD void tile_lmn(const Plan& p, int tile, int& l, int& m_tile,
+                         int& n_tile) {
+  const uint32_t t = static_cast<uint32_t>(tile);
+  const int u = static_cast<int>(div_by(t, p.mt_mul, p.mt_shift));
+  m_tile = tile - u * p.m_tiles;
+  if (p.L == 1) {
+    l = 0;
+    n_tile = u;
+  } else {
+    l = static_cast<int>(div_by(static_cast<uint32_t>(u), p.nt_mul,
+                                p.nt_shift));
+    n_tile = u - l * p.n_tiles;
+  }
+}
+
+// (m_tile, n_tile) of linear tile index `tile` of an unbatched plan.
+NVFP4DG_HD void tile_mn(const Plan& p, int tile, int& m_tile, int& n_tile) {
+  int l;
+  tile_lmn(p, tile, l, m_tile, n_tile);
 }
 
 struct Work {

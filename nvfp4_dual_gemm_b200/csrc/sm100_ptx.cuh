@@ -475,6 +475,20 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       : "memory");
 }
 
+// The same with a third (batch) coordinate, for batched problems (L > 1).
+__device__ __forceinline__ void tma_load_3d_pair(void* dst, const CUtensorMap* m,
+                                                 uint32_t bar_cluster, int c0,
+                                                 int c1, int c2,
+                                                 uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::"
+      "complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem,
                                                 uint32_t ncols) {
   asm volatile(

@@ -41,8 +41,11 @@ def test_invalid_arguments_rejected_without_gpu():
     # K not a multiple of 256
     rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 128, 100, 1, 0, None)
     assert rc == _lib.ERR_INVALID
-    # L != 1
-    rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 128, 256, 2, 0, None)
+    # L < 1; batched problems (L > 1) only through the main entry points
+    rc = lib.nvfp4_dual_gemm_run(p, p, p, p, p, p, p, 128, 128, 256, 0, 0, None)
+    assert rc == _lib.ERR_INVALID and "L must be >= 1" in _lib.last_error()
+    rc = lib.nvfp4_dual_gemm_run_noalloc(p, p, p, p, p, p, p, 128, 128, 256, 2,
+                                         0, None)
     assert rc == _lib.ERR_INVALID and "L must be 1" in _lib.last_error()
     # misaligned pointer
     q = ctypes.c_void_p(24)
