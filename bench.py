@@ -723,7 +723,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--flags", type=int, default=0,
                     help="NVFP4DG_FLAG_* bits (0 = automatic schedule)")
-    ap.add_argument("--e2e-steps", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=50)
     ap.add_argument("--shapes", action="store_true",
                     help="also time C2/C3/C4 and report their geomean")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -411,7 +411,8 @@ def test_weight_placement_and_merged_copy(order, flags):
 
 @pytest.mark.parametrize("dtype", ["float32", "float16", "bfloat16"])
 @pytest.mark.parametrize("rows,k,pitch", [(300, 1024, 0), (1, 64, 0),
-                                          (129, 7168, 0), (77, 512, 640)])
+                                          (129, 7168, 0), (77, 512, 640),
+                                          (130, 576, 0), (5, 960, 1024)])
 def test_activation_quantizer_dtypes_and_pitch(dtype, rows, k, pitch):
     # fp32 / fp16 / bf16 rows (optionally inside a wider row pitch) quantised
     # on the GPU: bit-exact against the oracle applied to the same values
