@@ -329,7 +329,11 @@ def run_ours(args, world, rank):
     wl = WORKLOADS[args.workload]
     m, n, k = rank_problem(wl, world, rank)
     sets, nsets = make_sets(dg, m, n, k, wl, rank)
-    flags = args.flags
+    # The timed calls never write the weights (inputs rotate over sets made
+    # before timing), so they may be read before the dependency wait.
+    from nvfp4_dual_gemm_b200 import _lib
+    flags = args.flags | (0 if args.no_static_weights
+                          else _lib.FLAG_STATIC_WEIGHTS)
     ws_bytes = dg.workspace_size(m, n, k, flags)
     ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device="cuda")
 
@@ -374,7 +378,7 @@ def run_ours(args, world, rank):
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
 
     def e2e_step():
-        dg.dual_gemm_host(*host_in, c_host, flags=flags)
+        dg.dual_gemm_host(*host_in, c_host, flags=args.flags)
 
     e2e_ms, h2d, d2h = time_e2e(e2e_step, host_in, c_host, e2e_steps, world)
     e2e_ms = max_over_ranks(e2e_ms, world)
@@ -395,7 +399,11 @@ def run_ours(args, world, rank):
                    "l2": f"{nsets} rotating input sets of "
                          f"{algo_bytes(m, n, k) / 1e6:.1f} MB "
                          f"(> 2 x 126 MB L2 between reuses)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+                   "timed": "one CUDA graph of `steps` calls, replayed once",
+                   "flags": (f"{flags:#x}" + (
+                       " (STATIC_WEIGHTS: the weights, constant across the "
+                       "timed calls, are copied before the dependency wait)"
+                       if flags & _lib.FLAG_STATIC_WEIGHTS else ""))},
         "roofline": roof,
         "e2e": {"value": round(e2e_val, 3), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -406,7 +414,7 @@ def run_ours(args, world, rank):
         "clocks": clocks,
     }
     if args.shapes and world == 1:
-        line["shapes"] = shape_sweep(dg, args)
+        line["shapes"] = shape_sweep(dg, args, flags)
         vals = [s["tflops"] for s in line["shapes"]]
         line["geomean_tflops"] = round(math.exp(sum(map(math.log, vals)) /
                                                 len(vals)), 3)
@@ -418,21 +426,21 @@ def run_ours(args, world, rank):
     return line
 
 
-def shape_sweep(dg, args):
+def shape_sweep(dg, args, flags=0):
     out = []
     peaks = load_peaks()
     for key in ("c2", "c3", "c4"):
         wl = WORKLOADS[key]
         m, n, k = wl["M"], wl["N"], wl["K"]
         sets, nsets = make_sets(dg, m, n, k, wl, 0)
-        ws = torch.zeros(max(dg.workspace_size(m, n, k, 0), 256),
+        ws = torch.zeros(max(dg.workspace_size(m, n, k, flags), 256),
                          dtype=torch.uint8, device="cuda")
         steps = max(10, min(args.steps, 200))
 
         def step(i):
             d = sets[i % nsets]
             dg.dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9],
-                         workspace=ws)
+                         workspace=ws, flags=flags)
 
         ms, _ = time_graph(step, steps, 3, 1)
         us = ms * 1e3 / steps
@@ -727,6 +735,9 @@ def main():
     ap.add_argument("--shapes", action="store_true",
                     help="also time C2/C3/C4 and report their geomean")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-static-weights", action="store_true",
+                    help="time without NVFP4DG_FLAG_STATIC_WEIGHTS (weight "
+                         "copies then also wait for the previous kernel)")
     ap.add_argument("--plumbing", choices=sorted(PLUMBING),
                     help="time the activation quantiser or the scale layout "
                          "converter instead of the dual GEMM (1 GPU)")

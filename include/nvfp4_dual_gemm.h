@@ -86,6 +86,17 @@ extern "C" {
                                            grid in the stream finishes, and
                                            waits for it before touching global
                                            memory)                            */
+#define NVFP4DG_FLAG_STATIC_WEIGHTS (1u << 24) /* the caller guarantees that
+                                              no kernel enqueued before this
+                                              call writes B1, B2, SFB1 or
+                                              SFB2: the weight copies start
+                                              before the programmatic
+                                              dependency wait, overlapping
+                                              the previous kernel's tail
+                                              (decode steps on constant
+                                              weights); A, SFA and C still
+                                              wait.  No effect with
+                                              NVFP4DG_FLAG_NO_PDL. */
 #define NVFP4DG_FLAG_NO_MERGED_B (1u << 23) /* copy B1 and B2 tiles with
                                               separate copies (by default one
                                               copy brings both when B2 lies

@@ -36,6 +36,7 @@ from ._lib import (  # noqa: F401
     FLAG_NO_STREAMK,
     FLAG_PAIR,
     FLAG_SPLITK,
+    FLAG_STATIC_WEIGHTS,
     FLAG_SYNC_CHECK,
     NativeLibraryError,
 )

@@ -35,6 +35,7 @@ FLAG_SPLITK = 1 << 20
 FLAG_NO_SPLITK = 1 << 21
 FLAG_NO_PDL = 1 << 22
 FLAG_NO_MERGED_B = 1 << 23
+FLAG_STATIC_WEIGHTS = 1 << 24
 
 # Input element types of nvfp4_quantize_rows.
 DTYPE_F32 = 0

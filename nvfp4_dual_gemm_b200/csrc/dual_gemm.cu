@@ -89,6 +89,10 @@ struct KParams {
   // 1-SM kernel: tmB1 is a 3-D map whose third coordinate selects B1 (0) or
   // B2 (1), so one copy brings both tiles of a K block (see b_pair_map)
   int b_merged;
+  // NVFP4DG_FLAG_STATIC_WEIGHTS: the weight producer (warp 5: B1/B2 tiles and
+  // all B scale runs) starts before the dependency wait; the activation
+  // producer (warp 4: A and its scales) still waits
+  int static_weights;
 };
 
 __device__ unsigned g_err_word;
@@ -759,7 +763,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      griddep_wait();  // global memory only after the previous grid
+      // global memory only after the previous grid, except for the weights
+      // when the caller declares them unwritten by earlier kernels
+      const bool w_early = p.static_weights != 0;
+      if (a_side || !w_early) griddep_wait();
       if (a_side) NVFP4DG_STAMP(1, 62);
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
@@ -777,11 +784,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (a_side) {
             bulk_load(sf_dst, sfa_src + run, kSfRunBytes, &sfdata_bar[stage],
                       pol);
-            bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
-                      kSfRunBytes, &sfdata_bar[stage], pol);
+            if (!w_early)
+              bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
+                        kSfRunBytes, &sfdata_bar[stage], pol);
             tma_load_3d(st, &tmA, &full_bar[stage], kb * kRowBytes,
                         m_tile * kBM, l, pol);
           } else {
+            if (w_early)
+              bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
+                        kSfRunBytes, &sfdata_bar[stage], pol);
             bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
             // (the merged map's third coordinate picks B1 / B2; it is only
@@ -1272,7 +1283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       long long issued = 0;
       bool ok = true;
-      griddep_wait();  // global memory only after the previous grid
+      // global memory only after the previous grid, except for the weights
+      // when the caller declares them unwritten by earlier kernels
+      const bool w_early = p.static_weights != 0;
+      if (a_side || !w_early) griddep_wait();
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (issued >= S &&
@@ -1294,8 +1308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                   mapa_shared(smem_u32(&empty_bar[stage]), lead + 1u));
             bulk_load(sf_dst, sfa_src + run, kSfRunBytes, &sfdata_bar[stage],
                       pol);
-            bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
-                      kSfRunBytes, &sfdata_bar[stage], pol);
+            if (!w_early)
+              bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
+                        kSfRunBytes, &sfdata_bar[stage], pol);
             // unbatched problems use 2-D maps, batched ones 3-D maps whose
             // third coordinate is the batch
             if (plan.L == 1)
@@ -1305,6 +1320,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                pol);
             NVFP4DG_STAMP(1, issued);
           } else {
+            if (w_early)
+              bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
+                        kSfRunBytes, &sfdata_bar[stage], pol);
             bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
             if (plan.L == 1)
@@ -2275,6 +2293,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
                    : nullptr;
   kp.err = dev.err;
   kp.b_merged = merged ? 1 : 0;
+  kp.static_weights = (flags & NVFP4DG_FLAG_STATIC_WEIGHTS) ? 1 : 0;
   // Programmatic dependent launch lets this grid be scheduled while the
   // previous one in the stream finishes (the kernel waits for it before its
   // first global access); clusters as set below.
@@ -2588,6 +2607,9 @@ int run_host_impl(const void* A, const void* B1, const void* B2,
   if (slabs < 0 || slabs > kMaxSlabs)
     return fail(NVFP4DG_ERR_INVALID,
                 "slabs must be 0 (automatic) to " + std::to_string(kMaxSlabs));
+  // The staging buffer's weights are rewritten by every call's uploads, so
+  // the weights may never be read before the dependency wait here.
+  flags &= ~NVFP4DG_FLAG_STATIC_WEIGHTS;
   // Host buffers need no alignment (the copies take any address).
   int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags,
                          false);

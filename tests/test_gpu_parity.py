@@ -454,3 +454,38 @@ def test_scale_layout_converter(rows, k, pitch):
     back = dg.scales_from_blocked(blk, rows, k)
     torch.cuda.synchronize()
     assert np.array_equal(back.cpu().numpy(), wide[:, :kb])
+
+
+@pytest.mark.parametrize("flags", [
+    0,
+    _lib.FLAG_SPLITK | _lib.FLAG_PAIR | _lib.FLAG_BN128,
+    _lib.FLAG_SPLITK | _lib.FLAG_NO_PAIR | _lib.FLAG_BN64,
+    _lib.FLAG_NO_PAIR | _lib.FLAG_NO_STREAMK | _lib.FLAG_BN128,
+    5 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_PAIR | _lib.FLAG_BN128,
+])
+def test_static_weights_back_to_back(flags):
+    # Weight copies issued before the dependency wait: several calls with
+    # the same weights and different activations, queued back to back with
+    # no synchronisation between them, each checked against the oracle.
+    base = O.make_problem(256, 512, 2048, seed=31)
+    d = to_device(base)
+    flags |= _lib.FLAG_STATIC_WEIGHTS
+    outs, refs = [], []
+    for i in range(3):
+        p = O.make_problem(256, 512, 2048, seed=40 + i)
+        q = dict(base, a=p["a"], sfa=p["sfa"], sfa_blocked=p["sfa_blocked"])
+        a = torch.from_numpy(q["a"]).cuda()
+        sfa = torch.from_numpy(q["sfa_blocked"]).cuda()
+        c = torch.full((256, 512), float("nan"), dtype=torch.float16,
+                       device="cuda")
+        dg.dual_gemm(a, d["b1"], d["b2"], sfa, d["sfb1_blocked"],
+                     d["sfb2_blocked"], c, flags=flags)
+        outs.append(c)
+        refs.append(O.reference_output(q))
+    torch.cuda.synchronize()
+    for i, (c, ref) in enumerate(zip(outs, refs)):
+        assert_close(c.cpu().numpy(), ref, f"call {i} flags {flags:#x}")
+    import ctypes
+    word = ctypes.c_uint(123)
+    rc = _lib.load().nvfp4_dual_gemm_device_status(0, ctypes.byref(word))
+    assert rc == 0 and word.value == 0  # no bounded wait expired
