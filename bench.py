@@ -533,6 +533,11 @@ PLUMBING = {
     "batched": dict(rows=256, K=7168, N=4096, L=8,
                     name="batched dual GEMM, L = 8 problems of C2's shape "
                          "(256x4096x7168) in one launch vs 8 launches"),
+    "grouped": dict(rows=[512, 300, 128, 64, 40, 8, 0, 200], K=7168,
+                    N=2048,
+                    name="grouped dual GEMM (MoE FFN): 8 experts, N = 2048, "
+                         "K = 7168, 1252 tokens in skewed groups, one launch "
+                         "vs one launch per expert"),
     "nvfp4_out": dict(rows=256, K=7168, N=4096,
                       name="dual GEMM with NVFP4 output (C2 256x4096x7168): "
                            "fused quantising epilogue vs fp16 C + quantiser"),
@@ -552,11 +557,13 @@ def run_plumbing(args):
     rows, k = cfg["rows"], cfg["K"]
     lib = _lib.load()
     stream = lambda: torch.cuda.current_stream().cuda_stream  # noqa: E731
-    blocked = ((rows + 127) // 128) * (k // 64) * 512
     if args.plumbing == "nvfp4_out":
         return run_nvfp4_out(args, cfg)
     if args.plumbing == "batched":
         return run_batched(args, cfg)
+    if args.plumbing == "grouped":
+        return run_grouped(args, cfg)
+    blocked = ((rows + 127) // 128) * (k // 64) * 512
     if args.plumbing == "quantize":
         dt = getattr(torch, cfg["dtype"])
         per = rows * k * 2 + rows * k // 2 + blocked
@@ -659,6 +666,75 @@ def run_batched(args, cfg):
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4),
+                     "algorithmic_bytes": per,
+                     "peak_source": f"{peaks['source']} HBM copy GB/s"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+
+
+def run_grouped(args, cfg):
+    """Experts with their own token counts in one launch
+    (``dual_gemm_grouped``) against one launch per non-empty expert on the
+    same buffers; both graph-timed over rotating input sets > 2 x L2."""
+    import nvfp4_dual_gemm_b200 as dg
+
+    rows, n, k = cfg["rows"], cfg["N"], cfg["K"]
+    G = len(rows)
+    row0 = dg.group_offsets(rows)
+    R = max(r + m for r, m in zip(row0, rows) if m)
+    blk_a = ((R + 127) // 128) * (k // 64) * 512
+    blk_b = ((n + 127) // 128) * (k // 64) * 512
+    per = R * k // 2 + blk_a + G * (n * k + 2 * blk_b) + 2 * R * n
+    nsets = max(2, math.ceil(2 * L2_BYTES / per))
+    sets = []
+    for s_ in range(nsets):
+        a = dg.generate_input(R, n, k, l=1, seed=100 + s_)  # A rows, SFA
+        w = dg.generate_input(128, n, k, l=G, seed=200 + s_)  # experts
+        sets.append((a[0].squeeze(-1), w[1], w[2], a[6], w[7], w[8],
+                     torch.empty((R, n), dtype=torch.float16, device="cuda")))
+    torch.cuda.synchronize()
+    ws = torch.zeros(1 << 24, dtype=torch.uint8, device="cuda")
+    # one problem per expert: slices of the same buffers
+    def per_expert(i):
+        d = sets[i % nsets]
+        for g in range(G):
+            if rows[g] == 0:
+                continue
+            rs = slice(row0[g], row0[g] + rows[g])
+            dg.dual_gemm(d[0][rs], d[1][..., g], d[2][..., g],
+                         d[3][(row0[g] // 128) * (k // 64) * 512:],
+                         d[4][g * blk_b:(g + 1) * blk_b],
+                         d[5][g * blk_b:(g + 1) * blk_b], d[6][rs],
+                         workspace=ws)
+
+    wsg = torch.zeros(max(dg.grouped_workspace_size(rows, n, k), 256),
+                      dtype=torch.uint8, device="cuda")
+
+    def grouped(i):
+        d = sets[i % nsets]
+        dg.dual_gemm_grouped(*d, rows, workspace=wsg)
+
+    ms_g, clocks = time_graph(grouped, args.steps, args.warmup, 1)
+    ms_e, _ = time_graph(per_expert, args.steps, args.warmup, 1)
+    us_g = ms_g * 1e3 / args.steps
+    us_e = ms_e * 1e3 / args.steps
+    flops = 4 * sum(rows) * n * k
+    peaks = load_peaks()
+    return {
+        "metric": cfg["name"], "value": round(flops / (us_g * 1e-6) / 1e12, 3),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_g / args.steps,
+        "us_per_call": round(us_g, 3),
+        "per_expert_launches_us_per_call": round(us_e, 3),
+        "higher_is_better": True, "data": "synthetic: seeded randn -> NVFP4",
+        "config": {"workload": "grouped", "group_rows": rows, "N": n, "K": k,
+                   "l2": f"{nsets} rotating input sets (> 2 x 126 MB L2)",
+                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+        "roofline": {"bound": "hbm",
+                     "achieved": round(per / (us_g * 1e-6) / 1e9, 1),
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(per / (us_g * 1e-6) / 1e9 /
+                                   peaks["hbm_gbs"], 4),
                      "algorithmic_bytes": per,
                      "peak_source": f"{peaks['source']} HBM copy GB/s"},
         "gpu_launches": args.steps, "clocks": clocks,

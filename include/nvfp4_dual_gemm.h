@@ -165,6 +165,39 @@ NVFP4DG_API int nvfp4_dual_gemm_run_nvfp4_out(
     int K, int L, unsigned flags, void* stream);
 
 /*
+ * Grouped dual GEMM (mixture-of-experts FFN): `groups` (1..64) problems that
+ * share N and K but have their own row counts, in one launch.  Group g's
+ * activations are rows [group_row0[g], group_row0[g] + group_rows[g]) of A,
+ * SFA and C (group_row0[g] a multiple of 128; groups in increasing order,
+ * each group's rows rounded up to 128 ending before the next group starts;
+ * rows between groups are neither read into any output nor written), and its
+ * weights are batch g of B1, B2, SFB1, SFB2 (per-batch sizes as at the top of
+ * this file).  A / C hold max(group_row0[g] + group_rows[g]) rows, SFA the
+ * blocked layout of that many rows.  group_rows / group_row0 are HOST arrays,
+ * read during the call.  Groups may be empty.  Schedules: 2-SM pair or
+ * single-CTA tiles, whole tiles or stream-K (NVFP4DG_FLAG_SPLITK is
+ * rejected); `workspace` as for nvfp4_dual_gemm_run_ws (NULL: the library's
+ * own), flags otherwise as for nvfp4_dual_gemm_run.  The
+ * reference has no grouped form: its tensors' L dimension is ignored
+ * (nvfp4_dual_gemm.cu:381-446).
+ */
+NVFP4DG_API int nvfp4_dual_gemm_run_grouped(
+    const void* A, const void* B1, const void* B2, const void* SFA,
+    const void* SFB1, const void* SFB2, void* C, const int* group_rows,
+    const int* group_row0, int groups, int N, int K, unsigned flags,
+    void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Bytes of caller-owned workspace nvfp4_dual_gemm_run_grouped needs for
+ * these group row counts (0 when its schedule splits no tile along K).
+ * With workspace == NULL, nvfp4_dual_gemm_run_grouped uses the library's
+ * per-(device, stream) workspace instead, as nvfp4_dual_gemm_run does.  No
+ * counterpart in the reference.
+ */
+NVFP4DG_API size_t nvfp4_dual_gemm_grouped_workspace_size(
+    const int* group_rows, int groups, int N, int K, unsigned flags);
+
+/*
  * Quantise fp32 rows to NVFP4 on the GPU: X is [rows, K] fp32 row-major;
  * writes codes [rows, K/2] (low nibble = even element), the plain scales
  * [rows, K/16] and the blocked scales (ceil(rows/128) * (K/64) * 512 bytes;

@@ -8,9 +8,12 @@ from .api import (  # noqa: F401
     cuda_nvfp4_dual_gemm,
     custom_kernel,
     dual_gemm,
+    dual_gemm_grouped,
     dual_gemm_host,
     dual_gemm_nvfp4,
     generate_input,
+    group_offsets,
+    grouped_workspace_size,
     host_staging_size,
     plan,
     plan_work,

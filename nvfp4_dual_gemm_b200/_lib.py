@@ -63,6 +63,9 @@ SIGNATURES = {
                                                      _vp]),
     "nvfp4_dual_gemm_run_nvfp4_out": (_i, [_vp] * 8 + [_i, _i, _i, _i, _u,
                                                        _vp]),
+    "nvfp4_dual_gemm_run_grouped": (_i, [_vp] * 7 + [_ip, _ip, _i, _i, _i,
+                                                     _u, _vp, _sz, _vp]),
+    "nvfp4_dual_gemm_grouped_workspace_size": (_sz, [_ip, _i, _i, _i, _u]),
     "nvfp4_quantize": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
     "nvfp4_quantize_rows": (_i, [_vp, _i, _i, _i, ctypes.c_longlong, _vp, _vp,
                                  _vp, _vp]),

@@ -224,6 +224,79 @@ def dual_gemm_nvfp4(A, B1, B2, SFA, SFB1, SFB2, Cq=None, SFC=None, *,
     return Cq, SFC
 
 
+def group_offsets(group_rows) -> list[int]:
+    """Default first rows of the groups: each group's rows rounded up to 128,
+    one group after another."""
+    out, r = [], 0
+    for n in group_rows:
+        out.append(r)
+        r += (int(n) + 127) // 128 * 128
+    return out
+
+
+def grouped_workspace_size(group_rows, N: int, K: int,
+                           flags: int = 0) -> int:
+    """Bytes of caller-owned workspace :func:`dual_gemm_grouped` needs."""
+    rows = [int(n) for n in group_rows]
+    lib = _lib.load()
+    return int(lib.nvfp4_dual_gemm_grouped_workspace_size(
+        (ctypes.c_int * len(rows))(*rows), len(rows), N, K, flags))
+
+
+def dual_gemm_grouped(A, B1, B2, SFA, SFB1, SFB2, C, group_rows,
+                      group_row0=None, *, flags: int = 0,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped dual GEMM (a mixture-of-experts FFN) in one launch: group g
+    computes rows [row0[g], row0[g] + group_rows[g]) of C from the same rows
+    of A / SFA and expert g's weights (batch g of B1, B2 [N, K/2, G] and of
+    SFB1 / SFB2, G blocked layouts one after another).  ``group_row0``
+    (multiples of 128, increasing, non-overlapping once each group's rows are
+    rounded up to 128) defaults to :func:`group_offsets`.  A is [R, K/2], SFA
+    the blocked layout of R rows and C [R, N] with R = max(row0 + rows); rows
+    outside the groups are not written (``nvfp4_dual_gemm_run_grouped``).
+    ``workspace`` (zero-initialised uint8 CUDA tensor of at least
+    :func:`grouped_workspace_size` bytes) makes the call allocation-free,
+    e.g. for CUDA graph capture; otherwise the library keeps one."""
+    rows = [int(n) for n in group_rows]
+    G = len(rows)
+    row0 = group_offsets(rows) if group_row0 is None else \
+        [int(r) for r in group_row0]
+    if len(row0) != G:
+        raise ValueError("group_row0 needs one entry per group")
+    R = max([r + n for r, n in zip(row0, rows) if n > 0], default=0)
+    for name, t in (("A", A), ("B1", B1), ("B2", B2)):
+        _check_bytes(name, t, True)
+    N = B1.size(0)
+    K = 2 * B1.size(1) if B1.dim() >= 2 else 0
+    _rows_dense("A", A, A.size(0), K // 2)
+    if A.size(0) < R:
+        raise ValueError(f"A has {A.size(0)} rows, the groups need {R}")
+    _rows_dense("B1", B1, N, K // 2, G)
+    _rows_dense("B2", B2, N, K // 2, G)
+    _check_blocked("SFA", SFA, A.size(0), K, True)
+    _check_blocked("SFB1", SFB1, N, K, True, G)
+    _check_blocked("SFB2", SFB2, N, K, True, G)
+    if (C.dtype != torch.float16 or not C.is_cuda or not C.is_contiguous()
+            or C.dim() != 2 or C.size(1) != N or C.size(0) < R):
+        raise ValueError(f"C must be a contiguous CUDA float16 [>= {R}, {N}] "
+                         "tensor")
+    dev = C.device
+    for name, t in (("A", A), ("B1", B1), ("B2", B2), ("SFA", SFA),
+                    ("SFB1", SFB1), ("SFB2", SFB2)):
+        if t.device != dev:
+            raise ValueError(f"{name} is on {t.device}, C on {dev}")
+    arr = ctypes.c_int * G
+    lib = _lib.load()
+    with torch.cuda.device(dev):
+        rc = lib.nvfp4_dual_gemm_run_grouped(
+            _ptr(A), _ptr(B1), _ptr(B2), _ptr(SFA), _ptr(SFB1), _ptr(SFB2),
+            _ptr(C), arr(*rows), arr(*row0), G, N, K, flags,
+            None if workspace is None else _ptr(workspace),
+            0 if workspace is None else workspace.numel(), _stream(dev))
+    _lib.check(rc, "nvfp4_dual_gemm_run_grouped")
+    return C
+
+
 def host_staging_size(M: int, N: int, K: int) -> int:
     """Bytes of device staging :func:`dual_gemm_host` needs (host-only)."""
     lib = _lib.load()

@@ -23,6 +23,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <vector>
 #include <mutex>
 #include <string>
 #include <utility>
@@ -64,6 +65,19 @@ struct Cfg {
                 "stream-K fixup staging reuses the stage buffers");
 };
 
+// Grouped problems (nvfp4_dual_gemm_run_grouped): `count` problems sharing N
+// and K whose activations (rows of A, SFA, C) are concatenated, group g at
+// rows [row0[g], row0[g] + rows[g]) with row0[g] a multiple of 128, and whose
+// weights are batches g of B1 / B2 / SFB1 / SFB2.  Linear tiles [tile0[g],
+// tile0[g + 1]) belong to group g (m fastest, as for one problem).
+constexpr int kMaxGroups = 64;
+struct GroupTable {
+  int count;  // 0: not a grouped launch
+  int tile0[kMaxGroups + 1];
+  int row0[kMaxGroups];
+  int rows[kMaxGroups];
+};
+
 struct KParams {
   Plan plan;
   int M, N, K;
@@ -93,6 +107,9 @@ struct KParams {
   // all B scale runs) starts before the dependency wait; the activation
   // producer (warp 4: A and its scales) still waits
   int static_weights;
+  // pair kernel: 3-D tensor maps (batch / group coordinate) instead of 2-D
+  int maps3d;
+  GroupTable groups;
 };
 
 __device__ unsigned g_err_word;
@@ -288,21 +305,58 @@ __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
   }
 }
 
-__device__ __forceinline__ OutRow out_row(const KParams& p, int l, int grow,
-                                          int col0) {
+// Where a linear tile lies: its batch (or group) l, its tile coordinates in
+// that problem, and the problem's rows (first row in A / SFA / C, count).
+struct TileLoc {
+  int l, m_tile, n_tile, row0, rows;
+};
+
+__device__ __forceinline__ TileLoc locate(const KParams& p, int tile) {
+  TileLoc t;
+  if (p.groups.count == 0) {
+    tile_lmn(p.plan, tile, t.l, t.m_tile, t.n_tile);
+    t.row0 = 0;
+    t.rows = p.M;
+    return t;
+  }
+  // the last group whose first tile is <= tile (empty groups have no tiles)
+  int lo = 0, hi = p.groups.count - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.groups.tile0[mid] <= tile)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  const int local = tile - p.groups.tile0[lo];
+  const int span = kBM * p.plan.ctas;
+  const int mt = (p.groups.rows[lo] + span - 1) / span;
+  t.l = lo;
+  t.n_tile = local / mt;
+  t.m_tile = local - t.n_tile * mt;
+  t.row0 = p.groups.row0[lo];
+  t.rows = p.groups.rows[lo];
+  return t;
+}
+
+// Output row `grow` (counted within the tile's problem) of the tile at `t`.
+__device__ __forceinline__ OutRow out_row(const KParams& p, const TileLoc& t,
+                                          int grow, int col0) {
   OutRow o;
   o.col0 = col0;
-  o.row_ok = grow < p.M;
-  const size_t mn = (size_t)l * p.M * p.N;  // elements before batch l
+  o.row_ok = grow < t.rows;
+  // rows of C before this one: whole earlier batches, or the group's offset
+  const size_t r = (size_t)t.l * (p.groups.count ? 0 : p.M) + t.row0 + grow;
   if (p.cq != nullptr) {
     o.c = nullptr;
-    o.q = p.cq + mn / 2 + (size_t)grow * (p.N / 2) + col0 / 2;
-    o.sf = p.sfc + (size_t)l * p.sfc_batch +
-           (size_t)(grow / 128) * (p.N / 64) * kSfAtomBytes +
-           (grow % 32) * 16 + ((grow % 128) / 32) * 4;
-    o.sf_ok = grow < (p.M + 127) / 128 * 128;
+    o.q = p.cq + r * (p.N / 2) + col0 / 2;
+    const int sr = t.row0 + grow;  // row in its blocked scale layout
+    o.sf = p.sfc + (size_t)(p.groups.count ? 0 : t.l) * p.sfc_batch +
+           (size_t)(sr / 128) * (p.N / 64) * kSfAtomBytes + (sr % 32) * 16 +
+           ((sr % 128) / 32) * 4;
+    o.sf_ok = grow < (t.rows + 127) / 128 * 128;
   } else {
-    o.c = p.C + mn + (size_t)grow * p.N + col0;
+    o.c = p.C + r * p.N + col0;
     o.q = nullptr;
     o.sf = nullptr;
     o.sf_ok = false;
@@ -520,7 +574,7 @@ template <int BN>
 __device__ __forceinline__ void split_epilogue(
     const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
     uint64_t* ready_bar, uint64_t* recv_bar, int warp, int lane, int part,
-    int own, uint32_t xpeer, int l, int grow0, int n_tile,
+    int own, uint32_t xpeer, const TileLoc& loc, int grow0, int n_tile,
     bool& cluster_waited) {
   constexpr int kHalf = BN / 2;
   constexpr int kHalfChunks = kHalf / 16;
@@ -529,7 +583,7 @@ __device__ __forceinline__ void split_epilogue(
   const int row = 32 * (warp % 4) + lane;
   const uint32_t t_row = tmem + (static_cast<uint32_t>(32 * (warp % 4)) << 16);
   const int grow = grow0 + row;
-  const OutRow out = out_row(p, l, grow, n_tile * BN);
+  const OutRow out = out_row(p, loc, grow, n_tile * BN);
 
   griddep_wait();  // global memory only after the previous grid
   bool ok = mbar_wait(acc_full_bar, 0, p.err, kErrEpilogue);
@@ -629,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB1,
                      const __grid_constant__ CUtensorMap tmB2,
-                     const KParams p) {
+                     const __grid_constant__ KParams p) {
   using Cf = Cfg<BN>;
   constexpr int S = Cf::kStages;
   constexpr uint32_t kBytesA = Cf::kABytes;
@@ -707,9 +761,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool cluster_waited = false;
   // Split-K: this CTA's half of K (= its cluster rank) and its tile.
   const int split_own = static_cast<int>(blockIdx.x & 1);
-  int split_l, split_m_tile, split_n_tile;
-  tile_lmn(plan, static_cast<int>(blockIdx.x >> 1), split_l, split_m_tile,
-           split_n_tile);
+  const TileLoc split_loc = locate(p, static_cast<int>(blockIdx.x >> 1));
+  const int split_m_tile = split_loc.m_tile, split_n_tile = split_loc.n_tile;
   // Everything above touched only this CTA's on-chip state; the inputs, C and
   // the workspace may be written by the previous grid in the stream.
   // Each role waits for the previous grid (griddepcontrol.wait) only after
@@ -747,10 +800,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     int l = 0, m_tile = 0, n_tile = 0;
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
+    int a_row = 0, a_layer = 0;
     auto place = [&] {
-      tile_lmn(plan, w.tile, l, m_tile, n_tile);
-      sfa_src = p.sfa + (size_t)l * p.sfa_batch +
-                (size_t)m_tile * kblk64 * kSfAtomBytes;
+      const TileLoc t = locate(p, w.tile);
+      l = t.l;
+      m_tile = t.m_tile;
+      n_tile = t.n_tile;
+      // A and SFA: rows of batch l, or the group's rows of the one matrix
+      a_row = t.row0 + m_tile * kBM;
+      a_layer = p.groups.count ? 0 : l;
+      sfa_src = p.sfa + (size_t)a_layer * p.sfa_batch +
+                (size_t)(a_row / kBM) * kblk64 * kSfAtomBytes;
       sfb_off = (size_t)l * p.sfb_batch +
                 (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
     };
@@ -787,8 +847,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!w_early)
               bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
                         kSfRunBytes, &sfdata_bar[stage], pol);
-            tma_load_3d(st, &tmA, &full_bar[stage], kb * kRowBytes,
-                        m_tile * kBM, l, pol);
+            tma_load_3d(st, &tmA, &full_bar[stage], kb * kRowBytes, a_row,
+                        a_layer, pol);
           } else {
             if (w_early)
               bulk_load(sf_dst + kSfRunBytes, p.sfb1 + sfb_off + run,
@@ -846,8 +906,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (; ok && have; have = work_next(plan, it, w)) {
       // BN = 64: the tile's B rows are one half of a 128-row atom, i.e.
       // atom words 2h and 2h+1 (rows 64h .. 64h+63).
-      int l_, m_tile, n_tile;
-      tile_lmn(plan, w.tile, l_, m_tile, n_tile);
+      const int n_tile = locate(p, w.tile).n_tile;
       const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got = mbar_wait(&sfdata_bar[stage], phase, p.err, kErrMma);
@@ -929,7 +988,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                         warp, lane, 1, split_own, split_own ^ 1u, split_l,
+                         warp, lane, 1, split_own, split_own ^ 1u, split_loc,
                          split_m_tile * kBM, split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -1000,7 +1059,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                       warp, lane, 0, split_own, split_own ^ 1u, split_l,
+                       warp, lane, 0, split_own, split_own ^ 1u, split_loc,
                        split_m_tile * kBM, split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
@@ -1018,10 +1077,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit);
       tc_fence_after();
-      int l, m_tile, n_tile;
-      tile_lmn(plan, w.tile, l, m_tile, n_tile);
-      const int grow = m_tile * kBM + row;
-      const OutRow out = out_row(p, l, grow, n_tile * BN);
+      const TileLoc loc = locate(p, w.tile);
+      const int n_tile = loc.n_tile;
+      const int grow = loc.m_tile * kBM + row;
+      const OutRow out = out_row(p, loc, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -1146,7 +1205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB1,
                           const __grid_constant__ CUtensorMap tmB2,
-                          const KParams p) {
+                          const __grid_constant__ KParams p) {
   using Cf = PairCfg<BN>;
   constexpr int S = Cf::kStages;
 
@@ -1182,8 +1241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
   // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
   const int split_own = static_cast<int>(crank >> 1);
-  int split_l, split_m_tile, split_n_tile;
-  tile_lmn(plan, unit >> 1, split_l, split_m_tile, split_n_tile);
+  const TileLoc split_loc = locate(p, unit >> 1);
+  const int split_m_tile = split_loc.m_tile, split_n_tile = split_loc.n_tile;
   const int split_grow0 =
       split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
   bool cluster_waited = true;  // the start-up cluster barrier (below)
@@ -1256,20 +1315,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     work_begin(plan, unit, it);
     Work w;
     bool have = work_next(plan, it, w);
-    int l = 0, n_tile = 0, a_row = 0;
+    int l = 0, n_tile = 0, a_row = 0, a_layer = 0;
     const uint8_t* sfa_src = nullptr;
     size_t sfb_off = 0;
     auto place = [&] {
-      int m_tile;
-      tile_lmn(plan, w.tile, l, m_tile, n_tile);
-      a_row = m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
-      // SFA holds ceil(M / 128) row blocks.  When the odd CTA's 128 rows
-      // lie wholly past M (M in (256t, 256t + 128] for the last pair tile)
-      // it copies the last block instead: its A rows are zero-filled by the
-      // tensor map and its accumulator rows are never stored.
-      const int a_blk = min(m_tile * 2 + static_cast<int>(rank),
-                            (p.M + kBM - 1) / kBM - 1);
-      sfa_src = p.sfa + (size_t)l * p.sfa_batch +
+      const TileLoc t = locate(p, w.tile);
+      l = t.l;
+      n_tile = t.n_tile;
+      // A and SFA: rows of batch l, or the group's rows of the one matrix
+      a_layer = p.groups.count ? 0 : l;
+      a_row = t.row0 + t.m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+      // A problem's SFA holds ceil(rows / 128) row blocks.  When the odd
+      // CTA's 128 rows lie wholly past them (rows in (256t, 256t + 128] for
+      // the last pair tile) it copies the last block instead: its A rows are
+      // zero-filled by the tensor map (or belong to the next group) and its
+      // accumulator rows are never stored.
+      const int a_blk = t.row0 / kBM +
+                        min(t.m_tile * 2 + static_cast<int>(rank),
+                            (t.rows + kBM - 1) / kBM - 1);
+      sfa_src = p.sfa + (size_t)a_layer * p.sfa_batch +
                 (size_t)a_blk * kblk64 * kSfAtomBytes;
       sfb_off = (size_t)l * p.sfb_batch +
                 (size_t)((n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
@@ -1313,11 +1377,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kSfRunBytes, &sfdata_bar[stage], pol);
             // unbatched problems use 2-D maps, batched ones 3-D maps whose
             // third coordinate is the batch
-            if (plan.L == 1)
+            if (!p.maps3d)
               tma_load_2d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, pol);
             else
-              tma_load_3d_pair(st, &tmA, full_s, kb * kRowBytes, a_row, l,
-                               pol);
+              tma_load_3d_pair(st, &tmA, full_s, kb * kRowBytes, a_row,
+                               a_layer, pol);
             NVFP4DG_STAMP(1, issued);
           } else {
             if (w_early)
@@ -1325,7 +1389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kSfRunBytes, &sfdata_bar[stage], pol);
             bulk_load(sf_dst + 2 * kSfRunBytes, p.sfb2 + sfb_off + run,
                       kSfRunBytes, &sfdata_bar[stage], pol);
-            if (plan.L == 1)
+            if (!p.maps3d)
               tma_load_2d_pair(st + Cf::kABytes, rank == 0 ? &tmB1 : &tmB2,
                                full_s, kb * kRowBytes, n_tile * BN, pol);
             else
@@ -1371,8 +1435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool have = work_next(plan, it, w);
     griddep_wait();  // global memory only after the previous grid
     for (; ok && have; have = work_next(plan, it, w)) {
-      int l_, m_tile, n_tile;
-      tile_lmn(plan, w.tile, l_, m_tile, n_tile);
+      const int n_tile = locate(p, w.tile).n_tile;
       const int half = (BN == 64) ? (n_tile & 1) : 0;
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         const bool got =
@@ -1454,7 +1517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Split-K: the scale warps help finish the tile.
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                         warp, lane, 1, split_own, crank ^ 2u, split_l,
+                         warp, lane, 1, split_own, crank ^ 2u, split_loc,
                          split_grow0, split_n_tile, cluster_waited);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
@@ -1527,7 +1590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
-                       warp, lane, 0, split_own, crank ^ 2u, split_l,
+                       warp, lane, 0, split_own, crank ^ 2u, split_loc,
                        split_grow0, split_n_tile, cluster_waited);
   } else {
     // ------------------------------------------------------------ epilogue
@@ -1547,10 +1610,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!group_all<1>(got)) break;  // the four warps leave together
       if (threadIdx.x == 0) NVFP4DG_STAMP(4, unit_i);
       tc_fence_after();
-      int l, m_tile, n_tile;
-      tile_lmn(plan, w.tile, l, m_tile, n_tile);
-      const int grow = m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
-      const OutRow out = out_row(p, l, grow, n_tile * BN);
+      const TileLoc loc = locate(p, w.tile);
+      const int n_tile = loc.n_tile;
+      const int grow =
+          loc.m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
+      const OutRow out = out_row(p, loc, grow, n_tile * BN);
       if (w.slot < 0) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -2244,7 +2308,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
            const void* B1, const void* B2, const void* SFA, const void* SFB1,
            const void* SFB2, void* C, int M, int N, int K, void* ws,
            unsigned flags, cudaStream_t stream, void* cq = nullptr,
-           void* sfc = nullptr) {
+           void* sfc = nullptr, const GroupTable* groups = nullptr) {
   constexpr int kSmem = PAIR ? PairCfg<BN>::kSmemBytes : Cfg<BN>::kSmemBytes;
   auto kernel = PAIR ? dual_gemm_pair_kernel<BN> : dual_gemm_kernel<BN>;
   bool& attr = PAIR ? (BN == 64 ? dev.attr64p : dev.attr128p)
@@ -2261,17 +2325,24 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   // both weight tiles of a K block in one copy when a single map can cover
   // B1 and B2.  Batched problems (L > 1) use 3-D maps in both kernels, the
   // batch being the third coordinate, and separate B1 / B2 maps.
-  const int L = plan.L;
-  const int rank = (PAIR && L == 1) ? 2 : 3;
-  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta, rank, L))) return rc;
-  const bool merged = !PAIR && L == 1 &&
+  // Grouped problems: A is one matrix of M (all groups') rows, the weights
+  // one batch per group.
+  const int a_layers = groups ? 1 : plan.L;
+  const int b_layers = groups ? groups->count : plan.L;
+  const bool maps3d = !PAIR || a_layers > 1 || b_layers > 1;
+  const int rank = maps3d ? 3 : 2;
+  if ((rc = tensor_map(A, M, K / 2, kBM, devid, &ta, rank, a_layers)))
+    return rc;
+  const bool merged = !PAIR && b_layers == 1 &&
                       !(flags & NVFP4DG_FLAG_NO_MERGED_B) &&
                       b_pair_map(B1, B2, N, K / 2, BN, devid, &tb1);
   if (merged) {
     tb2 = tb1;
   } else {
-    if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1, rank, L))) return rc;
-    if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2, rank, L))) return rc;
+    if ((rc = tensor_map(B1, N, K / 2, BN, devid, &tb1, rank, b_layers)))
+      return rc;
+    if ((rc = tensor_map(B2, N, K / 2, BN, devid, &tb2, rank, b_layers)))
+      return rc;
   }
   KParams kp;
   kp.plan = plan;
@@ -2294,6 +2365,12 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.err = dev.err;
   kp.b_merged = merged ? 1 : 0;
   kp.static_weights = (flags & NVFP4DG_FLAG_STATIC_WEIGHTS) ? 1 : 0;
+  kp.maps3d = maps3d ? 1 : 0;
+  if (groups) {
+    kp.groups = *groups;
+  } else {
+    kp.groups.count = 0;
+  }
   // Programmatic dependent launch lets this grid be scheduled while the
   // previous one in the stream finishes (the kernel waits for it before its
   // first global access); clusters as set below.
@@ -2346,12 +2423,57 @@ int read_status(int dev, unsigned* word) {
   return rc;
 }
 
+// Grouped problems: the schedule over all groups' tiles (m fastest within a
+// group, then n, then the group) and the kernels' group table.  Cluster
+// split-K is not used; among 2-SM pair and single-CTA tiles, each tile width
+// and stream-K or not, the plan with the least modelled cost is taken, the
+// m tiles of all groups counting as the rows of one problem.
+Plan choose_plan_grouped(const int* rows, const int* row0, int G, int N,
+                         int K, unsigned flags, int sms, GroupTable* table) {
+  Plan best{};
+  double best_cost = 1e300;
+  for (int ctas = 2; ctas >= 1; --ctas) {
+    if (ctas == 2 && (flags & NVFP4DG_FLAG_NO_PAIR)) continue;
+    if (ctas == 1 && (flags & NVFP4DG_FLAG_PAIR)) continue;
+    long long mt = 0;
+    for (int g = 0; g < G; ++g)
+      mt += (rows[g] + kBM * ctas - 1) / (kBM * ctas);
+    if (mt == 0) continue;
+    const unsigned f = (flags & ~(NVFP4DG_FLAG_PAIR | NVFP4DG_FLAG_NO_PAIR)) |
+                       NVFP4DG_FLAG_NO_SPLITK |
+                       (ctas == 2 ? NVFP4DG_FLAG_PAIR : NVFP4DG_FLAG_NO_PAIR);
+    const Plan p = choose_plan(static_cast<int>(mt * kBM * ctas), N, K, f, sms);
+    if (p.grid == 0) continue;
+    const double c = plan_cost(p);
+    if (c < best_cost) {
+      best_cost = c;
+      best = p;
+    }
+  }
+  if (best.grid == 0) return best;
+  table->count = G;
+  int t = 0;
+  for (int g = 0; g < G; ++g) {
+    table->tile0[g] = t;
+    table->row0[g] = row0[g];
+    table->rows[g] = rows[g];
+    t += (rows[g] + kBM * best.ctas - 1) / (kBM * best.ctas) * best.n_tiles;
+  }
+  table->tile0[G] = t;
+  return best;
+}
+
 // `cq` / `sfc` not null: NVFP4 output (codes and blocked scales) instead of
 // the fp16 C, which is then unused (nvfp4_dual_gemm_run_nvfp4_out).
+// `G` > 0: grouped problems (nvfp4_dual_gemm_run_grouped); M is then the row
+// count of A and C over all groups, L is 1, and `group_rows` / `group_row0`
+// give each group's rows (validated by the caller).
 int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
              const void* SFB1, const void* SFB2, void* C, int M, int N, int K,
              int L, unsigned flags, void* ws, size_t ws_bytes, bool own_ws,
-             void* stream_ptr, void* cq = nullptr, void* sfc = nullptr) {
+             void* stream_ptr, void* cq = nullptr, void* sfc = nullptr,
+             const int* group_rows = nullptr, const int* group_row0 = nullptr,
+             int G = 0) {
   g_last_error.clear();
   const bool q_out = cq != nullptr || sfc != nullptr;
   int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, q_out ? cq : C, M, N, K,
@@ -2383,7 +2505,18 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   DevInfo* dev = nullptr;
   if ((rc = device_info(devid, &dev))) return rc;
-  const Plan plan = choose_plan(M, N, K, flags, dev->sms, L);
+  GroupTable table;
+  table.count = 0;
+  const GroupTable* groups = nullptr;
+  Plan plan;
+  if (G > 0) {
+    plan = choose_plan_grouped(group_rows, group_row0, G, N, K, flags,
+                               dev->sms, &table);
+    if (plan.grid == 0) return NVFP4DG_OK;  // every group is empty
+    groups = &table;
+  } else {
+    plan = choose_plan(M, N, K, flags, dev->sms, L);
+  }
   if (plan.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
                 "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
@@ -2420,16 +2553,20 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
   }
   if (plan.ctas == 2 && plan.bn == 128)
     rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, flags, stream, cq, sfc);
+                           N, K, ws, flags, stream, cq, sfc,
+                           groups);
   else if (plan.ctas == 2)
     rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                          N, K, ws, flags, stream, cq, sfc);
+                          N, K, ws, flags, stream, cq, sfc,
+                           groups);
   else if (plan.bn == 128)
     rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, flags, stream, cq, sfc);
+                            M, N, K, ws, flags, stream, cq, sfc,
+                           groups);
   else
     rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                           M, N, K, ws, flags, stream, cq, sfc);
+                           M, N, K, ws, flags, stream, cq, sfc,
+                           groups);
   if (rc) return rc;
   if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
     unsigned word = 0;
@@ -2733,6 +2870,80 @@ int nvfp4_dual_gemm_run(const void* A, const void* B1, const void* B2,
                         void* stream) {
   return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, nullptr, 0,
                   true, stream);
+}
+
+int nvfp4_dual_gemm_run_grouped(const void* A, const void* B1,
+                                const void* B2, const void* SFA,
+                                const void* SFB1, const void* SFB2, void* C,
+                                const int* group_rows, const int* group_row0,
+                                int groups, int N, int K, unsigned flags,
+                                void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  g_last_error.clear();
+  if (groups < 1 || groups > kMaxGroups)
+    return fail(NVFP4DG_ERR_INVALID,
+                "groups must be 1.." + std::to_string(kMaxGroups));
+  if (group_rows == nullptr || group_row0 == nullptr)
+    return fail(NVFP4DG_ERR_INVALID, "group_rows and group_row0 are required");
+  if (flags & NVFP4DG_FLAG_SPLITK)
+    return fail(NVFP4DG_ERR_INVALID,
+                "cluster split-K is not available for grouped problems");
+  long long next = 0, R = 0;
+  for (int g = 0; g < groups; ++g) {
+    const long long rows = group_rows[g], r0 = group_row0[g];
+    if (rows < 0 || r0 < 0 || r0 % kBM != 0)
+      return fail(NVFP4DG_ERR_INVALID,
+                  "group " + std::to_string(g) +
+                      ": rows must be >= 0 and the first row a multiple of "
+                      "128");
+    if (r0 < next)
+      return fail(NVFP4DG_ERR_INVALID,
+                  "group " + std::to_string(g) +
+                      " overlaps the previous one (each group's rows, rounded "
+                      "up to 128, must end before the next group starts)");
+    next = r0 + (rows + kBM - 1) / kBM * kBM;
+    if (rows > 0) R = std::max(R, r0 + rows);
+  }
+  if (next >= (1ll << 31))
+    return fail(NVFP4DG_ERR_INVALID, "too many rows");
+  const int M = static_cast<int>(R);
+  if (K == 0 && M > 0 && N > 0) {  // empty sums: each group's rows are 0
+    int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, 1, flags);
+    if (rc) return rc;
+    for (int g = 0; g < groups; ++g) {
+      if (group_rows[g] == 0) continue;
+      cudaError_t e = cudaMemsetAsync(
+          static_cast<__half*>(C) + (size_t)group_row0[g] * N, 0,
+          (size_t)group_rows[g] * N * sizeof(__half),
+          static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+    }
+    return NVFP4DG_OK;
+  }
+  return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, 1,
+                  flags | NVFP4DG_FLAG_NO_SPLITK, workspace, workspace_bytes,
+                  workspace == nullptr, stream, nullptr, nullptr, group_rows,
+                  group_row0, groups);
+}
+
+size_t nvfp4_dual_gemm_grouped_workspace_size(const int* group_rows,
+                                              int groups, int N, int K,
+                                              unsigned flags) {
+  g_last_error.clear();
+  if (group_rows == nullptr || groups < 1 || groups > kMaxGroups || N <= 0 ||
+      K <= 0 || N % 64 || K % 256)
+    return 0;
+  int devid = 0;
+  if (cudaGetDevice(&devid) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DevInfo* dev = nullptr;
+  if (device_info(devid, &dev)) return 0;
+  std::vector<int> row0(groups, 0);
+  GroupTable table;
+  const Plan p = choose_plan_grouped(group_rows, row0.data(), groups, N, K,
+                                     flags | NVFP4DG_FLAG_NO_SPLITK, dev->sms,
+                                     &table);
+  return p.grid == 0 ? 0 : static_cast<size_t>(workspace_bytes(p));
 }
 
 int nvfp4_dual_gemm_run_nvfp4_out(const void* A, const void* B1,
