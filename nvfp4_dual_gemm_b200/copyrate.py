@@ -10,9 +10,10 @@ one bulk global->shared copy, the cycles per copy until all bytes landed,
 and the bytes per cycle each SM received.  These are the two figures the
 kernels' producers are designed around: a thread issues its copies one at a
 time while different warps issue side by side, and the global->shared
-bandwidth an SM gets falls as more SMs copy at the same time.  A second table gives the distributed-shared-memory exchange rate of
-clusters of two CTAs sending 64 KiB to each other (bulk copies of several
-sizes, and 16-byte st.async stores), the cluster split-K epilogue's pattern.
+bandwidth an SM gets falls as more SMs copy at the same time.  A second
+table gives the distributed-shared-memory exchange rate of clusters of two
+CTAs sending 64 KiB to each other (bulk copies of several sizes, and
+16-byte st.async stores), the cluster split-K epilogue's pattern.
 """
 from __future__ import annotations
 
