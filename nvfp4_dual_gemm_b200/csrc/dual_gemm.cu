@@ -23,6 +23,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <type_traits>
 #include <vector>
 #include <mutex>
 #include <string>
@@ -255,6 +256,91 @@ __device__ __forceinline__ uint8_t quant_block16(const float* v, uint32_t& w0,
   return static_cast<uint8_t>(sb);
 }
 
+// The same block quantiser for 16-bit elements (fp16 or bf16), held as
+// eight packed pairs (element 2i in the low half of p[i]), two elements per
+// instruction.  Every midpoint product t * s (at most 7 significant bits,
+// between 2^-11 and 2240) is exact in fp16 and in bf16, and for a 16-bit v,
+// v >= T <=> v > the 16-bit value below T; so comparing 16-bit keys with
+// packed 2-wide compares gives exactly the codes of the fp32 form above.
+template <typename H2>
+struct Half2Ops;
+template <>
+struct Half2Ops<__half2> {
+  static __device__ __forceinline__ uint32_t bits(float x) {  // x exact
+    return __half_as_ushort(__float2half_rn(x));
+  }
+  static __device__ __forceinline__ float lo(uint32_t u) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(u)));
+  }
+  static __device__ __forceinline__ float hi(uint32_t u) { return lo(u >> 16); }
+};
+template <>
+struct Half2Ops<__nv_bfloat162> {
+  static __device__ __forceinline__ uint32_t bits(float x) {  // x exact
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+  static __device__ __forceinline__ float lo(uint32_t u) {
+    return __uint_as_float(u << 16);
+  }
+  static __device__ __forceinline__ float hi(uint32_t u) {
+    return __uint_as_float(u & 0xFFFF0000u);
+  }
+};
+
+template <typename H2>
+__device__ __forceinline__ H2 as_h2(uint32_t u) {
+  return *reinterpret_cast<const H2*>(&u);
+}
+
+template <typename H2>
+__device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
+                                                    uint32_t& w0,
+                                                    uint32_t& w1) {
+  using Ops = Half2Ops<H2>;
+  uint32_t a[8];  // |v| pairs: the keys
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a[i] = p[i] & 0x7FFF7FFFu;
+  H2 m2 = as_h2<H2>(a[0]);
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m2 = __hmax2(m2, as_h2<H2>(a[i]));
+  uint32_t mu;
+  *reinterpret_cast<H2*>(&mu) = m2;
+  const float amax = fmaxf(Ops::lo(mu), Ops::hi(mu));
+  const __nv_fp8_storage_t sb =
+      __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+  const float sd =
+      __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
+  w0 = 0;
+  w1 = 0;
+  if (sd > 0.f) {
+    auto rep2 = [](uint32_t b) { return b | (b << 16); };
+    const uint32_t t0 = rep2(Ops::bits(0.25f * sd)),
+                   t1 = rep2(Ops::bits(0.75f * sd) - 1u),
+                   t2 = rep2(Ops::bits(1.25f * sd)),
+                   t3 = rep2(Ops::bits(1.75f * sd) - 1u),
+                   t4 = rep2(Ops::bits(2.5f * sd)),
+                   t5 = rep2(Ops::bits(3.5f * sd) - 1u),
+                   t6 = rep2(Ops::bits(5.0f * sd));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const H2 k = as_h2<H2>(a[i]);
+      const uint32_t b2 = __hgt2_mask(k, as_h2<H2>(t3));
+      const uint32_t b1 = __hgt2_mask(k, as_h2<H2>((t5 & b2) | (t1 & ~b2)));
+      const uint32_t th = (t6 & b1) | (t4 & ~b1), tl = (t2 & b1) | (t0 & ~b1);
+      const uint32_t b0 = __hgt2_mask(k, as_h2<H2>((th & b2) | (tl & ~b2)));
+      const uint32_t code = (b2 & 0x00040004u) | (b1 & 0x00020002u) |
+                            (b0 & 0x00010001u) |
+                            ((p[i] >> 12) & 0x00080008u);  // the sign bits
+      const uint32_t byte = (code & 0xFu) | ((code >> 12) & 0xF0u);
+      if (i < 4)
+        w0 |= byte << (8 * i);
+      else
+        w1 |= byte << (8 * (i - 4));
+    }
+  }
+  return static_cast<uint8_t>(sb);
+}
+
 // Where the epilogue of one tile row writes its outputs: fp16 C, or NVFP4
 // codes and blocked scales (KParams::cq).  `col0` is the tile's first column.
 struct OutRow {
@@ -369,12 +455,13 @@ __device__ __forceinline__ OutRow out_row(const KParams& p, const TileLoc& t,
 __device__ __forceinline__ void quant_store16(const OutRow& o, int cc,
                                               const float* x,
                                               const float* y) {
-  float h[16];  // the values the fp16 output would hold
+  uint32_t h[8];  // the fp16 values the fp16 output would hold, in pairs
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    h[i] = __half2float(__float2half_rn(silu_mul(x[i], y[i])));
+  for (int i = 0; i < 8; ++i)
+    h[i] = pack_half2(silu_mul(x[2 * i], y[2 * i]),
+                      silu_mul(x[2 * i + 1], y[2 * i + 1]));
   uint32_t w0, w1;
-  const uint8_t sb = quant_block16(h, w0, w1);
+  const uint8_t sb = quant_block16_x2<__half2>(h, w0, w1);
   const int col = o.col0 + cc;
   if (o.row_ok) *reinterpret_cast<uint2*>(o.q + cc / 2) = make_uint2(w0, w1);
   if (o.sf_ok) o.sf[(col / 64) * kSfAtomBytes + (col / 16) % 4] = sb;
@@ -1735,38 +1822,30 @@ struct In16<float> {
     }
   }
 };
-template <>
-struct In16<__half> {
-  static __device__ __forceinline__ void load(const __half* p, float (&v)[16]) {
+// One 16-element block of a row: its raw loaded form and its encoder (fp32
+// values through quant_block16; fp16 / bf16 kept as packed pairs for
+// quant_block16_x2).
+template <typename T>
+struct Block16 {
+  uint32_t raw[8];
+  __device__ __forceinline__ void load(const T* p) {
     const uint4* s = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const uint4 t = __ldg(s + q);
-      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        v[8 * q + 2 * i] = f.x;
-        v[8 * q + 2 * i + 1] = f.y;
-      }
-    }
+    const uint4 a = __ldg(s), b = __ldg(s + 1);
+    raw[0] = a.x; raw[1] = a.y; raw[2] = a.z; raw[3] = a.w;
+    raw[4] = b.x; raw[5] = b.y; raw[6] = b.z; raw[7] = b.w;
+  }
+  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1) const {
+    using H2 = typename std::conditional<std::is_same<T, __half>::value,
+                                         __half2, __nv_bfloat162>::type;
+    return quant_block16_x2<H2>(raw, w0, w1);
   }
 };
 template <>
-struct In16<__nv_bfloat16> {
-  static __device__ __forceinline__ void load(const __nv_bfloat16* p,
-                                              float (&v)[16]) {
-    const uint4* s = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const uint4 t = __ldg(s + q);
-      const uint32_t w[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        v[8 * q + 2 * i] = __uint_as_float(w[i] << 16);
-        v[8 * q + 2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-      }
-    }
+struct Block16<float> {
+  float v[16];
+  __device__ __forceinline__ void load(const float* p) { In16<float>::load(p, v); }
+  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1) const {
+    return quant_block16(v, w0, w1);
   }
 };
 
@@ -1789,14 +1868,13 @@ __global__ void __launch_bounds__(256)
       uint8_t* dst = codes + (size_t)r * (K / 2) + (size_t)g * 32;
       // all four 16-element loads of the group before any arithmetic, so
       // that each lane keeps its whole 64-element run in flight
-      float vv[4][16];
+      Block16<T> blk[4];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) In16<T>::load(src + 16 * b, vv[b]);
+      for (int b = 0; b < 4; ++b) blk[b].load(src + 16 * b);
 #pragma unroll
       for (int b = 0; b < 4; ++b) {
-        const float* v = vv[b];
         uint32_t w0, w1;
-        const uint8_t sb = quant_block16(v, w0, w1);
+        const uint8_t sb = blk[b].encode(w0, w1);
         *reinterpret_cast<uint2*>(dst + 8 * b) = make_uint2(w0, w1);
         sfw |= static_cast<uint32_t>(sb) << (8 * b);
       }

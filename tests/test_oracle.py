@@ -201,3 +201,54 @@ def test_division_free_e2m1_encoding_equals_division():
         got = _threshold_codes(v, sd)
         bad = np.flatnonzero(got != want)
         assert bad.size == 0, (b, v[bad[:4]], got[bad[:4]], want[bad[:4]])
+
+
+def _bf16(x):
+    """float32 -> the bf16 values (round to nearest even) as float32."""
+    u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return (u.astype(np.uint32) << 16).view(np.float32)
+
+
+def test_packed_16bit_e2m1_encoding_equals_division():
+    # The CUDA quantiser's form for fp16 / bf16 data (quant_block16_x2):
+    # the midpoint products t * s rounded to the 16-bit type (exact: at most
+    # 7 significant bits, within range) and compared with |v| as 16-bit
+    # values, the >= midpoints as > the 16-bit value just below.  Every fp16
+    # value and a spread of bf16 values, for every positive e4m3 scale.
+    h16 = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16)
+    h16 = h16[~np.isnan(h16)]
+    rng = np.random.default_rng(2)
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    for b in range(1, 0x7F):
+        sd = O.e4m3_decode(np.uint8(b)).astype(np.float32)
+        for kind in ("f16", "bf16"):
+            if kind == "f16":
+                v = h16.astype(np.float32)
+                t = (mids * sd).astype(np.float16)
+                assert np.array_equal(t.astype(np.float32), mids * sd)
+                below = (t.view(np.uint16) - 1).view(np.float16).astype(
+                    np.float32)
+                t = t.astype(np.float32)
+            else:
+                v = _bf16(np.concatenate([
+                    rng.standard_normal(20000).astype(np.float32) * 3 * sd,
+                    mids * sd, [0.0, np.inf]]).astype(np.float32))
+                t = _bf16(mids * sd)
+                assert np.array_equal(t, mids * sd)
+                below = ((t.view(np.uint32) >> 16) - 1).astype(
+                    np.uint32) << 16
+                below = below.view(np.float32)
+            ts = [t[0], below[1], t[2], below[3], t[4], below[5], t[6]]
+            v = np.concatenate([v, -v]).astype(np.float32)
+            a = np.abs(v)
+            b2 = a > ts[3]
+            b1 = a > np.where(b2, ts[5], ts[1])
+            b0 = a > np.where(b2, np.where(b1, ts[6], ts[4]),
+                              np.where(b1, ts[2], ts[0]))
+            got = ((4 * b2 + 2 * b1 + b0) |
+                   np.where(np.signbit(v), 8, 0)).astype(np.uint8)
+            with np.errstate(over="ignore", invalid="ignore"):
+                want = O.e2m1_encode(v / sd)
+            bad = np.flatnonzero(got != want)
+            assert bad.size == 0, (b, kind, v[bad[:4]])
