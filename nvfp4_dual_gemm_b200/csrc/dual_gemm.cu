@@ -1896,6 +1896,9 @@ __global__ void __launch_bounds__(256)
 // contiguous), so both sides are coalesced.  Padding rows of the blocked
 // buffer are written as zero.
 constexpr int kCvtGroups = 32;
+// words each of the 256 threads moves: a fixed count, so that every load of a
+// thread is issued before the first one is used
+constexpr int kCvtIters = 128 * kCvtGroups / 256;
 
 __global__ void __launch_bounds__(256)
     scales_to_blocked_kernel(const uint8_t* __restrict__ plain, int rows,
@@ -1905,12 +1908,21 @@ __global__ void __launch_bounds__(256)
   const int rb = blockIdx.y;
   const int g0 = blockIdx.x * kCvtGroups;
   const int ng = min(kCvtGroups, groups - g0);
-  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+  uint32_t v[kCvtIters];
+#pragma unroll
+  for (int j = 0; j < kCvtIters; ++j) {
+    const int i = threadIdx.x + j * 256;
     const int r = i / ng, gg = i - r * ng;
     const int row = rb * 128 + r;
-    tile[r][gg] = row < rows ? *reinterpret_cast<const uint32_t*>(
-                                   plain + (size_t)row * ld + 4 * (g0 + gg))
-                             : 0u;
+    v[j] = (i < 128 * ng && row < rows)
+               ? __ldg(reinterpret_cast<const uint32_t*>(
+                     plain + (size_t)row * ld + 4 * (g0 + gg)))
+               : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kCvtIters; ++j) {
+    const int i = threadIdx.x + j * 256;
+    if (i < 128 * ng) tile[i / ng][i % ng] = v[j];
   }
   __syncthreads();
   uint32_t* out = reinterpret_cast<uint32_t*>(blocked) +
@@ -1931,9 +1943,17 @@ __global__ void __launch_bounds__(256)
   const int ng = min(kCvtGroups, groups - g0);
   const uint32_t* in = reinterpret_cast<const uint32_t*>(blocked) +
                        ((size_t)rb * groups + g0) * (kSfAtomBytes / 4);
-  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
+  uint32_t v[kCvtIters];
+#pragma unroll
+  for (int j = 0; j < kCvtIters; ++j) {
+    const int i = threadIdx.x + j * 256;
+    v[j] = i < 128 * ng ? __ldg(in + i) : 0u;
+  }
+#pragma unroll
+  for (int j = 0; j < kCvtIters; ++j) {
+    const int i = threadIdx.x + j * 256;
     const int gg = i >> 7, w = i & 127;
-    tile[(w >> 2) + 32 * (w & 3)][gg] = in[i];
+    if (i < 128 * ng) tile[(w >> 2) + 32 * (w & 3)][gg] = v[j];
   }
   __syncthreads();
   for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
