@@ -98,11 +98,6 @@ NVFP4DG_HD void tile_lmn(const Plan& p, int tile, int& l, int& m_tile,
   }
 }
 
-// (m_tile, n_tile) of linear tile index `tile` of an unbatched plan.
-NVFP4DG_HD void tile_mn(const Plan& p, int tile, int& m_tile, int& n_tile) {
-  int l;
-  tile_lmn(p, tile, l, m_tile, n_tile);
-}
 
 struct Work {
   int tile;  // linear tile index; m fastest: m = tile % m_tiles

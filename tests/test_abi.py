@@ -373,8 +373,9 @@ def test_stream_k_small_grid_search():
 
 
 def test_tile_division_by_multiply_high():
-    # Restatement of set_tile_div / tile_mn (schedule.h): the quotient of
-    # every tile index by every row-tile count the planner can produce.
+    # Restatement of set_div / div_by (schedule.h, used by tile_lmn for the
+    # row-tile and the column-tile counts): the quotient of every tile index
+    # by every divisor the planner can produce.
     import numpy as np
     n = np.arange(1 << 17, dtype=np.uint64)
     for d in list(range(1, 1025)) + [4095, 4096, 8191, 16384]:
