@@ -415,3 +415,32 @@ def test_scale_converter_rejects_bad_arguments_without_gpu():
     assert back(ctypes.c_void_p(260), 4, 128, p, 8, None) == _lib.ERR_ALIGN
     assert to(None, 4, 128, 8, p, None) == _lib.ERR_INVALID
     assert to(None, 0, 128, 8, None, None) == _lib.OK
+
+
+def test_grouped_arguments_rejected_without_gpu():
+    # nvfp4_dual_gemm_run_grouped validates its group table before any CUDA
+    # call: group count, row offsets on 128-row boundaries, no overlap once
+    # each group is rounded up to 128 rows, no cluster split-K.
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    run = lib.nvfp4_dual_gemm_run_grouped
+
+    def call(rows, row0, flags=0, n=128, k=256, groups=None):
+        g = len(rows) if groups is None else groups
+        r = (ctypes.c_int * max(1, len(rows)))(*rows)
+        o = (ctypes.c_int * max(1, len(row0)))(*row0)
+        return run(p, p, p, p, p, p, p, r, o, g, n, k, flags, None, 0, None)
+
+    assert call([128], [0], groups=0) == _lib.ERR_INVALID
+    assert call([1] * 65, [128 * i for i in range(65)]) == _lib.ERR_INVALID
+    assert call([128, 64], [0, 100]) == _lib.ERR_INVALID
+    assert "multiple of 128" in _lib.last_error()
+    assert call([130, 64], [0, 128]) == _lib.ERR_INVALID
+    assert "overlaps" in _lib.last_error()
+    assert call([-1], [0]) == _lib.ERR_INVALID
+    assert call([128], [0], flags=_lib.FLAG_SPLITK) == _lib.ERR_INVALID
+    assert "split-K" in _lib.last_error()
+    assert call([128], [0], n=100) == _lib.ERR_INVALID
+    assert run(p, p, p, p, p, p, p, None, None, 1, 128, 256, 0, None, 0,
+               None) == _lib.ERR_INVALID
+
