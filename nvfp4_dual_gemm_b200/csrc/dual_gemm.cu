@@ -1793,16 +1793,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ===========================================================================
 // Activation quantiser: rows of fp32 / fp16 / bf16 -> e2m1 codes and e4m3
 // block scales, written straight into the blocked layout the dual GEMM
-// reads.  One lane per (row, 64-element group): it reads 64 contiguous
-// elements (16-byte loads), writes 32 bytes of codes and the group's four
-// scales as one 32-bit word, so a warp (32 consecutive rows, one group)
-// writes 32 words of one blocked atom (row r's 16-byte atom row at
-// (r % 32) * 16, quarter (r % 128) / 32 at +4 within it).  Lanes of the
-// padding rows up to a multiple of 128 write zero scales, so no memset of
-// the blocked buffer is needed.  Arithmetic as the oracle's quantiser:
-// scale = e4m3(amax / 6) RN saturating, codes = e2m1(x / scale) RN
-// saturating (an IEEE division, as the oracle's), zero codes for a zero
-// scale.
+// reads.  One warp per 1024 consecutive elements of a row: lane i
+// quantises the 16-element blocks at 16 i and 512 + 16 i, loading both
+// (16-byte loads) before encoding either, so each warp load instruction
+// covers one contiguous run of the row and its code stores 256 contiguous
+// bytes; the four lanes of a 64-element group gather their scales into one
+// 32-bit word for the plain layout and for the blocked one (row r's 16-byte
+// atom row at (r % 32) * 16, quarter (r % 128) / 32 at +4 within it).  Warps
+// of the padding rows up to a multiple of 128 write zero scales, so no
+// memset of the blocked buffer is needed.  (One lane per row, each reading
+// its own row, made every load instruction touch 32 cache lines: 54.4
+// instead of 43.2 us on 8192 x 7168 bf16.)
 template <typename T>
 struct In16 {
   // 16 consecutive elements at p (16-byte aligned) as fp32
@@ -1856,35 +1857,44 @@ __global__ void __launch_bounds__(256)
                          uint8_t* __restrict__ sf_plain,
                          uint8_t* __restrict__ sf_blocked) {
   const int groups = K / 64;
-  const long long units = (long long)((rows + 127) / 128) * 4 * groups;
+  const int chunks = (K + 1023) / 1024;  // 1024-element runs per row
+  const long long units = (long long)((rows + 127) / 128) * 128 * chunks;
   const int lane = threadIdx.x & 31;
   for (long long u = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
        u < units; u += (long long)gridDim.x * (blockDim.x / 32)) {
-    const int g = static_cast<int>(u % groups);  // consecutive warps: along K
-    const int r = static_cast<int>(u / groups) * 32 + lane;
-    uint32_t sfw = 0;
-    if (r < rows) {
-      const T* src = X + (size_t)r * ldx + (size_t)g * 64;
-      uint8_t* dst = codes + (size_t)r * (K / 2) + (size_t)g * 32;
-      // all four 16-element loads of the group before any arithmetic, so
-      // that each lane keeps its whole 64-element run in flight
-      Block16<T> blk[4];
+    const int r = static_cast<int>(u / chunks);
+    const int c0 = static_cast<int>(u - (long long)r * chunks) * 1024 + 16 * lane;
+    Block16<T> blk[2];
+    bool act[2];
 #pragma unroll
-      for (int b = 0; b < 4; ++b) blk[b].load(src + 16 * b);
-#pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        uint32_t w0, w1;
-        const uint8_t sb = blk[b].encode(w0, w1);
-        *reinterpret_cast<uint2*>(dst + 8 * b) = make_uint2(w0, w1);
-        sfw |= static_cast<uint32_t>(sb) << (8 * b);
-      }
-      if (sf_plain)
-        *reinterpret_cast<uint32_t*>(sf_plain + (size_t)r * (K / 16) +
-                                     (size_t)g * 4) = sfw;
+    for (int h = 0; h < 2; ++h) {
+      act[h] = c0 + 512 * h < K;
+      if (act[h] && r < rows) blk[h].load(X + (size_t)r * ldx + c0 + 512 * h);
     }
-    *reinterpret_cast<uint32_t*>(
-        sf_blocked + ((size_t)(r / 128) * groups + g) * kSfAtomBytes +
-        (r % 32) * 16 + ((r % 128) / 32) * 4) = sfw;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = c0 + 512 * h;
+      uint32_t sb = 0;
+      if (act[h] && r < rows) {
+        uint32_t w0, w1;
+        sb = blk[h].encode(w0, w1);
+        *reinterpret_cast<uint2*>(codes + (size_t)r * (K / 2) + c / 2) =
+            make_uint2(w0, w1);
+      }
+      const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 1);
+      const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 2);
+      const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 3);
+      if ((lane & 3) == 0 && act[h]) {
+        const uint32_t word = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+        const int g = c / 64;
+        if (sf_plain != nullptr && r < rows)
+          *reinterpret_cast<uint32_t*>(sf_plain + (size_t)r * (K / 16) +
+                                       (size_t)g * 4) = word;
+        *reinterpret_cast<uint32_t*>(
+            sf_blocked + ((size_t)(r / 128) * groups + g) * kSfAtomBytes +
+            (r % 32) * 16 + ((r % 128) / 32) * 4) = word;
+      }
+    }
   }
 }
 
@@ -3252,7 +3262,8 @@ int nvfp4_quantize_rows(const void* X, int dtype, int rows, int K,
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const long long units = (long long)((rows + 127) / 128) * 4 * (K / 64);
+  const long long units =
+      (long long)((rows + 127) / 128) * 128 * ((K + 1023) / 1024);
   const int threads = 256;
   const long long want = (units + threads / 32 - 1) / (threads / 32);
   const int blocks = (int)std::min<long long>(want, (long long)sms * 8);
