@@ -1,25 +1,41 @@
 #!/usr/bin/env python
 """Benchmark of the NVFP4 dual GEMM  C = silu(A B1^T) * (A B2^T).
 
-One step = one dual-GEMM call on one batch of seeded synthetic NVFP4 input
-(randn -> e2m1 codes + e4m3 per-16 scales).  Default workload: BASELINE
-config 2, the decode shape M=256, N=4096, K=7168.  Prints ONE JSON line on
-rank 0.
+The metric is BASELINE's: dual-GEMM us per call and effective TFLOP/s (as a
+fraction of the FP4-tensor / HBM roofline), geomean over shapes.  The
+default workload is every benchmark shape in one run:
 
-Timed region: the K steps are captured once in a CUDA graph and replayed
-between two CUDA events (barrier + synchronize on both sides); inputs rotate
-over enough independent sets that the data touched between two uses of a set
-exceeds the 126 MB L2, so every call streams its operands from HBM.
+  C2 decode   256 x  4096 x 7168   (HBM-bound)
+  C3 mid      512 x  3072 x 7168
+  C4 prefill 4096 x 14336 x 4096   (tensor-bound)
+  C5 N-sharded FFN 8192 x 28672 x 8192, N split over the ranks
 
-Multi-GPU (torchrun, one process per GPU): for the c2/c3/c4 workloads every
-rank owns its own N-slice of a wider problem of the same per-rank shape (A
-replicated, no collective: weak scaling); for c5 the fixed N = 28672 is split
-over the ranks (strong scaling).  Time = max over ranks.
+One step = one call of each shape (through the reference-compatible entry
+point ``custom_kernel(data)``, one call at a time, as the reference's harness
+calls it); ``value`` is the geomean over the shapes of the whole job's
+TFLOP/s.  Inputs: seeded randn fp32 quantised to NVFP4 (e2m1 codes, e4m3
+per-16 scale = amax / 6, blocked scale layout) by plain torch operations on
+the GPU (``make_data``), the same bytes for both arms.
 
-  --impl reference  times the reference's own implementation on the same
-                    workload: its kernel compiled from its sources
-                    (oracle/_ref, shapes of its dispatch table), else the CPU
-                    port of its algorithm in oracle/.
+Timing: per shape, W untimed calls, then `repeats` timed regions of exactly
+K back-to-back calls, each between two CUDA events on the launching stream
+with a barrier and a synchronize on both sides; the region's median is the
+shape's time (max over ranks).  Inputs rotate over enough independent sets
+that more than 2 x the 126 MB L2 is touched between two uses of a set.
+Beside it, per shape: the same calls captured in a CUDA graph, and end to
+end through the host-buffer API (pinned host inputs and output).
+
+Multi-GPU (torchrun, one process per GPU): C2/C3/C4 run the full shape on
+every rank (weak scaling); C5's N = 28672 is split over the ranks (strong
+scaling: rank r owns B1/B2 rows [r N/w, (r+1) N/w) and their scale bytes,
+A is replicated).  No collective on the timed path.
+
+  --impl reference  the reference's own implementation of the path on the
+                    same inputs: its kernel, compiled from its sources
+                    (oracle/_ref; its dispatch entry for C2/C3, its launcher
+                    template instantiated for C4/C5), called eagerly the way
+                    its custom_kernel calls it.  Under torchrun rank 0 alone
+                    runs it, on one rank's shapes (n_gpus 1).
 """
 from __future__ import annotations
 
@@ -49,9 +65,15 @@ WORKLOADS = {
     "c5": dict(M=8192, N=28672, K=8192, a=0.5, w=0.02, strong=True,
                name="C5 N-sharded 8192x28672x8192 (BASELINE configs[4])"),
 }
+ALL = ["c2", "c3", "c4", "c5"]
 METRIC = ("dual-GEMM µs & effective TFLOPS (% of FP4/HBM roofline), "
           "geomean over shapes")
 L2_BYTES = 126 * 2 ** 20
+EAGER_TIMED = ("per shape: `repeats` regions of exactly `steps` back-to-back "
+               "eager calls, CUDA events on the launching stream, barrier + "
+               "synchronize around each region; median region")
+GRAPH_TIMED = ("`repeats` replays of one CUDA graph of `steps` calls, CUDA "
+               "events around each replay; median replay")
 
 
 def algo_bytes(m, n, k):
@@ -63,6 +85,13 @@ def algo_flops(m, n, k):
     return 4.0 * m * n * k
 
 
+def geomean(vals):
+    vals = [v for v in vals if v is not None and v > 0]
+    if not vals:
+        return None
+    return math.exp(sum(map(math.log, vals)) / len(vals))
+
+
 def load_peaks():
     path = os.path.join(REPO, "MEASURED_PEAKS.json")
     try:
@@ -70,9 +99,12 @@ def load_peaks():
             pk = json.load(f)
         return {"hbm_gbs": float(pk["hbm_gbs"]),
                 "bf16_tflops": float(pk["bf16_tflops"]),
+                "bf16_tflops_sustained": float(
+                    pk.get("bf16_tflops_sustained", pk["bf16_tflops"])),
                 "source": "measured"}
     except Exception:
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0,
+                "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 def load_traffic(workload):
@@ -86,8 +118,42 @@ def load_traffic(workload):
         return None
 
 
+def roofline(m, n, k, us, peaks, workload):
+    """Roofline object of one call of m x n x k taking `us`: the slower of
+    the FP4-tensor bound (4 x the measured bf16 rate, NVIDIA's dense FP4:bf16
+    ratio; the burst figure for short calls, the sustained one for calls of
+    a millisecond or more) and the HBM bound (measured copy bandwidth)."""
+    byts = algo_bytes(m, n, k)
+    flops = algo_flops(m, n, k)
+    bf16 = peaks["bf16_tflops"] if us < 1000 else peaks["bf16_tflops_sustained"]
+    fp4 = 4.0 * bf16
+    t_hbm = byts / (peaks["hbm_gbs"] * 1e9)
+    t_tc = flops / (fp4 * 1e12)
+    if t_hbm >= t_tc:
+        ach = byts / (us * 1e-6) / 1e9
+        r = {"bound": "hbm", "achieved": round(ach, 1),
+             "peak": peaks["hbm_gbs"], "unit": "GB/s",
+             "frac": round(ach / peaks["hbm_gbs"], 4)}
+    else:
+        ach = flops / (us * 1e-6) / 1e12
+        r = {"bound": "tensor", "achieved": round(ach, 1), "peak": fp4,
+             "unit": "TFLOP/s", "frac": round(ach / fp4, 4)}
+    r["traffic"] = load_traffic(workload)
+    r["traffic_source"] = ("dram__bytes_read.sum + dram__bytes_write.sum per "
+                           "launch from an earlier ncu capture of this "
+                           "workload (profiles/dram_traffic.json), not "
+                           "measured in this run")
+    r["algorithmic_bytes"] = byts
+    r["algorithmic_flops"] = flops
+    r["peak_source"] = (
+        f"{peaks['source']} HBM copy GB/s; FP4 dense = 4 x {peaks['source']} "
+        f"bf16 cuBLAS TF/s ({'burst' if us < 1000 else 'sustained'})")
+    return r
+
+
 class ClockSampler:
-    """Polls NVML (SM clock, throttle reasons) from a thread while running."""
+    """Polls NVML (SM clock, throttle reasons) from a thread while running;
+    samples accumulate over every timed region it brackets."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting",
@@ -100,9 +166,10 @@ class ClockSampler:
         self.samples = []
         self.reasons = 0
         self.max_mhz = None
-        self._stop = threading.Event()
         self._period = period_s
         self._h = None
+        self._stop = None
+        self._t = None
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -112,7 +179,6 @@ class ClockSampler:
                 self._h, pynvml.NVML_CLOCK_SM)
         except Exception:
             self._h = None
-        self._t = threading.Thread(target=self._run, daemon=True)
 
     def _sample(self):
         nv = self._nv
@@ -129,12 +195,14 @@ class ClockSampler:
 
     def __enter__(self):
         if self._h is not None:
+            self._stop = threading.Event()
+            self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
         if self._h is not None:
+            self._stop.set()
             self._t.join()
             try:
                 self._sample()
@@ -175,37 +243,174 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(x, world):
+def gather_ranks(x, world):
+    """Every rank's value of x (a float), in rank order."""
     if world == 1:
-        return x
-    from nvfp4_dual_gemm_b200.shard import max_over_ranks as _max
-    return _max(x, device="cuda")
+        return [x]
+    import torch.distributed as dist
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    out = [torch.zeros_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
 
 
 # --------------------------------------------------------------------------
-# inputs
+# inputs: NVFP4 quantisation in plain torch (no library code), the same
+# recipe as the oracle's quantiser (oracle/nvfp4_oracle.py: quantize,
+# to_blocked); tests/test_bench_inputs.py checks the bytes against it.
 # --------------------------------------------------------------------------
-def rank_problem(wl, world, rank):
-    m, n, k = wl["M"], wl["N"], wl["K"]
-    if wl.get("strong"):
-        if n % (64 * world):
-            raise SystemExit(f"N={n} does not split into {world} x 64")
-        n = n // world
-    return m, n, k
+_E2M1_CUTS = (0.25, float(np.nextafter(np.float32(0.75), np.float32(0))), 1.25,
+              float(np.nextafter(np.float32(1.75), np.float32(0))), 2.5,
+              float(np.nextafter(np.float32(3.5), np.float32(0))), 5.0)
 
 
-def make_sets(dg, m, n, k, wl, rank, min_sets=2):
-    per = algo_bytes(m, n, k)
-    nsets = max(min_sets, math.ceil(2 * L2_BYTES / per))
-    sets = [dg.generate_input(m, n, k, seed=1000 * rank + s, a_scale=wl["a"],
-                              w_scale=wl["w"]) for s in range(nsets)]
+def nvfp4_quantize_torch(x):
+    """[rows, K] float32 -> (codes [rows, K/2] uint8, element 2i in the low
+    nibble; scales [rows, K/16] uint8 e4m3).  Scale = e4m3(amax / 6) (round
+    to nearest even, saturating at 448); code = e2m1(x / scale) rounded to
+    nearest with ties to the even code, saturating at 6, sign kept; a block
+    whose scale is 0 gets zero codes."""
+    rows, k = x.shape
+    blk = x.reshape(rows, k // 16, 16)
+    amax = blk.abs().amax(dim=2)
+    sf = (amax / 6.0).clamp(max=448.0).to(torch.float8_e4m3fn)
+    sd = sf.to(torch.float32).unsqueeze(-1)
+    q = torch.where(sd > 0, blk / sd, torch.zeros_like(blk))
+    cuts = torch.tensor(_E2M1_CUTS, dtype=torch.float32, device=x.device)
+    mag = torch.bucketize(q.abs(), cuts, right=False).to(torch.uint8)
+    codes = (mag | (torch.signbit(q).to(torch.uint8) << 3)).reshape(rows, k)
+    packed = codes[:, 0::2] | (codes[:, 1::2] << 4)
+    return packed.contiguous(), sf.view(torch.uint8)
+
+
+def blocked_torch(sf):
+    """Plain scales [rows, K/16] uint8 -> the blocked layout (512-byte atoms
+    of 128 rows x 4 scales, atom = rowblock * (K/64) + k64, byte
+    (r % 32) * 16 + ((r % 128) // 32) * 4 + c % 4), padding rows zero."""
+    rows, kb = sf.shape
+    rb = (rows + 127) // 128
+    pad = torch.zeros((rb * 128, kb), dtype=torch.uint8, device=sf.device)
+    pad[:rows] = sf
+    return (pad.view(rb, 4, 32, kb // 4, 4).permute(0, 3, 2, 1, 4)
+            .contiguous().view(-1))
+
+
+def make_data(m, n, k, seed, a_scale, w_scale, device, chunk=4096):
+    """The reference's ``data`` 10-tuple (a, b1, b2, sfa, sfb1, sfb2,
+    sfa_blocked, sfb1_blocked, sfb2_blocked, c) for one seeded problem:
+    operands float4_e2m1fn_x2 [rows, K/2, 1], plain scales float8_e4m3fn
+    [rows, K/16, 1], blocked scales float8_e4m3fn (flat), c float16
+    [m, n, 1]."""
+    gen = torch.Generator(device=device)
+    out, plain, blocked = [], [], []
+    for idx, (rows, scale) in enumerate(((m, a_scale), (n, w_scale),
+                                         (n, w_scale))):
+        gen.manual_seed(seed * 1000003 + idx)
+        codes = torch.empty((rows, k // 2), dtype=torch.uint8, device=device)
+        sf = torch.empty((rows, k // 16), dtype=torch.uint8, device=device)
+        for r0 in range(0, rows, chunk):
+            r1 = min(rows, r0 + chunk)
+            x = torch.randn((r1 - r0, k), generator=gen, device=device,
+                            dtype=torch.float32)
+            if scale != 1.0:
+                x.mul_(scale)
+            codes[r0:r1], sf[r0:r1] = nvfp4_quantize_torch(x)
+            del x
+        out.append(codes.view(torch.float4_e2m1fn_x2).unsqueeze(-1))
+        plain.append(sf.view(torch.float8_e4m3fn).unsqueeze(-1))
+        blocked.append(blocked_torch(sf).view(torch.float8_e4m3fn))
+    c = torch.empty((m, n, 1), dtype=torch.float16, device=device)
+    return (out[0], out[1], out[2], plain[0], plain[1], plain[2],
+            blocked[0], blocked[1], blocked[2], c)
+
+
+def shard_data(d, n, k, world, rank):
+    """Rank `rank`'s slice of a full problem for N-sharding: B1/B2 rows
+    [r N/w, (r+1) N/w) and the matching bytes of their blocked scales (one
+    contiguous range when N/w is a multiple of 128; views, no copies), A and
+    SFA replicated, a local C [m, N/w, 1]."""
+    if world == 1:
+        return d
+    rows = n // world
+    if rows % 128:
+        raise SystemExit(f"N / world = {rows} is not a multiple of 128")
+    n0 = rank * rows
+    per_rb = (k // 64) * 512
+    s0, s1 = (n0 // 128) * per_rb, ((n0 + rows) // 128) * per_rb
+    c = torch.empty((d[9].size(0), rows, 1), dtype=torch.float16,
+                    device=d[9].device)
+    return (d[0], d[1][n0:n0 + rows], d[2][n0:n0 + rows], d[3],
+            d[4][n0:n0 + rows], d[5][n0:n0 + rows], d[6], d[7][s0:s1],
+            d[8][s0:s1], c)
+
+
+def rank_shape(key, world):
+    wl = WORKLOADS[key]
+    n = wl["N"] // world if wl.get("strong") else wl["N"]
+    return wl["M"], n, wl["K"]
+
+
+def make_sets(key, world, rank, device, seed0=0):
+    """Rotating input sets for one workload on this rank: enough that more
+    than 2 x L2 is touched between two uses of a set.  For the strong
+    (N-sharded) workload each set is generated in full and sliced."""
+    wl = WORKLOADS[key]
+    m, n, k = rank_shape(key, world)
+    nsets = max(2, math.ceil(2 * L2_BYTES / algo_bytes(m, n, k)))
+    sets = []
+    for s in range(nsets):
+        seed = seed0 + 100 * s + (0 if wl.get("strong") else rank)
+        if wl.get("strong"):
+            full = make_data(wl["M"], wl["N"], wl["K"], seed, wl["a"],
+                             wl["w"], device)
+            sets.append(shard_data(full, wl["N"], wl["K"], world, rank))
+        else:
+            sets.append(make_data(m, n, k, seed, wl["a"], wl["w"], device))
     torch.cuda.synchronize()
-    return sets, nsets
+    return sets
 
 
-def time_graph(step_fn, steps, warmup, world):
-    """Warm up eagerly, capture `steps` calls in one CUDA graph, replay it in
-    the timed region.  Returns (ms, clock summary)."""
+# --------------------------------------------------------------------------
+# timing
+# --------------------------------------------------------------------------
+def _region(fn, world, clk=None):
+    """One timed region: barrier + synchronize, events around fn(),
+    synchronize + barrier; returns ms."""
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record()
+    fn()
+    end.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    return start.elapsed_time(end)
+
+
+def time_eager(step_fn, steps, warmup, world, repeats):
+    """W untimed calls, then `repeats` regions of exactly `steps`
+    back-to-back calls; returns (median ms per region, every region's ms,
+    clock summary)."""
+    for i in range(warmup):
+        step_fn(i)
+    torch.cuda.synchronize()
+
+    def region():
+        for i in range(steps):
+            step_fn(i)
+
+    times = []
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for _ in range(repeats):
+            times.append(_region(region, world))
+    return statistics.median(times), times, clk.summary()
+
+
+def time_graph(step_fn, steps, warmup, world, repeats=1):
+    """Warm up eagerly, capture `steps` calls in one CUDA graph, replay it
+    `repeats` times, each replay a timed region; returns (median ms per
+    replay, clock summary)."""
     for i in range(warmup):
         step_fn(i)
     torch.cuda.synchronize()
@@ -219,307 +424,366 @@ def time_graph(step_fn, steps, warmup, world):
     torch.cuda.current_stream().wait_stream(s)
     g.replay()  # one untimed replay: first-replay setup is not part of a step
     torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    dev = torch.cuda.current_device()
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(dev) as clk:
-        start.record()
-        g.replay()
-        end.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    ms = start.elapsed_time(end)
-    del g
-    return ms, clk.summary()
-
-
-def time_eager(step_fn, steps, warmup, world):
-    """Warm up, then time `steps` back-to-back eager calls between two events
-    on the current (default) stream.  Used for implementations whose launches
-    cannot be captured in a CUDA graph."""
-    for i in range(warmup):
-        step_fn(i)
-    torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
+    times = []
     with ClockSampler(torch.cuda.current_device()) as clk:
-        start.record()
-        for i in range(steps):
-            step_fn(i)
-        end.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    return start.elapsed_time(end), clk.summary()
+        for _ in range(repeats):
+            times.append(_region(g.replay, world))
+    del g
+    return statistics.median(times), clk.summary()
 
 
-def copy_call_copy(call, host_inputs, dev_inputs, c_dev, c_host):
-    """One end-to-end step through a device-buffer API: pinned H2D of the
-    inputs, the call, D2H of C, one after another on the current stream."""
-    def one():
-        for h, d in zip(host_inputs, dev_inputs):
-            d.copy_(h, non_blocking=True)
-        call()
-        c_host.copy_(c_dev, non_blocking=True)
-    return one
-
-
-def time_e2e(one, host_inputs, c_host, steps, world):
+def time_e2e(one, h2d, d2h, steps, world):
     """Events around `steps` end-to-end steps (each uploads its inputs from
-    pinned host memory and downloads C); returns (ms, H2D and D2H bytes per
-    step)."""
-    stream = torch.cuda.current_stream()
-    h2d = sum(t.numel() * t.element_size() for t in host_inputs)
-    d2h = c_host.numel() * c_host.element_size()
+    pinned host memory and downloads C); returns ms."""
     one()
     torch.cuda.synchronize()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    start.record(stream)
-    for _ in range(steps):
-        one()
-    end.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    return start.elapsed_time(end), h2d, d2h
+
+    def region():
+        for _ in range(steps):
+            one()
+
+    return _region(region, world)
 
 
-def cpu_baseline(host_a, host_sfa, host_b1, host_sfb1, host_b2, host_sfb2,
-                 m, n, k, budget_s=20.0):
-    """The oracle (CPU restatement of the path) on a bounded row sample,
-    with all host threads for the matmuls."""
+def merge_clocks(parts):
+    samples = sum(p.get("samples", 0) for p in parts)
+    mhz = [p["sm_mhz"] for p in parts if p.get("sm_mhz") is not None]
+    reasons = sorted({r for p in parts for r in p.get("reasons", [])})
+    return {"sm_mhz": statistics.median(mhz) if mhz else None,
+            "sm_max_mhz": next((p["sm_max_mhz"] for p in parts
+                                if p.get("sm_max_mhz")), None),
+            "reasons": reasons, "samples": samples,
+            "per_workload_sm_mhz": [p.get("sm_mhz") for p in parts]}
+
+
+# --------------------------------------------------------------------------
+# CPU baseline: the oracle (CPU restatement of the path) on a bounded sample
+# --------------------------------------------------------------------------
+def cpu_baseline(d, key, budget_s=6.0):
+    """Dequantise-to-fp32 + fp32 BLAS matmuls + SiLU (oracle/) on a row
+    sample of one workload, all host threads; dequantisation and matmuls
+    timed separately (median of up to 5 repetitions)."""
     from threadpoolctl import threadpool_info, threadpool_limits
 
     from oracle import nvfp4_oracle as O
 
+    m, n, k = d[0].size(0), d[1].size(0), 2 * d[0].size(1)
+    rows = min(m, 32 if n <= 4096 else 16)
+    cols = min(n, 4096 if n <= 4096 else 2048)
+    host = [t.view(torch.uint8).squeeze(-1)[:r].cpu().numpy()
+            for t, r in ((d[0], rows), (d[3], rows), (d[1], cols),
+                         (d[4], cols), (d[2], cols), (d[5], cols))]
     cores = os.cpu_count() or 1
+    t_dq, t_mm = [], []
     with threadpool_limits(limits=cores):
-        threads = max([d.get("num_threads", 1) for d in threadpool_info()] or [1])
-        rows = min(m, 32)
-        t0 = time.perf_counter()
-        O.dual_gemm(host_a[:rows], host_sfa[:rows], host_b1, host_sfb1,
-                    host_b2, host_sfb2)
-        dt = time.perf_counter() - t0
-        reps = 1
-        while time.perf_counter() - t0 + dt < min(budget_s, 10 * dt) and reps < 5:
-            O.dual_gemm(host_a[:rows], host_sfa[:rows], host_b1, host_sfb1,
-                        host_b2, host_sfb2)
-            reps += 1
-        total = time.perf_counter() - t0
-    per_call = total / reps
-    flops = algo_flops(rows, n, k)
-    return {"value": flops / per_call / 1e12, "unit": "TFLOP/s",
-            "cores": threads, "kind": "port",
-            "sample": f"{rows} of {m} rows of A against all {n} rows of "
-                      f"B1/B2 (dequantise + fp32 matmul + SiLU), {reps} reps",
-            "us_per_call_full_shape_est": per_call * (m / rows) * 1e6}
+        threads = max([i.get("num_threads", 1) for i in threadpool_info()]
+                      or [1])
+        t_start = time.perf_counter()
+        while len(t_dq) < 5 and (len(t_dq) < 1 or
+                                 time.perf_counter() - t_start < budget_s):
+            t0 = time.perf_counter()
+            a = O.dequantize(host[0], host[1])
+            b1 = O.dequantize(host[2], host[3])
+            b2 = O.dequantize(host[4], host[5])
+            t1 = time.perf_counter()
+            with np.errstate(over="ignore"):
+                O.silu_mul(a @ b1.T, a @ b2.T).astype(np.float16)
+            t2 = time.perf_counter()
+            t_dq.append(t1 - t0)
+            t_mm.append(t2 - t1)
+    dq, mm = statistics.median(t_dq), statistics.median(t_mm)
+    flops = algo_flops(rows, cols, k)
+    return {"workload": key, "value": flops / (dq + mm) / 1e12,
+            "unit": "TFLOP/s", "cores": threads,
+            "sample": f"{rows} rows of A x {cols} rows of B1/B2, K = {k}",
+            "dequantise_s": dq, "matmul_silu_s": mm, "reps": len(t_dq)}
+
+
+def cpu_baseline_all(data_by_key):
+    per = [cpu_baseline(d, key) for key, d in data_by_key.items()]
+    return {"value": geomean([p["value"] for p in per]), "unit": "TFLOP/s",
+            "cores": max(p["cores"] for p in per), "kind": "port",
+            "sample": "geomean over the shapes of the oracle (dequantise + "
+                      "fp32 matmul + SiLU) on a row sample of each: " +
+                      "; ".join(f"{p['workload']}: {p['sample']}" for p in per),
+            "shapes": per}
 
 
 # --------------------------------------------------------------------------
 # arms
 # --------------------------------------------------------------------------
+def _host_copies(d):
+    """Pinned host copies of one set's six inputs (uint8) and of C."""
+    dev_in = [d[0], d[1], d[2], d[6], d[7], d[8]]
+    host_in = [t.view(torch.uint8).cpu().pin_memory() for t in dev_in]
+    c_host = torch.empty(d[9].shape, dtype=torch.float16).pin_memory()
+    return dev_in, host_in, c_host
+
+
+def _nbytes(ts):
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
 def run_ours(args, world, rank):
     import nvfp4_dual_gemm_b200 as dg
 
-    wl = WORKLOADS[args.workload]
-    m, n, k = rank_problem(wl, world, rank)
-    sets, nsets = make_sets(dg, m, n, k, wl, rank)
-    # The timed calls never write the weights (inputs rotate over sets made
-    # before timing), so they may be read before the dependency wait.
-    from nvfp4_dual_gemm_b200 import _lib
-    flags = args.flags | (0 if args.no_static_weights
-                          else _lib.FLAG_STATIC_WEIGHTS)
-    ws_bytes = dg.workspace_size(m, n, k, flags)
-    ws = torch.zeros(max(ws_bytes, 256), dtype=torch.uint8, device="cuda")
-
-    def step(i):
-        d = sets[i % nsets]
-        dg.dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9], flags=flags,
-                     workspace=ws)
-
-    ms, clocks = time_graph(step, args.steps, args.warmup, world)
-    ms = max_over_ranks(ms, world)
-    ranks_flops = algo_flops(m, n, k) * world
-    us_call = ms * 1e3 / args.steps
-    tflops = ranks_flops * args.steps / (ms * 1e-3) / 1e12
+    keys = ALL if args.workload == "all" else [args.workload]
     peaks = load_peaks()
-    byts = algo_bytes(m, n, k)
-    fp4_peak = 4.0 * peaks["bf16_tflops"]
-    t_hbm = byts / (peaks["hbm_gbs"] * 1e9)
-    t_tc = algo_flops(m, n, k) / (fp4_peak * 1e12)
-    if t_hbm >= t_tc:
-        ach = byts / (us_call * 1e-6) / 1e9
-        roof = {"bound": "hbm", "achieved": round(ach, 1),
-                "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": round(ach / peaks["hbm_gbs"], 4)}
-    else:
-        ach = algo_flops(m, n, k) / (us_call * 1e-6) / 1e12
-        roof = {"bound": "tensor", "achieved": round(ach, 1),
-                "peak": fp4_peak, "unit": "TFLOP/s",
-                "frac": round(ach / fp4_peak, 4)}
-    roof["traffic"] = load_traffic(args.workload)
-    roof["algorithmic_bytes"] = byts
-    roof["algorithmic_flops"] = algo_flops(m, n, k)
-    roof["peak_source"] = (
-        f"{peaks['source']} HBM copy GB/s; FP4 dense = 4 x {peaks['source']} "
-        "bf16 cuBLAS TF/s")
+    shapes, clocks, cpu = [], [], []
+    h2d_total = d2h_total = 0
+    launches = 0
+    for key in keys:
+        m, n, k = rank_shape(key, world)
+        sets = make_sets(key, world, rank, "cuda")
+        ns = len(sets)
 
-    # end to end through the public host-buffer API: pinned host inputs and
-    # output, the library uploads, computes and downloads (slab-pipelined)
-    d = sets[0]
-    dev_in = [d[0], d[1], d[2], d[6], d[7], d[8]]
-    host_in = [t.cpu().view(torch.uint8).pin_memory() for t in dev_in]
-    c_host = torch.empty(d[9].shape[:2], dtype=torch.float16).pin_memory()
-    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+        def step(i):
+            dg.custom_kernel(sets[i % ns])
 
-    def e2e_step():
-        dg.dual_gemm_host(*host_in, c_host, flags=args.flags)
+        ms, regions, clk = time_eager(step, args.steps, args.warmup, world,
+                                      args.repeats)
+        clocks.append(clk)
+        launches += args.steps * args.repeats
+        ranks_ms = gather_ranks(ms, world)
+        us = max(ranks_ms) * 1e3 / args.steps
+        flops_job = algo_flops(m, n, k) * world
+        ent = {"workload": key, "name": WORKLOADS[key]["name"], "M": m,
+               "N_per_rank": n, "K": k,
+               "us_per_call": round(us, 3),
+               "us_per_call_ranks": [round(v * 1e3 / args.steps, 3)
+                                     for v in ranks_ms],
+               "us_per_call_min_region": round(min(regions) * 1e3 /
+                                               args.steps, 3),
+               "tflops": round(flops_job / (us * 1e-6) / 1e12, 2),
+               "roofline": roofline(m, n, k, us, peaks, key),
+               "plan": dg.plan(m, n, k), "input_sets": ns,
+               "l2": f"{ns} rotating input sets of "
+                     f"{algo_bytes(m, n, k) / 1e6:.1f} MB (> 2 x 126 MB L2 "
+                     "between reuses)"}
+        # the same calls captured in a CUDA graph (caller workspace, so the
+        # capture allocates nothing), with and without STATIC_WEIGHTS
+        if not args.no_graph:
+            from nvfp4_dual_gemm_b200 import _lib
+            for tag, fl in (("graph", 0),
+                            ("graph_static_weights", _lib.FLAG_STATIC_WEIGHTS)):
+                ws = torch.zeros(max(dg.workspace_size(m, n, k, fl), 256),
+                                 dtype=torch.uint8, device="cuda")
 
-    e2e_ms, h2d, d2h = time_e2e(e2e_step, host_in, c_host, e2e_steps, world)
-    e2e_ms = max_over_ranks(e2e_ms, world)
-    e2e_val = ranks_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+                def gstep(i, fl=fl, ws=ws):
+                    d = sets[i % ns]
+                    dg.dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9],
+                                 flags=fl, workspace=ws)
 
+                gms, _ = time_graph(gstep, args.steps, args.warmup, world,
+                                    args.repeats)
+                ent[f"{tag}_us_per_call"] = round(
+                    max(gather_ranks(gms, world)) * 1e3 / args.steps, 3)
+                del ws
+        # end to end through the public host-buffer API: pinned host inputs
+        # and output; the library uploads, computes and downloads
+        if args.e2e_steps > 0:
+            dev_in, host_in, c_host = _host_copies(sets[0])
+            c_host = c_host.squeeze(-1)
+            e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+            def one():
+                dg.dual_gemm_host(*host_in, c_host)
+
+            e_ms = max(gather_ranks(time_e2e(one, None, None, e2e_steps,
+                                             world), world))
+            ent["e2e_tflops"] = round(flops_job * e2e_steps /
+                                      (e_ms * 1e-3) / 1e12, 3)
+            h2d_total += _nbytes(host_in)
+            d2h_total += _nbytes([c_host])
+            del host_in, c_host
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            cpu.append(cpu_baseline(sets[0], key))
+        shapes.append(ent)
+        del sets
+        torch.cuda.empty_cache()
+
+    value = geomean([s["tflops"] for s in shapes])
+    head = next((s for s in shapes if s["workload"] == "c2"), shapes[0])
+    roof = dict(head["roofline"])
+    roof["workload"] = head["workload"]
+    roof["geomean_frac_over_shapes"] = round(
+        geomean([s["roofline"]["frac"] for s in shapes]), 4)
+    strong = [k for k in keys if WORKLOADS[k].get("strong")]
     line = {
-        "metric": METRIC, "value": round(tflops, 3), "unit": "TFLOP/s",
+        "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "us_per_call": round(us_call, 3),
+        "repeats": args.repeats,
+        "ms_per_step": sum(s["us_per_call"] for s in shapes) / 1e3,
+        "us_per_call": {s["workload"]: s["us_per_call"] for s in shapes},
         "higher_is_better": True,
-        "scaling": "strong" if wl.get("strong") else "weak",
+        "scaling": "weak",
+        "scaling_by_workload": {k: ("strong" if WORKLOADS[k].get("strong")
+                                    else "weak") for k in keys},
         "vs_baseline": None,
         "dtype": "nvfp4 (e2m1 x e4m3/16, fp32 accumulate, fp16 out)",
-        "data": "synthetic: seeded randn -> NVFP4 on the GPU",
-        "config": {"workload": wl["name"], "M": m, "N_per_rank": n, "K": k,
-                   "L": 1, "parallelism": f"N-sharded x{world}" if world > 1
-                   else "single GPU", "plan": dg.plan(m, n, k, flags),
-                   "l2": f"{nsets} rotating input sets of "
-                         f"{algo_bytes(m, n, k) / 1e6:.1f} MB "
-                         f"(> 2 x 126 MB L2 between reuses)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once",
-                   "flags": (f"{flags:#x}" + (
-                       " (STATIC_WEIGHTS: the weights, constant across the "
-                       "timed calls, are copied before the dependency wait)"
-                       if flags & _lib.FLAG_STATIC_WEIGHTS else ""))},
+        "data": "synthetic: seeded randn -> NVFP4 by torch ops on the GPU",
+        "config": {
+            "workload": ("all four benchmark shapes (C2, C3, C4, C5)"
+                         if args.workload == "all"
+                         else WORKLOADS[args.workload]["name"]),
+            "shapes": keys, "L": 1,
+            "parallelism": (f"{world} ranks: " +
+                            ("C5 N-sharded (strong), " if strong else "") +
+                            "C2-C4 one full problem per rank (weak)")
+            if world > 1 else "single GPU",
+            "step": "one call of each shape",
+            "api": "custom_kernel(data) -> torch binding _C -> C ABI "
+                   "nvfp4_dual_gemm_run, default flags",
+            "timed": EAGER_TIMED,
+            "l2": "per shape, rotating input sets touching > 2 x 126 MB "
+                  "between reuses of a set"},
+        "shapes": shapes,
         "roofline": roof,
-        "e2e": {"value": round(e2e_val, 3), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "steps": e2e_steps,
-                "api": "nvfp4_dual_gemm_b200.dual_gemm_host "
-                       "(C ABI nvfp4_dual_gemm_run_host)"},
-        "gpu_launches": args.steps,
-        "clocks": clocks,
+        "e2e": {"value": round(geomean([s.get("e2e_tflops") for s in shapes])
+                               or 0.0, 3),
+                "unit": "TFLOP/s", "h2d_bytes_per_step": h2d_total,
+                "d2h_bytes_per_step": d2h_total,
+                "api": "nvfp4_dual_gemm_b200.dual_gemm_host (C ABI "
+                       "nvfp4_dual_gemm_run_host), geomean over the shapes"},
+        "gpu_launches": launches,
+        "gpu_launches_note": "dual GEMM kernel launches in the eager timed "
+                             "regions that give `value` (one per call)",
+        "clocks": merge_clocks(clocks),
     }
-    if args.shapes and world == 1:
-        line["shapes"] = shape_sweep(dg, args, flags)
-        vals = [s["tflops"] for s in line["shapes"]]
-        line["geomean_tflops"] = round(math.exp(sum(map(math.log, vals)) /
-                                                len(vals)), 3)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        hd = [t.view(torch.uint8).squeeze(-1).cpu().numpy() for t in
-              (d[0], d[3], d[1], d[4], d[2], d[5])]
-        line["cpu_baseline"] = cpu_baseline(*hd, m, n, k)
-    del sets
+    if cpu:
+        line["cpu_baseline"] = {
+            "value": geomean([p["value"] for p in cpu]), "unit": "TFLOP/s",
+            "cores": max(p["cores"] for p in cpu), "kind": "port",
+            "sample": "geomean over the shapes of the oracle (dequantise + "
+                      "fp32 matmul + SiLU) on a row sample of each: " +
+                      "; ".join(f"{p['workload']}: {p['sample']}"
+                                for p in cpu),
+            "shapes": cpu}
     return line
 
 
-def shape_sweep(dg, args, flags=0):
-    out = []
-    peaks = load_peaks()
-    for key in ("c2", "c3", "c4"):
-        wl = WORKLOADS[key]
-        m, n, k = wl["M"], wl["N"], wl["K"]
-        sets, nsets = make_sets(dg, m, n, k, wl, 0)
-        ws = torch.zeros(max(dg.workspace_size(m, n, k, flags), 256),
-                         dtype=torch.uint8, device="cuda")
-        steps = max(10, min(args.steps, 200))
-
-        def step(i):
-            d = sets[i % nsets]
-            dg.dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9],
-                         workspace=ws, flags=flags)
-
-        ms, _ = time_graph(step, steps, 3, 1)
-        us = ms * 1e3 / steps
-        t_roof = max(algo_bytes(m, n, k) / (peaks["hbm_gbs"] * 1e3),
-                     algo_flops(m, n, k) / (4 * peaks["bf16_tflops"] * 1e6))
-        out.append({"workload": key, "us": round(us, 3),
-                    "tflops": round(algo_flops(m, n, k) / us / 1e6, 2),
-                    "roofline_frac": round(t_roof / us, 4)})
-        del sets, ws
-        torch.cuda.empty_cache()
-    return out
+def ref_custom_kernel(entry, data):
+    """The reference's custom_kernel (submission.py:1153-1157): unpack the
+    10-tuple and call its torch-extension function with the blocked
+    scales."""
+    a, b1, b2, _sfa, _sfb1, _sfb2, sfa_b, sfb1_b, sfb2_b, c = data
+    return entry(a, b1, b2, sfa_b, sfb1_b, sfb2_b, c)
 
 
-def run_reference(args, world, rank):
-    """The reference's own implementation on the same workload."""
-    wl = WORKLOADS[args.workload]
-    m, n, k = rank_problem(wl, 1, 0)
-    import nvfp4_dual_gemm_b200 as dg  # input generation only
+def run_reference(args, world):
+    """The reference's own implementation on rank 0's shapes: its kernel
+    built from its sources (oracle/_ref), called eagerly as its
+    custom_kernel calls it; the CPU port of its algorithm where no kernel
+    is available.  Never imports this repository's package."""
     from oracle import build_ref
 
     mod = build_ref.load()
-    line = {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "impl": "reference",
-            "scaling": "strong" if wl.get("strong") else "weak",
-            "vs_baseline": None,
-            "dtype": "nvfp4 (e2m1 x e4m3/16, fp32 accumulate, fp16 out)",
-            "data": "synthetic: seeded randn -> NVFP4 on the GPU",
-            "config": {"workload": wl["name"], "M": m, "N_per_rank": n, "K": k,
-                       "L": 1, "parallelism": "rank 0 only"}}
-    sets, nsets = make_sets(dg, m, n, k, wl, 0)
-    d0 = sets[0]
-    hd = [t.view(torch.uint8).squeeze(-1).cpu().numpy() for t in
-          (d0[0], d0[3], d0[1], d0[4], d0[2], d0[5])]
-    cpu = None if args.no_cpu_baseline else cpu_baseline(*hd, m, n, k)
-    if mod is not None and (m, n, k) in build_ref.SAFE_SHAPES:
-        def step(i):
-            d = sets[i % nsets]
-            mod.cuda_nvfp4_dual_gemm(d[0], d[1], d[2], d[6], d[7], d[8], d[9])
+    keys = ALL if args.workload == "all" else [args.workload]
+    peaks = load_peaks()
+    shapes, clocks, cpu = [], [], []
+    h2d_total = d2h_total = 0
+    missing = []
+    for key in keys:
+        m, n, k = rank_shape(key, world)
+        entry = build_ref.entry(mod, (m, n, k))
+        sets = make_sets(key, world, 0, "cuda")
+        ns = len(sets)
+        if entry is None:
+            missing.append(key)
+            cpu.append(cpu_baseline(sets[0], key))
+            shapes.append({"workload": key, "M": m, "N_per_rank": n, "K": k,
+                           "tflops": cpu[-1]["value"],
+                           "kind": "CPU port (no reference kernel)"})
+            del sets
+            continue
 
-        # The reference launches on the legacy default stream
-        # (nvfp4_dual_gemm.cu:368-372), which no CUDA graph can capture, so
-        # its steps are timed as back-to-back eager calls.
-        ms, clocks = time_eager(step, args.steps, args.warmup, 1)
-        tflops = algo_flops(m, n, k) * args.steps / (ms * 1e-3) / 1e12
-        dev_in = [d0[0], d0[1], d0[2], d0[6], d0[7], d0[8]]
-        host_in = [t.cpu().pin_memory() for t in dev_in]
-        c_host = torch.empty(d0[9].shape, dtype=torch.float16).pin_memory()
-        e2e_steps = max(1, min(args.steps, args.e2e_steps))
-        e2e_ms, h2d, d2h = time_e2e(
-            copy_call_copy(
-                lambda: mod.cuda_nvfp4_dual_gemm(d0[0], d0[1], d0[2], d0[6],
-                                                 d0[7], d0[8], d0[9]),
-                host_in, dev_in, d0[9], c_host),
-            host_in, c_host, e2e_steps, 1)
-        line.update({
-            "value": round(tflops, 3), "ms_per_step": ms / args.steps,
-            "us_per_call": round(ms * 1e3 / args.steps, 3),
-            "reference_kind": "the reference's CUDA kernel, compiled from its "
-                              "sources by oracle/build_ref.py, called through "
-                              "its cuda_nvfp4_dual_gemm entry",
-            "timed": "back-to-back eager calls (legacy default stream, "
-                     "not capturable in a CUDA graph)",
-            "e2e": {"value": round(algo_flops(m, n, k) * e2e_steps /
-                                   (e2e_ms * 1e-3) / 1e12, 3),
-                    "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "clocks": clocks, "cpu_baseline": cpu})
-    else:
-        why = ("oracle/_ref not built" if mod is None else
-               "shape outside the reference kernel's dispatch table")
-        if cpu is None:
-            cpu = cpu_baseline(*hd, m, n, k)
-        line.update({
-            "value": cpu["value"], "ms_per_step": None,
-            "reference_kind": f"CPU port of the reference algorithm ({why})",
-            "cpu_baseline": cpu,
-            "e2e": {"value": cpu["value"], "unit": "TFLOP/s",
-                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+        def step(i):
+            ref_custom_kernel(entry, sets[i % ns])
+
+        ms, regions, clk = time_eager(step, args.steps, args.warmup, 1,
+                                      args.repeats)
+        clocks.append(clk)
+        us = ms * 1e3 / args.steps
+        ent = {"workload": key, "name": WORKLOADS[key]["name"], "M": m,
+               "N_per_rank": n, "K": k, "us_per_call": round(us, 3),
+               "us_per_call_min_region": round(min(regions) * 1e3 /
+                                               args.steps, 3),
+               "tflops": round(algo_flops(m, n, k) / (us * 1e-6) / 1e12, 2),
+               "roofline": roofline(m, n, k, us, peaks, key),
+               "entry": ("cuda_nvfp4_dual_gemm (its dispatch table)"
+                         if (m, n, k) in build_ref.SAFE_SHAPES else
+                         "cuda_nvfp4_dual_gemm_generic (its launcher "
+                         "template, instantiated for this shape)")}
+        if args.e2e_steps > 0:
+            d0 = sets[0]
+            dev_in, host_in, c_host = _host_copies(d0)
+            e2e_steps = max(1, min(args.steps, args.e2e_steps))
+
+            def one():
+                for h, dv in zip(host_in, dev_in):
+                    dv.view(torch.uint8).copy_(h, non_blocking=True)
+                ref_custom_kernel(entry, d0)
+                c_host.copy_(d0[9], non_blocking=True)
+
+            e_ms = time_e2e(one, None, None, e2e_steps, 1)
+            ent["e2e_tflops"] = round(algo_flops(m, n, k) * e2e_steps /
+                                      (e_ms * 1e-3) / 1e12, 3)
+            h2d_total += _nbytes(host_in)
+            d2h_total += _nbytes([c_host])
+        if not args.no_cpu_baseline and world == 1:
+            cpu.append(cpu_baseline(sets[0], key))
+        shapes.append(ent)
+        del sets
+        torch.cuda.empty_cache()
+
+    value = geomean([s["tflops"] for s in shapes])
+    head = next((s for s in shapes if s["workload"] == "c2"), shapes[0])
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s",
+        "n_gpus": 1, "ranks_in_job": world, "impl": "reference",
+        "steps": args.steps, "warmup": args.warmup, "repeats": args.repeats,
+        "ms_per_step": sum(s.get("us_per_call", 0.0) for s in shapes) / 1e3,
+        "us_per_call": {s["workload"]: s.get("us_per_call") for s in shapes},
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "nvfp4 (e2m1 x e4m3/16, fp32 accumulate, fp16 out)",
+        "data": "synthetic: seeded randn -> NVFP4 by torch ops on the GPU "
+                "(the same bytes as the other arm)",
+        "config": {"workload": ("all four benchmark shapes (C2, C3, C4, C5)"
+                                if args.workload == "all"
+                                else WORKLOADS[args.workload]["name"]),
+                   "shapes": keys, "L": 1,
+                   "parallelism": ("rank 0 alone, on one rank's shapes "
+                                   f"(C5 N / {world})" if world > 1 else
+                                   "single GPU"),
+                   "timed": EAGER_TIMED},
+        "reference_kind": ("the reference's CUDA kernel compiled from its "
+                           "sources by oracle/build_ref.py, called as its "
+                           "custom_kernel calls it (submission.py:1153-1157)"
+                           if mod is not None else
+                           "CPU port of the reference algorithm "
+                           "(oracle/_ref not built)"),
+        "shapes": shapes,
+        "roofline": dict(head.get("roofline", {}), workload=head["workload"]),
+        "e2e": {"value": round(geomean([s.get("e2e_tflops") for s in shapes])
+                               or 0.0, 3), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d_total,
+                "d2h_bytes_per_step": d2h_total,
+                "api": "pinned H2D of the inputs, the reference's entry, "
+                       "D2H of C, on the current stream"},
+        "clocks": merge_clocks(clocks) if clocks else None,
+    }
+    if missing:
+        line["cpu_port_for"] = missing
+    if cpu:
+        line["cpu_baseline"] = {
+            "value": geomean([p["value"] for p in cpu]), "unit": "TFLOP/s",
+            "cores": max(p["cores"] for p in cpu), "kind": "port",
+            "sample": "; ".join(f"{p['workload']}: {p['sample']}"
+                                for p in cpu),
+            "note": "the reference's own CPU path (its harness's dequantise-"
+                    "to-fp32 check) is not part of the reference; this is "
+                    "the oracle's restatement of it",
+            "shapes": cpu}
     return line
 
 
@@ -545,8 +809,9 @@ PLUMBING = {
 
 
 def run_plumbing(args):
-    """Time one of the kernels beside the dual GEMM (SURVEY-style 'next'
-    rows): the activation quantiser or the scale layout converter, in a
+    """Time one of the kernels beside the dual GEMM (the formats and callers
+    on either side of it): the activation quantiser or the scale layout
+    converter, in a
     CUDA graph over rotating buffers larger than 2 x L2; one JSON line with
     GB/s against the measured HBM copy bandwidth."""
     import nvfp4_dual_gemm_b200 as dg
@@ -594,7 +859,7 @@ def run_plumbing(args):
                                              k // 16, blks[j].data_ptr(),
                                              stream())
             assert rc == 0, _lib.last_error()
-    ms, clocks = time_graph(step, args.steps, args.warmup, 1)
+    ms, clocks = time_graph(step, args.steps, args.warmup, 1, args.repeats)
     us = ms * 1e3 / args.steps
     gbs = per / (us * 1e-6) / 1e9
     peaks = load_peaks()
@@ -606,7 +871,7 @@ def run_plumbing(args):
         "config": {"workload": args.plumbing, "rows": rows, "K": k,
                    "bytes_per_call": per,
                    "l2": f"{nsets} rotating buffer sets (> 2 x 126 MB L2)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+                   "timed": GRAPH_TIMED},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4),
@@ -646,8 +911,8 @@ def run_batched(args, cfg):
                          d[8][b * blk_b:(b + 1) * blk_b], d[9][..., b],
                          workspace=ws)
 
-    ms_1, clocks = time_graph(one_launch, args.steps, args.warmup, 1)
-    ms_l, _ = time_graph(per_batch, args.steps, args.warmup, 1)
+    ms_1, clocks = time_graph(one_launch, args.steps, args.warmup, 1, args.repeats)
+    ms_l, _ = time_graph(per_batch, args.steps, args.warmup, 1, args.repeats)
     us_1 = ms_1 * 1e3 / args.steps
     us_l = ms_l * 1e3 / args.steps
     flops = L * algo_flops(m, n, k)
@@ -662,7 +927,7 @@ def run_batched(args, cfg):
         "higher_is_better": True, "data": "synthetic: seeded randn -> NVFP4",
         "config": {"workload": "batched", "M": m, "N": n, "K": k, "L": L,
                    "l2": f"{nsets} rotating input sets (> 2 x 126 MB L2)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+                   "timed": GRAPH_TIMED},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4),
@@ -714,8 +979,8 @@ def run_grouped(args, cfg):
         d = sets[i % nsets]
         dg.dual_gemm_grouped(*d, rows, workspace=wsg)
 
-    ms_g, clocks = time_graph(grouped, args.steps, args.warmup, 1)
-    ms_e, _ = time_graph(per_expert, args.steps, args.warmup, 1)
+    ms_g, clocks = time_graph(grouped, args.steps, args.warmup, 1, args.repeats)
+    ms_e, _ = time_graph(per_expert, args.steps, args.warmup, 1, args.repeats)
     us_g = ms_g * 1e3 / args.steps
     us_e = ms_e * 1e3 / args.steps
     flops = 4 * sum(rows) * n * k
@@ -729,7 +994,7 @@ def run_grouped(args, cfg):
         "higher_is_better": True, "data": "synthetic: seeded randn -> NVFP4",
         "config": {"workload": "grouped", "group_rows": rows, "N": n, "K": k,
                    "l2": f"{nsets} rotating input sets (> 2 x 126 MB L2)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+                   "timed": GRAPH_TIMED},
         "roofline": {"bound": "hbm",
                      "achieved": round(per / (us_g * 1e-6) / 1e9, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -751,8 +1016,8 @@ def run_nvfp4_out(args, cfg):
 
     lib = _lib.load()
     m, n, k = cfg["rows"], cfg["N"], cfg["K"]
-    wl = WORKLOADS["c2"]
-    sets, nsets = make_sets(dg, m, n, k, wl, 0)
+    sets = make_sets("c2", 1, 0, "cuda")
+    nsets = len(sets)
     cq = torch.empty((m, n // 2), dtype=torch.uint8, device="cuda")
     sfc = torch.empty((((m + 127) // 128) * (n // 64) * 512,),
                       dtype=torch.uint8, device="cuda")
@@ -769,8 +1034,8 @@ def run_nvfp4_out(args, cfg):
             sfc.data_ptr(), torch.cuda.current_stream().cuda_stream)
         assert rc == 0, _lib.last_error()
 
-    ms_f, clocks = time_graph(fused, args.steps, args.warmup, 1)
-    ms_u, _ = time_graph(unfused, args.steps, args.warmup, 1)
+    ms_f, clocks = time_graph(fused, args.steps, args.warmup, 1, args.repeats)
+    ms_u, _ = time_graph(unfused, args.steps, args.warmup, 1, args.repeats)
     us_f = ms_f * 1e3 / args.steps
     us_u = ms_u * 1e3 / args.steps
     tflops = algo_flops(m, n, k) / (us_f * 1e-6) / 1e12
@@ -787,7 +1052,7 @@ def run_nvfp4_out(args, cfg):
         "config": {"workload": "nvfp4_out", "M": m, "N": n, "K": k,
                    "plan": dg.plan(m, n, k),
                    "l2": f"{nsets} rotating input sets (> 2 x 126 MB L2)",
-                   "timed": "one CUDA graph of `steps` calls, replayed once"},
+                   "timed": GRAPH_TIMED},
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1),
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(gbs / peaks["hbm_gbs"], 4),
@@ -797,29 +1062,31 @@ def run_nvfp4_out(args, cfg):
     }
 
 
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__,
                                  formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=500)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20,
+                    help="calls per timed region (per shape)")
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--repeats", type=int, default=50,
+                    help="timed regions per shape; the median is reported")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
-    ap.add_argument("--flags", type=int, default=0,
-                    help="NVFP4DG_FLAG_* bits (0 = automatic schedule)")
-    ap.add_argument("--e2e-steps", type=int, default=50)
-    ap.add_argument("--shapes", action="store_true",
-                    help="also time C2/C3/C4 and report their geomean")
+    ap.add_argument("--workload", choices=["all"] + ALL, default="all")
+    ap.add_argument("--e2e-steps", type=int, default=10,
+                    help="end-to-end steps per shape (0: skip)")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="skip the CUDA-graph timings beside the eager ones")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-static-weights", action="store_true",
-                    help="time without NVFP4DG_FLAG_STATIC_WEIGHTS (weight "
-                         "copies then also wait for the previous kernel)")
     ap.add_argument("--plumbing", choices=sorted(PLUMBING),
-                    help="time the activation quantiser or the scale layout "
-                         "converter instead of the dual GEMM (1 GPU)")
+                    help="time one of the kernels beside the dual GEMM "
+                         "instead (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    args.repeats = max(1, args.repeats)
     if args.plumbing:
         print(json.dumps(run_plumbing(args)), flush=True)
         return
@@ -827,11 +1094,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
+        # rank 0 alone runs the reference arm; the other ranks have no work
         if rank != 0:
             return
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        line = run_reference(args, world, rank)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(run_reference(args, world)), flush=True)
         return
     world, rank, _ = dist_setup()
     try:

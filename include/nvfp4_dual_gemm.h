@@ -102,6 +102,20 @@ extern "C" {
                                               copy brings both when B2 lies
                                               above B1 at a multiple of 16
                                               bytes)                          */
+#define NVFP4DG_FLAG_TEST_SK_TIMEOUT (1u << 25) /* test hook, never for
+                                              production: the owner of each
+                                              tile split along K (stream-K)
+                                              waits for one contribution more
+                                              than exist, with a ~1e6-cycle
+                                              limit, so that its bounded wait
+                                              runs out and the call reports
+                                              NVFP4DG_ERR_DEVICE (with
+                                              NVFP4DG_FLAG_SYNC_CHECK) or
+                                              nvfp4_dual_gemm_device_status
+                                              does; the failure path is
+                                              tested without a GPU fault.  A
+                                              caller-owned workspace must be
+                                              zero-filled again afterwards. */
 
 /*
  * Run the dual GEMM on `stream` using a workspace the library keeps per
@@ -297,12 +311,15 @@ NVFP4DG_API int nvfp4_dual_gemm_plan_work(int M, int N, int K, unsigned flags, i
  * static array of NVFP4DG_NOALLOC_SCRATCH_BYTES that every GPU which loads
  * the library holds until the process exits, and it calls no cudaMalloc,
  * cudaFree or other allocating routine.  The caller passes inputs and
- * outputs as for nvfp4_dual_gemm_run.  The first call on a device looks up
- * the array's device address (cudaGetSymbolAddress) with that device
- * current; make that first call before any stream capture.  A problem whose
- * schedule needs more scratch than the array holds is rejected with
- * NVFP4DG_ERR_WORKSPACE (see the message; nvfp4_dual_gemm_run_ws takes a
- * larger caller-owned buffer, and NVFP4DG_FLAG_NO_STREAMK needs none).
+ * outputs as for nvfp4_dual_gemm_run, for one problem: L must be 1 (batched
+ * problems go through nvfp4_dual_gemm_run or nvfp4_dual_gemm_run_ws).  The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  When the automatic schedule would need more
+ * scratch than the array holds, the call runs whole tiles instead (no
+ * scratch); only a schedule forced with NVFP4DG_FLAG_FORCE_STREAMK that
+ * does not fit is rejected with NVFP4DG_ERR_WORKSPACE
+ * (nvfp4_dual_gemm_run_ws takes a larger caller-owned buffer).
  * Every call shares the one array, which keeps the last call's contents:
  * each call clears the tile counters it needs before launching.  Each
  * device has its own copy of the array, but calls that overlap on the GPU of

@@ -36,6 +36,7 @@ FLAG_NO_SPLITK = 1 << 21
 FLAG_NO_PDL = 1 << 22
 FLAG_NO_MERGED_B = 1 << 23
 FLAG_STATIC_WEIGHTS = 1 << 24
+FLAG_TEST_SK_TIMEOUT = 1 << 25
 
 # Input element types of nvfp4_quantize_rows.
 DTYPE_F32 = 0
@@ -115,6 +116,26 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
         return lib
+
+
+_ext_mod = None
+
+
+def ext():
+    """The torch binding ``_C`` (custom_kernel / cuda_nvfp4_dual_gemm /
+    dual_gemm over the C ABI, built in-tree beside libnvfp4dg.so)."""
+    global _ext_mod
+    if _ext_mod is not None:
+        return _ext_mod
+    load()  # the binding links against the library loaded here
+    try:
+        from . import _C
+    except ImportError as exc:
+        raise NativeLibraryError(
+            f"the torch binding _C is missing or fails to load ({exc}); "
+            "build it with `python -m nvfp4_dual_gemm_b200.build`") from exc
+    _ext_mod = _C
+    return _C
 
 
 def last_error() -> str:

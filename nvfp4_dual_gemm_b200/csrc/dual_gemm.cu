@@ -44,6 +44,11 @@ constexpr int kTmemCols = 512;
 constexpr int kSfTmemBase = 256;    // scale regions follow the accumulator
 constexpr int kSfTmemPerStage = 48; // SFA 4 x 4 cols, SFB 4 x (4 + 4) cols
 
+// Wait limit of the stream-K owner under NVFP4DG_FLAG_TEST_SK_TIMEOUT
+// (~0.5 ms): long enough for every real contribution to land, short enough
+// for a test.
+constexpr long long kTestWaitLimitCycles = 1000ll * 1000ll;
+
 // Device error word bits (role whose bounded wait expired).
 constexpr unsigned kErrProducer = 1u << 0;
 constexpr unsigned kErrMma = 1u << 1;
@@ -110,6 +115,11 @@ struct KParams {
   int static_weights;
   // pair kernel: 3-D tensor maps (batch / group coordinate) instead of 2-D
   int maps3d;
+  // stream-K owners wait for b_last - b_first + sk_extra contributions, at
+  // most sk_wait_limit cycles (sk_extra = 1 and a short limit only under
+  // NVFP4DG_FLAG_TEST_SK_TIMEOUT, to make that bounded wait run out)
+  int sk_extra;
+  long long sk_wait_limit;
   GroupTable groups;
 };
 
@@ -689,6 +699,7 @@ __device__ __forceinline__ void split_epilogue(
   }
   ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
   if (!split_group_all(ok)) return;
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 41);
   const uint32_t xbuf = smem_u32(smem);
   const uint32_t xdst = mapa_shared(xbuf, xpeer);
   // This warp's chunks j = part, part + 2 (at most two): all TMEM loads are
@@ -724,6 +735,7 @@ __device__ __forceinline__ void split_epilogue(
       }
     }
   }
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 42);
   bool all_ok = true;
   // Own chunks: both TMEM reads before one wait, then each chunk as soon as
   // the peer's partials of it have landed.
@@ -737,11 +749,13 @@ __device__ __forceinline__ void split_epilogue(
     }
   }
   tc_wait_ld();
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 43);
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
     const int c = part + 2 * i;
     if (c >= kHalfChunks) continue;
     all_ok = mbar_wait(&recv_bar[c], 0, p.err, kErrEpilogue) && all_ok;
+    if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 44 + i);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const uint4 rx = lds128(xbuf + ((c * 4 + q) * 128u + row) * 16u);
@@ -1217,7 +1231,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool ready = true;
           if (threadIdx.x == 0) {
             NVFP4DG_STAMP(5, 40);
-            ready = wait_count(counter, b_last - b_first, p.err, kErrEpilogue);
+            ready = wait_count(counter, b_last - b_first + p.sk_extra, p.err,
+                               kErrEpilogue, p.sk_wait_limit);
             if (ready) *counter = 0;  // ready for the next launch
           }
           if (!group_all<1>(ready)) break;
@@ -1353,6 +1368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&ready_bar, 1);
     for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
     fence_mbar_init();
+    NVFP4DG_STAMP(9, 56);
     // arm the first scale fill of every stage
     for (int s = 0; s < S; ++s)
       mbar_arrive_expect_tx(&sfdata_bar[s], 3 * kSfRunBytes);
@@ -1371,6 +1387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kMmaWarp) {
       tmem_alloc_pair(&tmem_base_sh, kTmemCols);
       tmem_relinquish_pair();
+      if (lane == 0) NVFP4DG_STAMP(9, 60);
     }
     tc_fence_before();
     named_bar_sync(kBarStart, kThreads - 64);  // TMEM base, barrier inits
@@ -1427,7 +1444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if (have) place();
     named_bar_sync(kBarInit, 96);  // this CTA's mbarriers are initialised
+    if (a_side && lane == 0) NVFP4DG_STAMP(9, 57);
     cluster_wait();                // and every other CTA's
+    if (a_side && lane == 0) NVFP4DG_STAMP(9, 58);
     if (lane == 0) {
       const uint32_t full_c = mapa_shared(smem_u32(&full_bar[0]), lead);
       int stage = 0;
@@ -1438,6 +1457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // when the caller declares them unwritten by earlier kernels
       const bool w_early = p.static_weights != 0;
       if (a_side || !w_early) griddep_wait();
+      if (a_side) NVFP4DG_STAMP(9, 59);
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (issued >= S &&
@@ -1714,6 +1734,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+            if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
           }
           emit32(out, 32 * c, x, y);
         }
@@ -1752,7 +1773,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool ready = true;
           if (threadIdx.x == 0) {
             NVFP4DG_STAMP(5, 40);
-            ready = wait_count(counter, b_last - b_first, p.err, kErrEpilogue);
+            ready = wait_count(counter, b_last - b_first + p.sk_extra, p.err,
+                               kErrEpilogue, p.sk_wait_limit);
             if (ready) *counter = 0;  // ready for the next launch
           }
           if (!group_all<1>(ready)) break;
@@ -2474,6 +2496,9 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.b_merged = merged ? 1 : 0;
   kp.static_weights = (flags & NVFP4DG_FLAG_STATIC_WEIGHTS) ? 1 : 0;
   kp.maps3d = maps3d ? 1 : 0;
+  const bool expire = (flags & NVFP4DG_FLAG_TEST_SK_TIMEOUT) != 0;
+  kp.sk_extra = expire ? 1 : 0;
+  kp.sk_wait_limit = expire ? kTestWaitLimitCycles : kWaitLimitCycles;
   if (groups) {
     kp.groups = *groups;
   } else {
@@ -2686,6 +2711,11 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
     if (word != 0) {
       const unsigned zero = 0;
       cudaMemcpyToSymbol(g_err_word, &zero, sizeof(zero));
+      // a stream-K owner that gave up left its tile counter behind: clear
+      // the counters of the library's own workspace for the next call (a
+      // caller-owned workspace must be zero-filled again by the caller)
+      if (own_ws && ws != nullptr)
+        cudaMemsetAsync(ws, 0, static_cast<size_t>(kCounterBytes), stream);
       return fail(NVFP4DG_ERR_DEVICE,
                   "kernel wait timed out (device error word " +
                       std::to_string(word) + ")");
@@ -3108,71 +3138,47 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
   g_last_error.clear();
   int rc = check_problem(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags);
   if (rc) return rc;
-  if (M == 0 || N == 0) return NVFP4DG_OK;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  if (K == 0) {  // empty sums: silu(0) * 0 = 0
-    cudaError_t e =
-        cudaMemsetAsync(C, 0, (size_t)M * N * sizeof(__half), stream);
-    return e == cudaSuccess ? NVFP4DG_OK : cuda_fail(e, "cudaMemsetAsync");
-  }
-  std::lock_guard<std::mutex> lock(g_mu);
-  int devid = 0;
-  cudaError_t e = cudaGetDevice(&devid);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  DevInfo* dev = nullptr;
-  if ((rc = device_info(devid, &dev))) return rc;
+  if (M == 0 || N == 0 || K == 0)  // nothing needs scratch
+    return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, nullptr,
+                    0, false, stream_ptr);
   void* scratch = nullptr;
-  if ((rc = noalloc_scratch(devid, &scratch))) return rc;
-  const Plan plan = choose_plan(M, N, K, flags, dev->sms);
-  if (plan.grid == 0)
-    return fail(NVFP4DG_ERR_UNSUPPORTED,
-                "cluster split-K needs 2 x tiles x CTAs per tile <= SMs and K >= 512");
-  const size_t need = static_cast<size_t>(workspace_bytes(plan));
-  if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
-    return fail(NVFP4DG_ERR_WORKSPACE,
-                "this schedule needs " + std::to_string(need) +
-                    " bytes of scratch; nvfp4_dual_gemm_run_noalloc holds "
-                    "at most " +
-                    std::to_string(NVFP4DG_NOALLOC_SCRATCH_BYTES) +
-                    " (use nvfp4_dual_gemm_run_ws, a smaller grid, or "
-                    "NVFP4DG_FLAG_NO_STREAMK)");
-  void* ws = nullptr;
-  if (need > 0) {
-    // The array keeps the previous call's contents: zero the tile counters.
-    e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(kCounterBytes),
-                        stream);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch)");
-    ws = scratch;
-  }
-  if (plan.ctas == 2 && plan.bn == 128)
-    rc = launch<128, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                           N, K, ws, flags, stream);
-  else if (plan.ctas == 2)
-    rc = launch<64, true>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C, M,
-                          N, K, ws, flags, stream);
-  else if (plan.bn == 128)
-    rc = launch<128, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                            M, N, K, ws, flags, stream);
-  else
-    rc = launch<64, false>(plan, *dev, devid, A, B1, B2, SFA, SFB1, SFB2, C,
-                           M, N, K, ws, flags, stream);
-  if (rc) return rc;
-  if (flags & NVFP4DG_FLAG_SYNC_CHECK) {
-    unsigned word = 0;
-    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess)
-      return cuda_fail(e, "cudaStreamSynchronize");
-    if ((e = cudaMemcpyFromSymbol(&word, g_err_word, sizeof(word))) !=
-        cudaSuccess)
-      return cuda_fail(e, "cudaMemcpyFromSymbol");
-    if (word != 0) {
-      const unsigned zero = 0;
-      cudaMemcpyToSymbol(g_err_word, &zero, sizeof(zero));
-      return fail(NVFP4DG_ERR_DEVICE,
-                  "kernel wait timed out (device error word " +
-                      std::to_string(word) + ")");
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    int devid = 0;
+    cudaError_t e = cudaGetDevice(&devid);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    DevInfo* dev = nullptr;
+    if ((rc = device_info(devid, &dev))) return rc;
+    if ((rc = noalloc_scratch(devid, &scratch))) return rc;
+    // The automatic schedule may split tiles along K over a full grid
+    // (stream-K), whose partials can exceed the array; whole tiles need no
+    // scratch at all, so fall back to them unless stream-K was forced.
+    size_t need = static_cast<size_t>(
+        workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+    if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES &&
+        !(flags & NVFP4DG_FLAG_FORCE_STREAMK)) {
+      flags |= NVFP4DG_FLAG_NO_STREAMK;
+      need = static_cast<size_t>(
+          workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+    }
+    if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
+      return fail(NVFP4DG_ERR_WORKSPACE,
+                  "this schedule needs " + std::to_string(need) +
+                      " bytes of scratch; nvfp4_dual_gemm_run_noalloc holds "
+                      "at most " +
+                      std::to_string(NVFP4DG_NOALLOC_SCRATCH_BYTES) +
+                      " (use nvfp4_dual_gemm_run_ws or a smaller forced "
+                      "grid)");
+    if (need > 0) {
+      // The array keeps the previous call's contents (a call that timed out
+      // may leave counts behind): zero the tile counters.
+      e = cudaMemsetAsync(scratch, 0, static_cast<size_t>(kCounterBytes),
+                          static_cast<cudaStream_t>(stream_ptr));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(scratch)");
     }
   }
-  return NVFP4DG_OK;
+  return run_impl(A, B1, B2, SFA, SFB1, SFB2, C, M, N, K, L, flags, scratch,
+                  NVFP4DG_NOALLOC_SCRATCH_BYTES, false, stream_ptr);
 }
 
 size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,

@@ -129,14 +129,15 @@ __device__ __forceinline__ int ld_acquire(const int* ptr) {
 
 // Wait until the counter at `ptr` reaches `target`, bounded like mbar_wait.
 __device__ __forceinline__ bool wait_count(const int* ptr, int target,
-                                           unsigned* err, unsigned code) {
+                                           unsigned* err, unsigned code,
+                                           long long limit = kWaitLimitCycles) {
   if (ld_acquire(ptr) == target) return true;
   const long long t0 = clock_cycles();
   for (;;) {
     __nanosleep(32);
     if (ld_acquire(ptr) == target) return true;
     if (*reinterpret_cast<volatile unsigned*>(err) != 0u) return false;
-    if (clock_cycles() - t0 > kWaitLimitCycles) {
+    if (clock_cycles() - t0 > limit) {
       atomicOr(err, code);
       return false;
     }

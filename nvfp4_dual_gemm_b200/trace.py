@@ -69,11 +69,42 @@ def summarise(buf: np.ndarray) -> dict:
         ])
     if not rows:
         return {}
+    # accumulator hold of whole-tile epilogues (ready -> released, role 8)
+    # and the phases of the cluster split-K epilogue (role 8, slots 41-45)
+    hold, split = [], []
+    for c in range(buf.shape[0]):
+        t = buf[c]
+        for u in range(40):
+            if t[4, u] > 0 and t[8, u] > 0:
+                hold.append(t[8, u] - t[4, u])
+        if t[4, 0] > 0 and t[8, 41] > 0 and t[8, 43] > 0:
+            split.append([t[8, 41] - t[4, 0], t[8, 42] - t[8, 41],
+                          t[8, 43] - t[8, 42], t[8, 44] - t[8, 43],
+                          t[5, 0] - t[8, 44]])
     med = np.median(np.array(rows, dtype=np.float64), axis=0)
     keys = ["first_mma", "period", "mma_issue", "scale_store", "scale_land",
             "epilogue", "kblocks"]
     out = {k: float(v) for k, v in zip(keys, med)}
     out["ctas"] = len(rows)
+    if hold:
+        out["epilogue_hold"] = float(np.median(hold))
+    # pair kernel prologue (role 9 slots 56-60, SM cycles from entry, role 4
+    # slot 61): barriers initialised, producer past its CTA barrier, past
+    # the cluster barrier, past the dependency wait, TMEM allocated (the
+    # 1-SM kernel uses role 9 for per-block stamps instead)
+    ent = buf[:, 4, 61]
+    for slot, name in ((56, "pro_bar_init"), (57, "pro_prod_cta_bar"),
+                       (58, "pro_prod_cluster_bar"), (59, "pro_prod_depwait"),
+                       (60, "pro_tmem_alloc")):
+        v = buf[:, 9, slot]
+        ok_ = (v > 0) & (ent > 0)
+        if ok_.sum() > 0:
+            out[name] = float(np.median(v[ok_] - ent[ok_]))
+    if split:
+        sm = np.median(np.array(split, dtype=np.float64), axis=0)
+        for k, v in zip(["split_peer_ready", "split_send", "split_own_ld",
+                         "split_first_recv", "split_rest"], sm):
+            out[k] = float(v)
     # global-timer stamps (ns) of every CTA: entry, past the dependency wait,
     # exit
     ent = buf[:, 5, 61]
@@ -119,6 +150,10 @@ def main(argv=None) -> None:
     ap.add_argument("--flags", type=lambda s: int(s, 0), default=0)
     ap.add_argument("--calls", type=int, default=4,
                     help="warm-up calls before the traced one")
+    ap.add_argument("--back-to-back", action="store_true",
+                    help="no synchronize before the traced call: it starts "
+                         "while the previous calls drain, as in a stream of "
+                         "calls (the stamps of the last call win)")
     args = ap.parse_args(argv)
 
     import torch
@@ -149,6 +184,9 @@ def main(argv=None) -> None:
         call(i)
     torch.cuda.synchronize()
     lib.nvfp4_dual_gemm_trace_read(buf.ctypes.data, buf.nbytes)  # clear
+    if args.back_to_back:
+        for i in range(args.calls):
+            call(i)
     call(args.calls)
     torch.cuda.synchronize()
     lib.nvfp4_dual_gemm_trace_read(buf.ctypes.data, buf.nbytes)

@@ -12,7 +12,10 @@ to GPU machines with the checkout, the reference sources do not.
 
 The reference directory defaults to ``reference`` beside this repository and can be overridden with ``NVFP4DG_REFERENCE_DIR``.
 
-The module exposes ``cuda_nvfp4_dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C)``.
+The module exposes ``cuda_nvfp4_dual_gemm(A, B1, B2, SFA, SFB1, SFB2, C)``
+(the reference's own dispatch entry) and ``cuda_nvfp4_dual_gemm_generic``
+(the same arguments; the reference's launcher template instantiated for
+``GENERIC_SHAPES``).
 Safe shapes: only those in the reference's dispatch table
 (nvfp4_dual_gemm.cu:403-442) with K / 256 >= 4; for K / 256 < 4 the
 reference's producer prologue issues scale copies past the end of the scale
@@ -41,6 +44,24 @@ SAFE_SHAPES = {
 # The reference returns C as a transposed view for this shape
 # (nvfp4_dual_gemm.cu:413-415): column-major storage.
 TRANSPOSED_SHAPES = {(512, 3072, 7168)}
+# Shapes outside the dispatch table run through the harness-side
+# instantiation of the reference's launcher template
+# (``cuda_nvfp4_dual_gemm_generic`` in ref_binding.cu): the benchmark's
+# prefill shape and its N-sharded rank slices for 1, 2, 4 and 8 GPUs.
+GENERIC_SHAPES = {(4096, 14336, 4096)} | {
+    (8192, 28672 // w, 8192) for w in (1, 2, 4, 8)}
+
+
+def entry(mod, shape):
+    """The reference module's function that runs `shape`, or None."""
+    if mod is None:
+        return None
+    if tuple(shape) in SAFE_SHAPES:
+        return mod.cuda_nvfp4_dual_gemm
+    if tuple(shape) in GENERIC_SHAPES and hasattr(
+            mod, "cuda_nvfp4_dual_gemm_generic"):
+        return mod.cuda_nvfp4_dual_gemm_generic
+    return None
 
 
 def reference_dir() -> str:

@@ -4,7 +4,7 @@ Run on a machine with a B200 and the reference kernel built into
 ``oracle/_ref`` (``python oracle/build_ref.py`` where the reference sources
 are present)::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [MxNxK ...]
 
 For each case the inputs come from ``oracle.nvfp4_oracle.make_problem`` (seeded
 numpy, bit-reproducible on any machine), the output from the reference's own
@@ -27,11 +27,16 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
 
 from oracle import nvfp4_oracle as O  # noqa: E402
 
-# (M, N, K, seed, a_scale, w_scale, sampled rows)
+# (M, N, K, seed, a_scale, w_scale, sampled rows); the last two are the
+# benchmark's decode (C2) and mid (C3) shapes, both in the reference's
+# dispatch table (nvfp4_dual_gemm.cu:404-406, 413-415; C3's output is
+# column-major there and is read back in row-major order)
 CASES = [
     (512, 768, 7168, 11, 1.0, 1.0, 8),
     (256, 3072, 4096, 12, 1.0, 1.0, 8),
     (512, 768, 7168, 14, 0.5, 0.02, 8),
+    (256, 4096, 7168, 21, 1.0, 1.0, 64),
+    (512, 3072, 7168, 22, 1.0, 1.0, 64),
 ]
 
 
@@ -62,7 +67,11 @@ def main() -> None:
     ref = build_ref.load()
     if ref is None:
         raise SystemExit("reference module not built (oracle/_ref)")
+    # optional filter: shapes as MxNxK (default: every case)
+    only = set(sys.argv[1:])
     for (m, n, k, seed, a_s, w_s, nrows) in CASES:
+        if only and f"{m}x{n}x{k}" not in only:
+            continue
         assert (m, n, k) in build_ref.SAFE_SHAPES
         p = O.make_problem(m, n, k, seed=seed, a_scale=a_s, w_scale=w_s)
         d = to_device(p)

@@ -4,7 +4,8 @@ GPU, this library) to the reference's outputs.
 The fixtures under tests/golden/ were produced by tests/golden/make_golden.py
 on a B200: seeded inputs from oracle.make_problem, the output of the
 reference's compiled ``cuda_nvfp4_dual_gemm`` (nvfp4_dual_gemm.cu:381-446).
-Each keeps 8 sampled output rows, the SHA-256 of the inputs and of the full
+Each keeps 8 (64 for the benchmark's C2 / C3 shapes) sampled output rows,
+the SHA-256 of the inputs and of the full
 output, and how many of all outputs fell outside rtol = atol = 1e-3 of the
 oracle.  The reference runs some dispatch shapes with an approximate SiLU
 (FAST_SILU, selected at nvfp4_dual_gemm.cu:131-133 and dispatched at :405 and :411), which leaves a few outputs
@@ -53,7 +54,9 @@ def allowed_mismatches(z, sampled):
 
 def test_fixtures_present():
     names = [os.path.basename(f) for f in FIXTURES]
-    assert len(names) >= 3, names
+    assert len(names) >= 5, names
+    assert "ref_256x4096x7168_s21.npz" in names  # C2
+    assert "ref_512x3072x7168_s22.npz" in names  # C3
 
 
 @pytest.mark.parametrize("path", FIXTURES, ids=os.path.basename)

@@ -38,6 +38,8 @@ def _noalloc(d, m, n, k, flags):
     # tiles split along K, so the static scratch is used
     5 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN64 | _lib.FLAG_NO_PAIR,
     6 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN128 | _lib.FLAG_PAIR,
+    # the largest forced stream-K grid whose partials still fit the array
+    31 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN64 | _lib.FLAG_NO_PAIR,
     # the automatic schedule (no scratch needed for this shape)
     0,
 ])
@@ -65,7 +67,57 @@ def test_noalloc_matches_run_twice(flags):
         assert_close(got, want, f"no-allocation call {call + 1}")
 
 
+def _ordinary(d, flags=0):
+    dg.dual_gemm(d["a"], d["b1"], d["b2"], d["sfa_blocked"],
+                 d["sfb1_blocked"], d["sfb2_blocked"], d["c"],
+                 flags=flags | _lib.FLAG_SYNC_CHECK)
+    torch.cuda.synchronize()
+    return d["c"].cpu().numpy()
+
+
+def test_noalloc_falls_back_to_whole_tiles_when_stream_k_does_not_fit():
+    # the automatic schedule of this shape is stream-K over a full grid,
+    # whose partials (~39 MB) exceed the array: the call runs whole tiles
+    m, n, k = 512, 5120, 4096
+    auto = dg.plan(m, n, k)
+    assert auto["sk_tiles"] > 0
+    assert dg.workspace_size(m, n, k) > _lib.NOALLOC_SCRATCH_BYTES
+    p = O.make_problem(m, n, k, seed=33)
+    d = to_device(p)
+    want = _ordinary(d)
+    for call in range(2):
+        d["c"].fill_(float("nan"))
+        rc = _noalloc(d, m, n, k, 0)
+        assert rc == _lib.OK, _lib.last_error()
+        torch.cuda.synchronize()
+        assert_close(d["c"].cpu().numpy(), want,
+                     f"no-allocation call {call + 1} (whole tiles)")
+
+
+def test_noalloc_calls_with_different_shapes_in_a_row():
+    # the second call finds the first one's partials and counters at other
+    # offsets of the array
+    cases = [
+        (256, 512, 2048, 5 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN64 |
+         _lib.FLAG_NO_PAIR, 41),
+        (384, 768, 2048, 6 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN128 |
+         _lib.FLAG_PAIR, 42),
+        (256, 512, 2048, 31 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN64 |
+         _lib.FLAG_NO_PAIR, 43),
+    ]
+    for m, n, k, flags, seed in cases:
+        assert dg.plan(m, n, k, flags)["sk_tiles"] > 0
+        d = to_device(O.make_problem(m, n, k, seed=seed))
+        want = _ordinary(d, flags)
+        d["c"].fill_(float("nan"))
+        rc = _noalloc(d, m, n, k, flags)
+        assert rc == _lib.OK, _lib.last_error()
+        torch.cuda.synchronize()
+        assert_close(d["c"].cpu().numpy(), want, f"{m}x{n}x{k}")
+
+
 def test_noalloc_rejects_schedules_beyond_the_static_scratch():
+    # a stream-K schedule forced by the caller is not replaced
     m, n, k = 256, 4096, 7168
     flags = 148 | _lib.FLAG_FORCE_STREAMK | _lib.FLAG_BN128 | _lib.FLAG_NO_PAIR
     assert dg.workspace_size(m, n, k, flags) > _lib.NOALLOC_SCRATCH_BYTES
