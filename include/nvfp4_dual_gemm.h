@@ -102,6 +102,11 @@ extern "C" {
                                               copy brings both when B2 lies
                                               above B1 at a multiple of 16
                                               bytes)                          */
+#define NVFP4DG_FLAG_NO_TMA_STORE (1u << 26) /* whole 2-SM pair tiles of
+                                              128 columns store their fp16 C
+                                              row by row from each thread
+                                              instead of staging it in shared
+                                              memory for TMA tensor stores */
 #define NVFP4DG_FLAG_TEST_SK_TIMEOUT (1u << 25) /* test hook, never for
                                               production: the owner of each
                                               tile split along K (stream-K)

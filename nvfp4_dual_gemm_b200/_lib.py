@@ -37,6 +37,7 @@ FLAG_NO_PDL = 1 << 22
 FLAG_NO_MERGED_B = 1 << 23
 FLAG_STATIC_WEIGHTS = 1 << 24
 FLAG_TEST_SK_TIMEOUT = 1 << 25
+FLAG_NO_TMA_STORE = 1 << 26
 
 # Input element types of nvfp4_quantize_rows.
 DTYPE_F32 = 0

@@ -39,6 +39,7 @@ constexpr int kBM = 128;            // tile rows (TMEM lanes)
 constexpr int kRowBytes = 128;      // one stage = 256 fp4 of K = 128 bytes/row
 constexpr int kSfAtomBytes = 512;   // 128 rows x 4 scales
 constexpr int kSfRunBytes = 2048;   // 4 atoms = the scales of 256 K elements
+constexpr int kCBoxBytes = 16384;   // fp16 C store box: 128 rows x 64 columns
 constexpr int kThreads = 352;
 constexpr int kTmemCols = 512;
 constexpr int kSfTmemBase = 256;    // scale regions follow the accumulator
@@ -120,6 +121,12 @@ struct KParams {
   // NVFP4DG_FLAG_TEST_SK_TIMEOUT, to make that bounded wait run out)
   int sk_extra;
   long long sk_wait_limit;
+  // pair kernel, BN = 128, fp16 C of ungrouped problems (unless
+  // NVFP4DG_FLAG_NO_TMA_STORE): whole tiles stage their fp16 outputs in
+  // shared memory and store them with TMA through the C tensor map (3-D,
+  // the batch as third coordinate, when c_layers > 1)
+  int c_tma;
+  int c_layers;
   GroupTable groups;
 };
 
@@ -203,8 +210,107 @@ __device__ __forceinline__ bool group_all(bool pred) {
   return out != 0;
 }
 
-__device__ __forceinline__ float silu_mul(float x, float y) {
-  return __fdividef(x, 1.0f + __expf(-x)) * y;
+// Start-up barrier initialisation by one warp, one barrier per lane (an
+// mbarrier.init is a shared-memory store: 32 lanes do 32 of them in one
+// instruction, where one thread would do them one after another): lanes
+// [0, S) take full[s], [S, 2S) sfdata[s], [2S, 3S) empty[s], then acc_full,
+// acc_empty, drain, ready, the four stream-K fixup barriers and the NRECV
+// split-K receive barriers.  Each lane fences its own initialisation; lanes
+// [0, S) then arm the first fill of their stage's scale barrier with
+// `sf_bytes`.
+template <int S, int NRECV>
+__device__ __forceinline__ void init_barriers_by_lane(
+    int lane, uint64_t* full, uint32_t full_count, uint64_t* sfdata,
+    uint64_t* empty, uint64_t* acc_full, uint64_t* acc_empty,
+    uint32_t acc_empty_count, uint64_t* drain, uint64_t* ready,
+    uint64_t* fix, uint64_t* recv, uint32_t sf_bytes) {
+  static_assert(3 * S + 4 + 4 + NRECV <= 32, "one barrier per lane");
+  uint64_t* bar = nullptr;
+  uint32_t count = 1;
+  if (lane < S) {
+    bar = full + lane;
+    count = full_count;
+  } else if (lane < 2 * S) {
+    bar = sfdata + (lane - S);
+  } else if (lane < 3 * S) {
+    bar = empty + (lane - 2 * S);
+  } else if (lane == 3 * S) {
+    bar = acc_full;
+  } else if (lane == 3 * S + 1) {
+    bar = acc_empty;
+    count = acc_empty_count;
+  } else if (lane == 3 * S + 2) {
+    bar = drain;
+  } else if (lane == 3 * S + 3) {
+    bar = ready;
+  } else if (lane < 3 * S + 4 + 4) {
+    bar = fix + (lane - (3 * S + 4));
+  } else if (lane < 3 * S + 8 + NRECV) {
+    bar = recv + (lane - (3 * S + 8));
+  }
+  if (bar != nullptr) {
+    mbar_init(bar, count);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  // arm the first scale fill of every stage (bytes may land before or after
+  // an arming: a barrier's transaction count may go negative meanwhile)
+  if (lane < S) mbar_arrive_expect_tx(sfdata + lane, sf_bytes);
+  fence_proxy_async_smem();
+}
+
+// silu(x) * y = x * y / (1 + e^-x) for two columns, rounded to fp16 and
+// packed (x0 / y0 in the low half).  One special-function (MUFU) operation
+// per output: e = 2^(-x log2 e) with ex2.approx; the reciprocal of
+// d = 1 + e is computed on the FMA pipe, two outputs per instruction
+// (fma.rn.f32x2), by three Newton-Raphson steps r <- r + r (1 - d r) from a
+// first guess read off the bits of d (the integer 0x7EF311C3 - bits(d)
+// approximates 1/d within 11 % for every positive normal d; here formed from
+// -d as 0xFEF311C3 - bits(-d)).  The error is quadratic per step, so after
+// three steps the reciprocal is exact to fp32 rounding; the result's
+// relative error stays below 4e-6 (from rounding x log2 e, as with any
+// exp2-based exp) against the 1e-3 tolerance of the fp16 output.  With
+// __expf and __fdividef (two MUFU operations per output) the epilogue was
+// bound by the SM's 16 MUFU results per cycle.  The exponent is clamped at
+// 126 so that d stays finite: silu(x) for x < -87 is below fp16's range
+// either way.
+__device__ __forceinline__ uint32_t silu_mul_h2(float x0, float x1, float y0,
+                                                float y1) {
+  uint32_t h;
+  asm("{\n\t"
+      ".reg .b64 X, Y, T, ND, R, E, ONE, NL2E;\n\t"
+      ".reg .b32 t0, t1, e0, e1, n0, n1, r0, r1;\n\t"
+      "mov.b64 X, {%1, %2};\n\t"
+      "mov.b64 Y, {%3, %4};\n\t"
+      "mov.b64 NL2E, {0xBFB8AA3B, 0xBFB8AA3B};\n\t"  // -log2(e)
+      "mov.b64 ONE, {0x3F800000, 0x3F800000};\n\t"
+      "mul.rn.f32x2 T, X, NL2E;\n\t"
+      "mov.b64 {t0, t1}, T;\n\t"
+      "min.f32 t0, t0, 0f42FC0000;\n\t"  // 126
+      "min.f32 t1, t1, 0f42FC0000;\n\t"
+      "ex2.approx.ftz.f32 e0, t0;\n\t"
+      "ex2.approx.ftz.f32 e1, t1;\n\t"
+      "sub.rn.f32 n0, 0fBF800000, e0;\n\t"  // -d = -(1 + e)
+      "sub.rn.f32 n1, 0fBF800000, e1;\n\t"
+      "sub.u32 r0, 0xFEF311C3, n0;\n\t"     // first guess of 1/d
+      "sub.u32 r1, 0xFEF311C3, n1;\n\t"
+      "mov.b64 ND, {n0, n1};\n\t"
+      "mov.b64 R, {r0, r1};\n\t"
+      "fma.rn.f32x2 E, ND, R, ONE;\n\t"
+      "fma.rn.f32x2 R, R, E, R;\n\t"
+      "fma.rn.f32x2 E, ND, R, ONE;\n\t"
+      "fma.rn.f32x2 R, R, E, R;\n\t"
+      "fma.rn.f32x2 E, ND, R, ONE;\n\t"
+      "fma.rn.f32x2 R, R, E, R;\n\t"
+      "mul.rn.f32x2 T, X, Y;\n\t"
+      "mul.rn.f32x2 T, T, R;\n\t"
+      "mov.b64 {r0, r1}, T;\n\t"
+      "cvt.rn.f16x2.f32 %0, r1, r0;\n\t"
+      "}"
+      : "=r"(h)
+      : "r"(__float_as_uint(x0)), "r"(__float_as_uint(x1)),
+        "r"(__float_as_uint(y0)), "r"(__float_as_uint(y1)));
+  return h;
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
@@ -371,14 +477,14 @@ __device__ __forceinline__ void store_row16(__half* dst, const float (&x)[16],
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
     uint4 v;
-    v.x = pack_half2(silu_mul(x[8 * q + 0], y[8 * q + 0]),
-                     silu_mul(x[8 * q + 1], y[8 * q + 1]));
-    v.y = pack_half2(silu_mul(x[8 * q + 2], y[8 * q + 2]),
-                     silu_mul(x[8 * q + 3], y[8 * q + 3]));
-    v.z = pack_half2(silu_mul(x[8 * q + 4], y[8 * q + 4]),
-                     silu_mul(x[8 * q + 5], y[8 * q + 5]));
-    v.w = pack_half2(silu_mul(x[8 * q + 6], y[8 * q + 6]),
-                     silu_mul(x[8 * q + 7], y[8 * q + 7]));
+    v.x = silu_mul_h2(x[8 * q + 0], x[8 * q + 1], y[8 * q + 0],
+                      y[8 * q + 1]);
+    v.y = silu_mul_h2(x[8 * q + 2], x[8 * q + 3], y[8 * q + 2],
+                      y[8 * q + 3]);
+    v.z = silu_mul_h2(x[8 * q + 4], x[8 * q + 5], y[8 * q + 4],
+                      y[8 * q + 5]);
+    v.w = silu_mul_h2(x[8 * q + 6], x[8 * q + 7], y[8 * q + 6],
+                      y[8 * q + 7]);
     d[q] = v;
   }
 }
@@ -389,14 +495,14 @@ __device__ __forceinline__ void store_row32(__half* dst, const float (&x)[32],
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     uint4 v;
-    v.x = pack_half2(silu_mul(x[8 * q + 0], y[8 * q + 0]),
-                     silu_mul(x[8 * q + 1], y[8 * q + 1]));
-    v.y = pack_half2(silu_mul(x[8 * q + 2], y[8 * q + 2]),
-                     silu_mul(x[8 * q + 3], y[8 * q + 3]));
-    v.z = pack_half2(silu_mul(x[8 * q + 4], y[8 * q + 4]),
-                     silu_mul(x[8 * q + 5], y[8 * q + 5]));
-    v.w = pack_half2(silu_mul(x[8 * q + 6], y[8 * q + 6]),
-                     silu_mul(x[8 * q + 7], y[8 * q + 7]));
+    v.x = silu_mul_h2(x[8 * q + 0], x[8 * q + 1], y[8 * q + 0],
+                      y[8 * q + 1]);
+    v.y = silu_mul_h2(x[8 * q + 2], x[8 * q + 3], y[8 * q + 2],
+                      y[8 * q + 3]);
+    v.z = silu_mul_h2(x[8 * q + 4], x[8 * q + 5], y[8 * q + 4],
+                      y[8 * q + 5]);
+    v.w = silu_mul_h2(x[8 * q + 6], x[8 * q + 7], y[8 * q + 6],
+                      y[8 * q + 7]);
     d[q] = v;
   }
 }
@@ -460,21 +566,36 @@ __device__ __forceinline__ OutRow out_row(const KParams& p, const TileLoc& t,
   return o;
 }
 
-// NVFP4 output of tile columns [cc, cc + 16) of one row: fp16(silu(x) * y)
-// quantised as one block.
-__device__ __forceinline__ void quant_store16(const OutRow& o, int cc,
-                                              const float* x,
-                                              const float* y) {
-  uint32_t h[8];  // the fp16 values the fp16 output would hold, in pairs
-#pragma unroll
-  for (int i = 0; i < 8; ++i)
-    h[i] = pack_half2(silu_mul(x[2 * i], y[2 * i]),
-                      silu_mul(x[2 * i + 1], y[2 * i + 1]));
+// NVFP4 output of 16 consecutive columns of one row, given the fp16 values
+// the fp16 output would hold (h, in pairs): quantised as one block, 8 bytes
+// of codes at q and the e4m3 scale of column `col` of the row's blocked
+// scales at sf.  Not inlined, and given its data by value: the epilogues,
+// which serve the fp16 and the NVFP4 output, then carry one call instead of
+// a copy of the quantiser at every output site (less code for the
+// instruction cache) and keep their values in registers.
+__device__ __noinline__ void quant_store16(uint8_t* q, uint8_t* sf, int col,
+                                          bool row_ok, bool sf_ok,
+                                          uint32_t h0, uint32_t h1,
+                                          uint32_t h2, uint32_t h3,
+                                          uint32_t h4, uint32_t h5,
+                                          uint32_t h6, uint32_t h7) {
+  const uint32_t h[8] = {h0, h1, h2, h3, h4, h5, h6, h7};
   uint32_t w0, w1;
   const uint8_t sb = quant_block16_x2<__half2>(h, w0, w1);
-  const int col = o.col0 + cc;
-  if (o.row_ok) *reinterpret_cast<uint2*>(o.q + cc / 2) = make_uint2(w0, w1);
-  if (o.sf_ok) o.sf[(col / 64) * kSfAtomBytes + (col / 16) % 4] = sb;
+  if (row_ok) *reinterpret_cast<uint2*>(q) = make_uint2(w0, w1);
+  if (sf_ok) sf[(col / 64) * kSfAtomBytes + (col / 16) % 4] = sb;
+}
+
+// NVFP4 output of tile columns [cc, cc + 16) of one row: fp16(silu(x) * y)
+// quantised as one block.
+__device__ __forceinline__ void quant_emit16(const OutRow& o, int cc,
+                                             const float* x, const float* y) {
+  uint32_t h[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    h[i] = silu_mul_h2(x[2 * i], x[2 * i + 1], y[2 * i], y[2 * i + 1]);
+  quant_store16(o.q + cc / 2, o.sf, o.col0 + cc, o.row_ok, o.sf_ok, h[0],
+                h[1], h[2], h[3], h[4], h[5], h[6], h[7]);
 }
 
 // Outputs of tile columns [cc, cc + 16) / [cc, cc + 32) of one row.
@@ -484,7 +605,7 @@ __device__ __forceinline__ void emit16(const OutRow& o, int cc,
   if (o.q == nullptr) {
     if (o.row_ok) store_row16(o.c + cc, x, y);
   } else {
-    quant_store16(o, cc, x, y);
+    quant_emit16(o, cc, x, y);
   }
 }
 
@@ -494,8 +615,97 @@ __device__ __forceinline__ void emit32(const OutRow& o, int cc,
   if (o.q == nullptr) {
     if (o.row_ok) store_row32(o.c + cc, x, y);
   } else {
-    quant_store16(o, cc, x, y);
-    quant_store16(o, cc + 16, x + 16, y + 16);
+    quant_emit16(o, cc, x, y);
+    quant_emit16(o, cc + 16, x + 16, y + 16);
+  }
+}
+
+// fp16(silu(x) * y) of 32 columns of one row into a C store box, whose
+// rows are 128 bytes in the 128-byte-swizzled layout of the C tensor map:
+// 16-byte chunk j of box row r sits at chunk j ^ (r % 8), so the 32 rows of
+// a warp write all banks.  `j0` is the first chunk (4 per 32 columns).
+__device__ __forceinline__ void stage_row32(uint8_t* row_base, int r, int j0,
+                                            const float (&x)[32],
+                                            const float (&y)[32]) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 v;
+    v.x = silu_mul_h2(x[8 * q + 0], x[8 * q + 1], y[8 * q + 0],
+                      y[8 * q + 1]);
+    v.y = silu_mul_h2(x[8 * q + 2], x[8 * q + 3], y[8 * q + 2],
+                      y[8 * q + 3]);
+    v.z = silu_mul_h2(x[8 * q + 4], x[8 * q + 5], y[8 * q + 4],
+                      y[8 * q + 5]);
+    v.w = silu_mul_h2(x[8 * q + 6], x[8 * q + 7], y[8 * q + 6],
+                      y[8 * q + 7]);
+    sts128(smem_u32(row_base + (((j0 + q) ^ (r & 7)) << 4)), v);
+  }
+}
+
+// Where a whole tile's fp16 outputs go when they are stored with TMA.
+struct CStore {
+  uint8_t* box;  // box 0 (columns [0, 64)); box 1 follows (BN = 128)
+  bool store;    // this CTA's 128 rows start below the problem's rows
+  int x, y, z;   // byte column, row and batch of box 0 in the C map
+};
+
+// Epilogue of a whole tile in the 2-SM pair kernel, run by the four
+// epilogue warps (thread = row), in phases of 64 columns of both GEMMs: a
+// phase's four TMEM loads (128 registers) are issued before one wait, and
+// the accumulator is released (on the even CTA's acc_empty barrier, cluster
+// address `acc_empty_c`) as soon as the last phase's loads have completed.
+// A TMEM load round trip costs ~500 cycles, far more than the math of 16
+// columns, so the epilogue's length is set by the number of load waits:
+// two here (BN = 128), against eight with 16-column chunks; and the next
+// tile's MMAs wait for one phase of math only.  With `cs` (fp16 C) a
+// phase's outputs go into its C store box and thread 0 stores the box with
+// TMA once the four warps have written it (after the box's previous store
+// has read it): a warp then writes shared memory 512 bytes per instruction
+// where its row stores to global memory touched 32 rows at 16 bytes each,
+// and the store engine writes whole lines.  Otherwise each thread stores
+// its row.
+template <int BN, bool TMA, typename Release>
+__device__ __forceinline__ void tile_epilogue(uint32_t t_row, const OutRow& out,
+                                              int row, Release release,
+                                              const CStore& cs,
+                                              const CUtensorMap* tmC,
+                                              int c_layers) {
+  constexpr int kPhases = BN / 64;
+  if (TMA) {
+    if (threadIdx.x == 0) bulk_wait_group_read0();
+    epi_bar();
+  }
+#pragma unroll 1
+  for (int ph = 0; ph < kPhases; ++ph) {
+    float x0[32], x1[32], y0[32], y1[32];
+    __syncwarp();
+    tc_ld_32cols(t_row + 64 * ph, x0);
+    tc_ld_32cols(t_row + 64 * ph + 32, x1);
+    tc_ld_32cols(t_row + BN + 64 * ph, y0);
+    tc_ld_32cols(t_row + BN + 64 * ph + 32, y1);
+    tc_wait_ld();
+    tie32(x0);
+    tie32(x1);
+    tie32(y0);
+    tie32(y1);
+    if (ph == kPhases - 1) release();
+    if (!TMA) {
+      emit32(out, 64 * ph, x0, y0);
+      emit32(out, 64 * ph + 32, x1, y1);
+      continue;
+    }
+    uint8_t* box = cs.box + ph * kCBoxBytes;
+    stage_row32(box + row * 128, row, 0, x0, y0);
+    stage_row32(box + row * 128, row, 4, x1, y1);
+    fence_proxy_async_smem();  // the generic writes, before the TMA read
+    epi_bar();
+    if (threadIdx.x == 0 && cs.store) {
+      if (c_layers > 1)
+        tma_store_3d(tmC, box, cs.x + 128 * ph, cs.y, cs.z);
+      else
+        tma_store_2d(tmC, box, cs.x + 128 * ph, cs.y);
+      bulk_commit_group();
+    }
   }
 }
 
@@ -551,6 +761,7 @@ static_assert(kThreads == 32 * (kSfWarp0 + kSfWarps), "thread count");
 // the accumulator after its last TMEM load.  Partials are added in
 // contributor order, so the result does not depend on timing.
 constexpr int kFixSlots = 4;
+static_assert(kFixSlots == 4, "init_barriers_by_lane gives 4 lanes to them");
 constexpr uint32_t kFixItemBytes = 32768;
 
 template <int BN, typename SlotPtr, typename ArriveEmpty>
@@ -697,15 +908,12 @@ __device__ __forceinline__ void split_epilogue(
       mbar_arrive_expect_tx(&recv_bar[c], kChunkBytes);
     mbar_arrive_cluster(mapa_shared(smem_u32(ready_bar), xpeer));
   }
-  ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
-  if (!split_group_all(ok)) return;
-  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 41);
-  const uint32_t xbuf = smem_u32(smem);
-  const uint32_t xdst = mapa_shared(xbuf, xpeer);
-  // This warp's chunks j = part, part + 2 (at most two): all TMEM loads are
-  // issued before one wait, then the stores go out.
+  // This warp's chunks j = part, part + 2 (at most two): every TMEM load —
+  // the peer's columns (`v`, sent) and this CTA's own (`ox`, `oy`, kept) —
+  // is issued before one wait, which overlaps the wait for the peer.
   constexpr int kMine = (kHalfChunks + 1) / 2;
   float v[kMine][2][16];
+  float ox[kMine][16], oy[kMine][16];
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
     const int c = part + 2 * i;
@@ -715,9 +923,16 @@ __device__ __forceinline__ void split_epilogue(
         tc_ld_16cols(t_row + static_cast<uint32_t>(xy * BN + other * kHalf +
                                                    16 * c),
                      v[i][xy]);
+      tc_ld_16cols(t_row + own * kHalf + 16 * c, ox[i]);
+      tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, oy[i]);
     }
   }
   tc_wait_ld();
+  ok = mbar_wait(ready_bar, 0, p.err, kErrEpilogue);
+  if (!split_group_all(ok)) return;
+  if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 41);
+  const uint32_t xbuf = smem_u32(smem);
+  const uint32_t xdst = mapa_shared(xbuf, xpeer);
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
     const int c = part + 2 * i;
@@ -737,18 +952,7 @@ __device__ __forceinline__ void split_epilogue(
   }
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 42);
   bool all_ok = true;
-  // Own chunks: both TMEM reads before one wait, then each chunk as soon as
-  // the peer's partials of it have landed.
-  float ox[kMine][16], oy[kMine][16];
-#pragma unroll
-  for (int i = 0; i < kMine; ++i) {
-    const int c = part + 2 * i;
-    if (c < kHalfChunks) {
-      tc_ld_16cols(t_row + own * kHalf + 16 * c, ox[i]);
-      tc_ld_16cols(t_row + BN + own * kHalf + 16 * c, oy[i]);
-    }
-  }
-  tc_wait_ld();
+  // Own chunks: each as soon as the peer's partials of it have landed.
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(8, 43);
 #pragma unroll
   for (int i = 0; i < kMine; ++i) {
@@ -784,6 +988,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB1,
                      const __grid_constant__ CUtensorMap tmB2,
+                     const __grid_constant__ CUtensorMap tmC,
                      const __grid_constant__ KParams p) {
   using Cf = Cfg<BN>;
   constexpr int S = Cf::kStages;
@@ -817,29 +1022,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
   // Warp 0 (an epilogue warp, idle until the first tile is computed)
   // initialises the mbarriers while the producers work out their first item.
-  if (warp == 0 && lane == 0) {
-    for (int s = 0; s < S; ++s) {
-      // the scale warps; the first one's arrival carries the tiles' bytes
-      mbar_init(&full_bar[s], kSfWarps);
-      mbar_init(&sfdata_bar[s], 1);        // one arming arrival
-      mbar_init(&empty_bar[s], 1);         // tcgen05.commit of the MMAs
-    }
-    mbar_init(&acc_full_bar, 1);
-    mbar_init(&acc_empty_bar, 32 * kEpiWarps);
-    mbar_init(&drain_bar, 1);
-    mbar_init(&ready_bar, 1);
-    for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
-    for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
-    fence_mbar_init();
-    // arm the first scale fill of every stage (bytes may land before or
-    // after an arming: a barrier's transaction count may go negative
-    // meanwhile)
-    for (int s = 0; s < S; ++s)
-      mbar_arrive_expect_tx(&sfdata_bar[s], kBytesSf);
-    fence_proxy_async_smem();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB1);
-    prefetch_tmap(&tmB2);
+  if (warp == 0) {
+    // full: the scale warps, the first one's arrival carrying the tiles'
+    // bytes; sfdata: one arming arrival; empty: the MMAs' tcgen05.commit
+    init_barriers_by_lane<S, BN / 32>(
+        lane, full_bar, kSfWarps, sfdata_bar, empty_bar, &acc_full_bar,
+        &acc_empty_bar, 32 * kEpiWarps, &drain_bar, &ready_bar, fix_bar,
+        recv_bar, kBytesSf);
+    if (lane == 0) prefetch_tmap(&tmA);
+    if (lane == 1) prefetch_tmap(&tmB1);
+    if (lane == 2) prefetch_tmap(&tmB2);
   }
   // Split-K clusters: every thread arrives on the cluster barrier once the
   // barriers are initialised; the epilogue waits on it before its first
@@ -1190,6 +1382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_ld_32cols(t_row + 32 * c, x);
           tc_ld_32cols(t_row + BN + 32 * c, y);
           tc_wait_ld();
+          tie32(x);
+          tie32(y);
           if (c == BN / 32 - 1) {
             tc_fence_before();
             mbar_arrive(&acc_empty_bar);
@@ -1292,7 +1486,11 @@ struct PairCfg {
   static constexpr int kABytes = kBM * kRowBytes;  // this CTA's A rows
   static constexpr int kBBytes = BN * kRowBytes;   // this CTA's B half
   static constexpr int kStageBytes = kABytes + kBBytes + 3 * kSfRunBytes;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  // BN = 128: this CTA's fp16 C tile (128 rows x 128 columns) staged for
+  // the TMA store, two 16 KiB boxes of 64 columns, after the stages
+  static constexpr int kCStageBytes = (BN == 128) ? 2 * kCBoxBytes : 0;
+  static constexpr int kSmemBytes =
+      kStages * kStageBytes + kCStageBytes + 1024;
   static constexpr int kSfBase = 2 * BN;  // scale regions follow the acc.
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-B aligned");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
@@ -1307,6 +1505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     dual_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                           const __grid_constant__ CUtensorMap tmB1,
                           const __grid_constant__ CUtensorMap tmB2,
+                          const __grid_constant__ CUtensorMap tmC,
                           const __grid_constant__ KParams p) {
   using Cf = PairCfg<BN>;
   constexpr int S = Cf::kStages;
@@ -1352,29 +1551,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
   // Warp 0 initialises the mbarriers while the producers work out their
   // first item (as in the 1-SM kernel).
-  if (warp == 0 && lane == 0) {
-    for (int s = 0; s < S; ++s) {
-      // the scale warps of both CTAs; on the even CTA the first one's
-      // arrival carries both CTAs' tile bytes
-      mbar_init(&full_bar[s], 2 * kSfWarps);
-      mbar_init(&sfdata_bar[s], 1);         // one arming arrival
-      // even CTA: the MMA commit; odd CTA: the even producer A's forward
-      mbar_init(&empty_bar[s], 1);
-    }
-    mbar_init(&acc_full_bar, 1);
-    mbar_init(&acc_empty_bar, 2 * kEpiWarps);
-    mbar_init(&drain_bar, 1);
-    for (int i = 0; i < kFixSlots; ++i) mbar_init(&fix_bar[i], 1);
-    mbar_init(&ready_bar, 1);
-    for (int c = 0; c < BN / 32; ++c) mbar_init(&recv_bar[c], 1);
-    fence_mbar_init();
-    NVFP4DG_STAMP(9, 56);
-    // arm the first scale fill of every stage
-    for (int s = 0; s < S; ++s)
-      mbar_arrive_expect_tx(&sfdata_bar[s], 3 * kSfRunBytes);
-    fence_proxy_async_smem();
-    prefetch_tmap(&tmA);
-    prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
+  if (warp == 0) {
+    // full: the scale warps of both CTAs, on the even CTA the first one's
+    // arrival carrying both CTAs' tile bytes; sfdata: one arming arrival;
+    // empty: the MMA commit (even CTA) or the even producer A's forward
+    init_barriers_by_lane<S, BN / 32>(
+        lane, full_bar, 2 * kSfWarps, sfdata_bar, empty_bar, &acc_full_bar,
+        &acc_empty_bar, 2 * kEpiWarps, &drain_bar, &ready_bar, fix_bar,
+        recv_bar, 3 * kSfRunBytes);
+    if (lane == 0) NVFP4DG_STAMP(9, 56);
+    if (lane == 0) prefetch_tmap(&tmA);
+    if (lane == 1) prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
+    if (lane == 2 && p.c_tma) prefetch_tmap(&tmC);
   }
   // Every CTA's barriers initialised (published by the mbarrier-init fence)
   // before any remote use: arrive now, wait after the TMEM allocation, so
@@ -1704,6 +1892,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = threadIdx.x;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), lead);
+    // the accumulator may be overwritten: one arrival per warp on the even
+    // CTA's barrier
+    auto release_acc = [&] {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+    };
     uint32_t acc_phase = 0;
     int unit_i = 0;
     WorkIter it;
@@ -1719,26 +1914,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const TileLoc loc = locate(p, w.tile);
       const int n_tile = loc.n_tile;
-      const int grow =
-          loc.m_tile * 2 * kBM + static_cast<int>(rank) * kBM + row;
-      const OutRow out = out_row(p, loc, grow, n_tile * BN);
-      if (w.slot < 0) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float x[32], y[32];
-          __syncwarp();
-          tc_ld_32cols(t_row + 32 * c, x);
-          tc_ld_32cols(t_row + BN + 32 * c, y);
-          tc_wait_ld();
-          if (c == BN / 32 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(acc_empty_c);
-            if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
-          }
-          emit32(out, 32 * c, x, y);
-        }
+      const int r0 = loc.m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+      if (w.slot < 0 && p.c_tma) {
+        // (only what this path needs is live across the epilogue: registers
+        // are tight with a phase's 128 values)
+        CStore cs;
+        cs.box = smem + S * Cf::kStageBytes;
+        cs.store = r0 < loc.rows;
+        cs.x = n_tile * BN * 2;
+        cs.y = r0;
+        cs.z = loc.l;
+        tile_epilogue<BN, true>(t_row, OutRow{}, row, release_acc, cs, &tmC,
+                                p.c_layers);
+        if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
+      } else if (w.slot < 0) {
+        const OutRow out = out_row(p, loc, r0 + row, n_tile * BN);
+        tile_epilogue<BN, false>(t_row, out, row, release_acc, CStore{},
+                                 &tmC, p.c_layers);
+        if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
       } else {
+        const OutRow out = out_row(p, loc, r0 + row, n_tile * BN);
         // Stream-K tile shared by units b_first..b_last: as in the 1-SM
         // kernel, unit b_first (for which these are its last K blocks) adds
         // the others' partials to its accumulator; each CTA of a pair deals
@@ -1800,6 +1995,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ------------------------------------------------------------ teardown
+  // the C stores must have read their boxes before shared memory goes away
+  if (p.c_tma && threadIdx.x == 0) bulk_wait_group0();
   tc_fence_before();
   cluster_sync();  // no CTA leaves while its peer may still signal it
   if (warp == kMmaWarp) {
@@ -2449,7 +2646,8 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
     attr = true;
   }
-  CUtensorMap ta, tb1, tb2;
+  CUtensorMap ta, tb1, tb2, tc;
+  std::memset(&tc, 0, sizeof(tc));
   int rc;
   // The pair kernel copies with 2-D maps; the 1-SM kernel with 3-D ones,
   // both weight tiles of a K block in one copy when a single map can cover
@@ -2496,6 +2694,18 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   kp.b_merged = merged ? 1 : 0;
   kp.static_weights = (flags & NVFP4DG_FLAG_STATIC_WEIGHTS) ? 1 : 0;
   kp.maps3d = maps3d ? 1 : 0;
+  // fp16 C through TMA stores (pair kernel, BN = 128, not grouped, unless
+  // NVFP4DG_FLAG_NO_TMA_STORE): a byte view of C, rows of 2N bytes,
+  // 128-byte x 128-row boxes (64 columns)
+  kp.c_tma = 0;
+  kp.c_layers = plan.L;
+  if (PAIR && BN == 128 && C != nullptr && groups == nullptr &&
+      !(flags & NVFP4DG_FLAG_NO_TMA_STORE)) {
+    if ((rc = tensor_map(C, M, 2ll * N, kBM, devid, &tc,
+                         plan.L > 1 ? 3 : 2, plan.L)))
+      return rc;
+    kp.c_tma = 1;
+  }
   const bool expire = (flags & NVFP4DG_FLAG_TEST_SK_TIMEOUT) != 0;
   kp.sk_extra = expire ? 1 : 0;
   kp.sk_wait_limit = expire ? kTestWaitLimitCycles : kWaitLimitCycles;
@@ -2531,7 +2741,7 @@ int launch(const Plan& plan, DevInfo& dev, int devid, const void* A,
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb1, tb2, kp);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ta, tb1, tb2, tc, kp);
   if (e != cudaSuccess) return cuda_fail(e, "dual_gemm_kernel launch");
   return NVFP4DG_OK;
 }

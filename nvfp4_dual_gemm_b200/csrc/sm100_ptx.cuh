@@ -346,6 +346,23 @@ __device__ __forceinline__ void tc_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Marks 32 registers as written here (an empty statement), to be placed
+// right after a tcgen05.wait::ld: uses of the registers a tcgen05.ld fills
+// asynchronously are then not scheduled before the wait.
+__device__ __forceinline__ void tie32(float (&a)[32]) {
+  asm volatile(""
+               : "+f"(a[0]), "+f"(a[1]), "+f"(a[2]), "+f"(a[3]), "+f"(a[4]),
+                 "+f"(a[5]), "+f"(a[6]), "+f"(a[7]), "+f"(a[8]), "+f"(a[9]),
+                 "+f"(a[10]), "+f"(a[11]), "+f"(a[12]), "+f"(a[13]),
+                 "+f"(a[14]), "+f"(a[15]), "+f"(a[16]), "+f"(a[17]),
+                 "+f"(a[18]), "+f"(a[19]), "+f"(a[20]), "+f"(a[21]),
+                 "+f"(a[22]), "+f"(a[23]), "+f"(a[24]), "+f"(a[25]),
+                 "+f"(a[26]), "+f"(a[27]), "+f"(a[28]), "+f"(a[29]),
+                 "+f"(a[30]), "+f"(a[31])
+               :
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Thread-block clusters and the 2-SM (cta_group::2) forms
 // ---------------------------------------------------------------------------
@@ -537,6 +554,48 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
       "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 "
       "[%0];" ::"r"(bar_cluster)
       : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMA tensor stores (shared -> global), bulk async-group completion
+// ---------------------------------------------------------------------------
+// 2-D / 3-D tiled store of a box from this CTA's shared memory; the copy
+// reads shared memory asynchronously and is tracked by the issuing thread's
+// bulk async-group (commit with bulk_commit_group).  Boxes that extend past
+// the tensor's bounds are clipped.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m,
+                                             const void* src, int c0,
+                                             int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], "
+      "[%3];" ::"l"(reinterpret_cast<uint64_t>(m)),
+      "r"(c0), "r"(c1), "r"(smem_u32(src))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* m,
+                                             const void* src, int c0, int c1,
+                                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%1, %2, "
+      "%3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(m)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(src))
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until every committed bulk group of this thread has finished reading
+// its shared-memory source (the buffer may be rewritten).
+__device__ __forceinline__ void bulk_wait_group_read0() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Wait until every committed bulk group of this thread has completed.
+__device__ __forceinline__ void bulk_wait_group0() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------

@@ -489,3 +489,23 @@ def test_static_weights_back_to_back(flags):
     word = ctypes.c_uint(123)
     rc = _lib.load().nvfp4_dual_gemm_device_status(0, ctypes.byref(word))
     assert rc == 0 and word.value == 0  # no bounded wait expired
+
+
+# Whole 2-SM pair tiles of 128 columns store fp16 C through shared memory
+# and TMA by default; NVFP4DG_FLAG_NO_TMA_STORE keeps the row-by-row stores.
+# Both against the oracle, with rows past M (the store boxes are clipped by
+# the tensor map, or skipped when a CTA's rows all lie past M), several
+# tiles per CTA (the boxes reused after their previous store has read them)
+# and a forced stream-K grid (tiles split along K keep row stores).
+@pytest.mark.parametrize("m,n,k", [(256, 512, 2048), (300, 768, 1024),
+                                   (129, 256, 512), (100, 256, 512),
+                                   (1024, 1024, 1024)])
+@pytest.mark.parametrize("extra", [0, _lib.FLAG_NO_TMA_STORE, 3,
+                                   6 | _lib.FLAG_FORCE_STREAMK])
+def test_pair_tile_c_store_paths(m, n, k, extra):
+    p = O.make_problem(m, n, k, seed=61)
+    flags = _lib.FLAG_PAIR | _lib.FLAG_BN128 | _lib.FLAG_NO_SPLITK | extra
+    if not extra & _lib.FLAG_FORCE_STREAMK:
+        flags |= _lib.FLAG_NO_STREAMK
+    got = run(p, flags)
+    assert_close(got, O.reference_output(p), f"flags {flags:#x}")
