@@ -642,6 +642,21 @@ __device__ __forceinline__ void stage_row32(uint8_t* row_base, int r, int j0,
   }
 }
 
+// The same for 16 columns: 16-byte chunks j0 and j0 + 1 of the box row.
+__device__ __forceinline__ void stage_row16(uint8_t* row_base, int r, int j0,
+                                            const float (&x)[16],
+                                            const float (&y)[16]) {
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint4 v;
+    v.x = silu_mul_h2(x[8 * q + 0], x[8 * q + 1], y[8 * q + 0], y[8 * q + 1]);
+    v.y = silu_mul_h2(x[8 * q + 2], x[8 * q + 3], y[8 * q + 2], y[8 * q + 3]);
+    v.z = silu_mul_h2(x[8 * q + 4], x[8 * q + 5], y[8 * q + 4], y[8 * q + 5]);
+    v.w = silu_mul_h2(x[8 * q + 6], x[8 * q + 7], y[8 * q + 6], y[8 * q + 7]);
+    sts128(smem_u32(row_base + (((j0 + q) ^ (r & 7)) << 4)), v);
+  }
+}
+
 // Where a whole tile's fp16 outputs go when they are stored with TMA.
 struct CStore {
   uint8_t* box;  // box 0 (columns [0, 64)); box 1 follows (BN = 128)
@@ -883,7 +898,8 @@ __device__ __forceinline__ void split_epilogue(
     const KParams& p, uint8_t* smem, uint32_t tmem, uint64_t* acc_full_bar,
     uint64_t* ready_bar, uint64_t* recv_bar, int warp, int lane, int part,
     int own, uint32_t xpeer, const TileLoc& loc, int grow0, int n_tile,
-    bool& cluster_waited) {
+    bool& cluster_waited, uint8_t* cbox = nullptr,
+    const CUtensorMap* tmC = nullptr) {
   constexpr int kHalf = BN / 2;
   constexpr int kHalfChunks = kHalf / 16;
   constexpr uint32_t kChunkBytes = 2u * 128u * 16u * 4u;  // GEMM1 + GEMM2
@@ -976,9 +992,23 @@ __device__ __forceinline__ void split_epilogue(
     }
     // after an expired wait the values are stale but every access stays in
     // bounds; the error word reports it
-    emit16(out, own * kHalf + 16 * c, ox[i], oy[i]);
+    if (kHalf == 64 && cbox != nullptr)
+      stage_row16(cbox + row * 128, row, 2 * c, ox[i], oy[i]);
+    else
+      emit16(out, own * kHalf + 16 * c, ox[i], oy[i]);
   }
+  if (kHalf == 64 && cbox != nullptr) fence_proxy_async_smem();
   split_group_all(all_ok);  // every participant finishes the tile together
+  // With a C store box (fp16 C, 64 columns per half): the half-tile's 128
+  // rows x 64 columns go out as one TMA store.
+  if (kHalf == 64 && cbox != nullptr && threadIdx.x == 0 && grow0 < loc.rows) {
+    const int bx = (n_tile * BN + own * kHalf) * 2;
+    if (p.c_layers > 1)
+      tma_store_3d(tmC, cbox, bx, grow0, loc.l);
+    else
+      tma_store_2d(tmC, cbox, bx, grow0);
+    bulk_commit_group();
+  }
   tc_fence_before();
   if (part == 0 && threadIdx.x == 0) NVFP4DG_STAMP(5, 0);
 }
@@ -1813,7 +1843,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (plan.split == 2)
       split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
                          warp, lane, 1, split_own, crank ^ 2u, split_loc,
-                         split_grow0, split_n_tile, cluster_waited);
+                         split_grow0, split_n_tile, cluster_waited,
+                         p.c_tma ? smem + S * Cf::kStageBytes : nullptr, &tmC);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
@@ -1886,7 +1917,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
                        warp, lane, 0, split_own, crank ^ 2u, split_loc,
-                       split_grow0, split_n_tile, cluster_waited);
+                       split_grow0, split_n_tile, cluster_waited,
+                       p.c_tma ? smem + S * Cf::kStageBytes : nullptr, &tmC);
   } else {
     // ------------------------------------------------------------ epilogue
     const int row = threadIdx.x;
@@ -2586,6 +2618,48 @@ Plan choose_plan(int M, int N, int K, unsigned flags, int sms, int L = 1) {
   return best;
 }
 
+// The schedules of recent problems: the cost model weighs a few dozen
+// candidate plans (~2 us of host time), which a caller that repeats the same
+// shapes (one call per layer and step) should pay once.  Small, direct
+// mapped, guarded by g_mu like the other host caches; the flag bits that
+// only affect the launch (not the plan) are left out of the key.
+struct PlanKey {
+  int M, N, K, L, sms;
+  unsigned flags;
+  bool operator==(const PlanKey& o) const {
+    return M == o.M && N == o.N && K == o.K && L == o.L && sms == o.sms &&
+           flags == o.flags;
+  }
+};
+constexpr int kPlanCacheSize = 32;
+struct PlanCacheEntry {
+  bool used;
+  PlanKey key;
+  Plan plan;
+};
+PlanCacheEntry g_plan_cache[kPlanCacheSize];
+
+Plan cached_plan(int M, int N, int K, unsigned flags, int sms, int L) {
+  constexpr unsigned kLaunchOnly = NVFP4DG_FLAG_SYNC_CHECK | NVFP4DG_FLAG_NO_PDL |
+                                   NVFP4DG_FLAG_NO_MERGED_B |
+                                   NVFP4DG_FLAG_STATIC_WEIGHTS |
+                                   NVFP4DG_FLAG_TEST_SK_TIMEOUT |
+                                   NVFP4DG_FLAG_NO_TMA_STORE;
+  const PlanKey key{M, N, K, L, sms, flags & ~kLaunchOnly};
+  const unsigned h = (static_cast<unsigned>(M) * 2654435761u ^
+                      static_cast<unsigned>(N) * 40503u ^
+                      static_cast<unsigned>(K) * 97u ^
+                      static_cast<unsigned>(L) * 131u ^ key.flags) %
+                     kPlanCacheSize;
+  PlanCacheEntry& e = g_plan_cache[h];
+  if (e.used && e.key == key) return e.plan;
+  const Plan plan = choose_plan(M, N, K, key.flags, sms, L);
+  e.used = true;
+  e.key = key;
+  e.plan = plan;
+  return plan;
+}
+
 int check_problem(const void* A, const void* B1, const void* B2,
                   const void* SFA, const void* SFB1, const void* SFB2,
                   const void* C, int M, int N, int K, int L, unsigned flags,
@@ -2858,7 +2932,7 @@ int run_impl(const void* A, const void* B1, const void* B2, const void* SFA,
     if (plan.grid == 0) return NVFP4DG_OK;  // every group is empty
     groups = &table;
   } else {
-    plan = choose_plan(M, N, K, flags, dev->sms, L);
+    plan = cached_plan(M, N, K, flags, dev->sms, L);
   }
   if (plan.grid == 0)
     return fail(NVFP4DG_ERR_UNSUPPORTED,
@@ -3364,12 +3438,12 @@ int nvfp4_dual_gemm_run_noalloc(const void* A, const void* B1, const void* B2,
     // (stream-K), whose partials can exceed the array; whole tiles need no
     // scratch at all, so fall back to them unless stream-K was forced.
     size_t need = static_cast<size_t>(
-        workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+        workspace_bytes(cached_plan(M, N, K, flags, dev->sms, 1)));
     if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES &&
         !(flags & NVFP4DG_FLAG_FORCE_STREAMK)) {
       flags |= NVFP4DG_FLAG_NO_STREAMK;
       need = static_cast<size_t>(
-          workspace_bytes(choose_plan(M, N, K, flags, dev->sms)));
+          workspace_bytes(cached_plan(M, N, K, flags, dev->sms, 1)));
     }
     if (need > NVFP4DG_NOALLOC_SCRATCH_BYTES)
       return fail(NVFP4DG_ERR_WORKSPACE,
@@ -3401,7 +3475,7 @@ size_t nvfp4_dual_gemm_workspace_size(int M, int N, int K, int L,
   DevInfo* dev = nullptr;
   if (device_info(devid, &dev)) return 0;
   return static_cast<size_t>(
-      workspace_bytes(choose_plan(M, N, K, flags, dev->sms, L)));
+      workspace_bytes(cached_plan(M, N, K, flags, dev->sms, L)));
 }
 
 int nvfp4_dual_gemm_plan(int M, int N, int K, unsigned flags, int num_sms,

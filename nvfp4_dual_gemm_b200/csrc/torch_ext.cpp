@@ -14,6 +14,7 @@
 // Invalid arguments raise ValueError; CUDA and device failures RuntimeError.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <torch/csrc/autograd/python_variable.h>
 #include <torch/extension.h>
 
 #include <string>
@@ -191,12 +192,23 @@ at::Tensor cuda_nvfp4_dual_gemm(const at::Tensor& A, const at::Tensor& B1,
 }
 
 // custom_kernel(data): data = (a, b1, b2, sfa, sfb1, sfb2, sfa_blocked,
-// sfb1_blocked, sfb2_blocked, c); the plain scales are not read.
-at::Tensor custom_kernel(const py::tuple& data) {
-  if (data.size() != 10)
+// sfb1_blocked, sfb2_blocked, c), a tuple or any sequence of 10 tensors; the
+// plain scales are not read.  The tensors are taken straight from the
+// sequence's items (no per-item conversion objects).
+at::Tensor custom_kernel(const py::object& data) {
+  PyObject* seq = PySequence_Fast(data.ptr(), "data must be a sequence");
+  if (seq == nullptr) throw py::error_already_set();
+  const py::object keep = py::reinterpret_steal<py::object>(seq);
+  if (PySequence_Fast_GET_SIZE(seq) != 10)
     bad("data must be the 10-tuple (a, b1, b2, sfa, sfb1, sfb2, "
         "sfa_blocked, sfb1_blocked, sfb2_blocked, c)");
-  auto t = [&](int i) { return data[i].cast<at::Tensor>(); };
+  PyObject** items = PySequence_Fast_ITEMS(seq);
+  auto t = [&](int i) -> const at::Tensor& {
+    if (!THPVariable_Check(items[i]))
+      throw py::type_error("data[" + std::to_string(i) +
+                           "] must be a torch.Tensor");
+    return THPVariable_Unpack(items[i]);
+  };
   return run(t(0), t(1), t(2), t(6), t(7), t(8), t(9), 0, nullptr);
 }
 
