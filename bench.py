@@ -232,6 +232,8 @@ def dist_setup():
         import datetime
 
         import torch.distributed as dist
+        # keep stdout to the one JSON line (NCCL prints its version at INFO)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     return world, rank, local

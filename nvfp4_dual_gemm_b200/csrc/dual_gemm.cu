@@ -1926,13 +1926,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), lead);
     // the accumulator may be overwritten: one arrival per warp on the even
     // CTA's barrier
+    uint32_t acc_phase = 0;
+    int unit_i = 0;
     auto release_acc = [&] {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc_empty_c);
+      if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
     };
-    uint32_t acc_phase = 0;
-    int unit_i = 0;
     WorkIter it;
     work_begin(plan, unit, it);
     Work w;
@@ -1958,12 +1959,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         cs.z = loc.l;
         tile_epilogue<BN, true>(t_row, OutRow{}, row, release_acc, cs, &tmC,
                                 p.c_layers);
-        if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
       } else if (w.slot < 0) {
         const OutRow out = out_row(p, loc, r0 + row, n_tile * BN);
         tile_epilogue<BN, false>(t_row, out, row, release_acc, CStore{},
                                  &tmC, p.c_layers);
-        if (threadIdx.x == 0) NVFP4DG_STAMP(8, unit_i);
       } else {
         const OutRow out = out_row(p, loc, r0 + row, n_tile * BN);
         // Stream-K tile shared by units b_first..b_last: as in the 1-SM
