@@ -1510,6 +1510,41 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the even CTA's `sf_ready` / `acc_empty`; the even CTA's MMA thread commits
 // to both CTAs' `empty` / `acc_full` barriers.
 // ===========================================================================
+// Before the dependency wait of the 2-SM pair kernel, the epilogue warps
+// (idle until the first accumulator is ready; lane 0 of warp q takes stages
+// q, q + 4, ...) prefetch into L2 the operands of the first S stages of the
+// CTA's first work item: its A rows and B half (tensor-map boxes) and the
+// three scale runs.  A prefetch only warms L2, which is coherent, so it is
+// correct whatever the previous grid writes; while the previous call drains,
+// it turns the first stages' HBM latency into L2 latency.  Ungrouped
+// problems with 2-D maps only.
+template <int BN, int S>
+__device__ __forceinline__ void pair_prefetch_first_stages(
+    const KParams& p, const CUtensorMap* tmA, const CUtensorMap* tmB,
+    int unit, int rank, int warp, int lane) {
+  if (lane != 0 || p.maps3d || p.groups.count) return;
+  WorkIter it;
+  work_begin(p.plan, unit, it);
+  Work w;
+  if (!work_next(p.plan, it, w)) return;
+  const TileLoc t = locate(p, w.tile);
+  const int kblk64 = p.K / 64;
+  const int a_row = t.m_tile * 2 * kBM + rank * kBM;
+  const int a_blk = min(t.m_tile * 2 + rank, (t.rows + kBM - 1) / kBM - 1);
+  const uint8_t* sfa = p.sfa + (size_t)a_blk * kblk64 * kSfAtomBytes;
+  const size_t sfb_off = (size_t)((t.n_tile * BN) / 128) * kblk64 * kSfAtomBytes;
+  const int nst = min(S, w.kb1 - w.kb0);
+  for (int j = warp; j < nst; j += kEpiWarps) {
+    const int kb = w.kb0 + j;
+    const size_t run = (size_t)kb * kSfRunBytes;
+    tma_prefetch_2d(tmA, kb * kRowBytes, a_row);
+    tma_prefetch_2d(tmB, kb * kRowBytes, t.n_tile * BN);
+    bulk_prefetch_l2(sfa + run, kSfRunBytes);
+    bulk_prefetch_l2(p.sfb1 + sfb_off + run, kSfRunBytes);
+    bulk_prefetch_l2(p.sfb2 + sfb_off + run, kSfRunBytes);
+  }
+}
+
 template <int BN>
 struct PairCfg {
   static constexpr int kStages = (BN == 128) ? 5 : 7;
@@ -1561,26 +1596,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   NVFP4DG_STAMP_NS(61);
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const Plan& plan = p.plan;
   // Clusters of 2 CTAs (one pair), or of 4 for split-K (two pairs: ranks
   // 2h and 2h + 1 take half h of K).  A pair is ranks (lead, lead + 1).
   const uint32_t crank = cluster_ctarank();
   const uint32_t rank = crank & 1u;   // position in the pair
   const uint32_t lead = crank & ~1u;  // cluster rank of the pair's even CTA
-  const int unit = blockIdx.x >> 1;   // the pair's work-unit index
-  const bool leader = (rank == 0);
-  // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
-  // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
-  const int split_own = static_cast<int>(crank >> 1);
-  const TileLoc split_loc = locate(p, unit >> 1);
-  const int split_m_tile = split_loc.m_tile, split_n_tile = split_loc.n_tile;
-  const int split_grow0 =
-      split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
-  bool cluster_waited = true;  // the start-up cluster barrier (below)
-
-  const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
-  // Warp 0 initialises the mbarriers while the producers work out their
-  // first item (as in the 1-SM kernel).
+  // Warp 0 initialises the mbarriers first of all: nothing of it depends on
+  // the kernel parameters, whose first reads miss the constant cache (a new
+  // parameter buffer each launch) and would otherwise delay every role
+  // waiting for the barriers.
   if (warp == 0) {
     // full: the scale warps of both CTAs, on the even CTA the first one's
     // arrival carrying both CTAs' tile bytes; sfdata: one arming arrival;
@@ -1592,13 +1616,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) NVFP4DG_STAMP(9, 56);
     if (lane == 0) prefetch_tmap(&tmA);
     if (lane == 1) prefetch_tmap(rank == 0 ? &tmB1 : &tmB2);
-    if (lane == 2 && p.c_tma) prefetch_tmap(&tmC);
   }
   // Every CTA's barriers initialised (published by the mbarrier-init fence)
   // before any remote use: arrive now, wait after the TMEM allocation, so
   // that the cluster-wide barrier completes meanwhile.
   __syncwarp();
   cluster_arrive_relaxed();
+  const Plan& plan = p.plan;
+  const int unit = blockIdx.x >> 1;   // the pair's work-unit index
+  const bool leader = (rank == 0);
+  // Split-K (4-CTA clusters): this pair's half of K, its tile, and the first
+  // output row of this CTA's 128 rows; the partner is cluster rank crank ^ 2.
+  const int split_own = static_cast<int>(crank >> 1);
+  const TileLoc split_loc = locate(p, unit >> 1);
+  const int split_m_tile = split_loc.m_tile, split_n_tile = split_loc.n_tile;
+  const int split_grow0 =
+      split_m_tile * 2 * kBM + static_cast<int>(rank) * kBM;
+  bool cluster_waited = true;  // the start-up cluster barrier (below)
+  const bool producer = (warp == kProdAWarp || warp == kProdBWarp);
+  if (warp == 0 && lane == 2 && p.c_tma) prefetch_tmap(&tmC);
   uint32_t tmem = 0;
   if (!producer) {
     if (warp == 0) named_bar_arrive(kBarInit, 96);
@@ -1915,12 +1951,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (plan.split == 2) {
     // ------------------------------------------------------------ epilogue
+    pair_prefetch_first_stages<BN, S>(p, &tmA, rank == 0 ? &tmB1 : &tmB2, unit,
+                                      static_cast<int>(rank), warp, lane);
     split_epilogue<BN>(p, smem, tmem, &acc_full_bar, &ready_bar, recv_bar,
                        warp, lane, 0, split_own, crank ^ 2u, split_loc,
                        split_grow0, split_n_tile, cluster_waited,
                        p.c_tma ? smem + S * Cf::kStageBytes : nullptr, &tmC);
   } else {
     // ------------------------------------------------------------ epilogue
+    pair_prefetch_first_stages<BN, S>(p, &tmA, rank == 0 ? &tmB1 : &tmB2, unit,
+                                      static_cast<int>(rank), warp, lane);
     const int row = threadIdx.x;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const uint32_t acc_empty_c = mapa_shared(smem_u32(&acc_empty_bar), lead);

@@ -187,6 +187,25 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src,
       : "memory");
 }
 
+// L2 prefetches (hints: nothing is written, nothing waits for them).  A
+// 2-D box of a tensor map, and a contiguous run (16-byte aligned, size a
+// multiple of 16).
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* m, int c0,
+                                                int c1) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src,
+                                                 uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src),
+               "r"(bytes)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: tensor memory
 // ---------------------------------------------------------------------------
