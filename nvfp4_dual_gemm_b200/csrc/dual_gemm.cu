@@ -156,8 +156,10 @@ __device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
       g_trace[blockIdx.x][role][idx] = clock_cycles();             \
   } while (0)
 // Global-timer (ns, comparable across SMs) stamps of thread 0 in role 5,
-// slots 61-63: kernel entry, past the dependency wait, exit; the SM clock at
-// the same moments goes to role 4, same slots.
+// slots 61-63: kernel entry, end of the prologue, exit (pair kernel also
+// 50-52: teardown start, C store boxes read, past the final cluster
+// barrier; 53: producer A past the dependency wait); the SM clock at the
+// same moments goes to role 4, same slots.
 #define NVFP4DG_STAMP_NS(idx)                                      \
   do {                                                             \
     if (threadIdx.x == 0 && blockIdx.x < kTraceCtas) {             \
@@ -167,7 +169,20 @@ __device__ long long g_trace[kTraceCtas][kTraceRoles][kTraceSlots];
       g_trace[blockIdx.x][5][idx] = t_;                            \
     }                                                              \
   } while (0)
+// The same from whichever thread executes it.
+#define NVFP4DG_STAMP_NS_ANY(idx)                                  \
+  do {                                                             \
+    if (blockIdx.x < kTraceCtas) {                                 \
+      long long t_;                                                \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));       \
+      g_trace[blockIdx.x][4][idx] = clock_cycles();                \
+      g_trace[blockIdx.x][5][idx] = t_;                            \
+    }                                                              \
+  } while (0)
 #else
+#define NVFP4DG_STAMP_NS_ANY(idx) \
+  do {                            \
+  } while (0)
 #define NVFP4DG_STAMP(role, idx) \
   do {                           \
   } while (0)
@@ -252,6 +267,7 @@ __device__ __forceinline__ void init_barriers_by_lane(
     mbar_init(bar, count);
     fence_mbar_init();
   }
+  if (lane == 0) s_wait_failed = 0u;
   __syncwarp();
   // arm the first scale fill of every stage (bytes may land before or after
   // an arming: a barrier's transaction count may go negative meanwhile)
@@ -1486,7 +1502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (the epilogue warps have already waited on the start-up phase).
   if (plan.split == 2) {
     if (!cluster_waited) cluster_wait();
-    cluster_sync();
+    cluster_sync_final();
   }
   if (warp == kMmaWarp) {
     __syncwarp();
@@ -1712,6 +1728,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool w_early = p.static_weights != 0;
       if (a_side || !w_early) griddep_wait();
       if (a_side) NVFP4DG_STAMP(9, 59);
+      if (a_side) NVFP4DG_STAMP_NS_ANY(53);
       while (ok && have) {
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (issued >= S &&
@@ -1945,6 +1962,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_commit_pair(mapa_shared(ab, peer));
         acc_phase ^= 1u;
       }
+      // The last unit's accumulator release (the odd CTA's epilogue warps
+      // arrive here remotely) is awaited like the others, so that no arrival
+      // is still in flight when the CTAs leave (cluster_sync_final).  Split-K
+      // epilogues release nothing: their exchange is awaited by each side.
+      if (ok && consumed > 0 && plan.split != 2)
+        mbar_wait_cluster(&acc_empty_bar, acc_phase ^ 1u, p.err, kErrMma);
       tc_commit_pair(mapa_shared(smem_u32(&drain_bar), lead));
       mbar_wait(&drain_bar, 0, p.err, kErrDrain, /*bail_on_err=*/false);
     }
@@ -2066,10 +2089,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ------------------------------------------------------------ teardown
-  // the C stores must have read their boxes before shared memory goes away
-  if (p.c_tma && threadIdx.x == 0) bulk_wait_group0();
+  // The C stores must have read their boxes before shared memory goes away;
+  // their global writes complete before the grid does.
+  if (lane == 0) NVFP4DG_STAMP(9, 40 + warp);
+  NVFP4DG_STAMP_NS(50);
+  if (p.c_tma && threadIdx.x == 0) bulk_wait_group_read0();
+  NVFP4DG_STAMP_NS(51);
   tc_fence_before();
-  cluster_sync();  // no CTA leaves while its peer may still signal it
+  cluster_sync_final();  // no CTA leaves while its peer may still signal it
+  NVFP4DG_STAMP_NS(52);
   if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();

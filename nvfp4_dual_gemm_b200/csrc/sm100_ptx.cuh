@@ -86,6 +86,16 @@ __device__ __forceinline__ long long clock_cycles() {
   return t;
 }
 
+// Set (to 1) in a CTA when one of its bounded waits gives up; cleared by the
+// kernels' barrier initialisation before any wait.  A CTA that gave up may
+// not have awaited every signal its cluster peers send it, so it lingers
+// before leaving (see linger_if_wait_failed).
+__shared__ unsigned s_wait_failed;
+
+__device__ __forceinline__ void note_wait_failed() {
+  *reinterpret_cast<volatile unsigned*>(&s_wait_failed) = 1u;
+}
+
 // Wait until the phase with parity `parity` of `bar` has completed.  Returns
 // false (after setting `code` in *err) if the time limit expires, or early if
 // *err is already non-zero because another role gave up.
@@ -104,10 +114,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
         t0 = now;
         continue;
       }
-      if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u)
+      if (bail_on_err && *reinterpret_cast<volatile unsigned*>(err) != 0u) {
+        note_wait_failed();
         return false;
+      }
       if (now - t0 > kWaitLimitCycles) {
         atomicOr(err, code);
+        note_wait_failed();
         return false;
       }
     }
@@ -136,9 +149,13 @@ __device__ __forceinline__ bool wait_count(const int* ptr, int target,
   for (;;) {
     __nanosleep(32);
     if (ld_acquire(ptr) == target) return true;
-    if (*reinterpret_cast<volatile unsigned*>(err) != 0u) return false;
+    if (*reinterpret_cast<volatile unsigned*>(err) != 0u) {
+      note_wait_failed();
+      return false;
+    }
     if (clock_cycles() - t0 > limit) {
       atomicOr(err, code);
+      note_wait_failed();
       return false;
     }
   }
@@ -445,6 +462,24 @@ __device__ __forceinline__ void sts128(uint32_t saddr, uint4 v) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(saddr),
                "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                : "memory");
+}
+
+// Final cluster barrier of a kernel in which every signal or copy into a
+// peer CTA's shared memory is awaited by that peer before it gets here: the
+// arrival needs no release ordering (a release arrival would wait for this
+// thread's outstanding global writes, e.g. the C tile stores, to complete).
+// A CTA in which a bounded wait gave up may have skipped some of those
+// waits; it stays resident for ~50K more cycles (a bounded spin) so that
+// anything still in flight towards it lands before its shared memory is
+// released.
+__device__ __forceinline__ void cluster_sync_final() {
+  cluster_arrive_relaxed();
+  cluster_wait();
+  if (*reinterpret_cast<volatile unsigned*>(&s_wait_failed) != 0u) {
+    const long long t0 = clock_cycles();
+    while (clock_cycles() - t0 < 50000) {
+    }
+  }
 }
 
 __device__ __forceinline__ void cluster_sync() {

@@ -105,7 +105,7 @@ def summarise(buf: np.ndarray) -> dict:
         for k, v in zip(["split_peer_ready", "split_send", "split_own_ld",
                          "split_first_recv", "split_rest"], sm):
             out[k] = float(v)
-    # global-timer stamps (ns) of every CTA: entry, past the dependency wait,
+    # global-timer stamps (ns) of every CTA: entry, end of the prologue,
     # exit
     ent = buf[:, 5, 61]
     ok = ent > 0
@@ -115,6 +115,32 @@ def summarise(buf: np.ndarray) -> dict:
         out["ns_prologue"] = float(np.median(dep - ent))
         out["ns_cta_span"] = float(np.median(ext - ent))
         out["ns_kernel_span"] = float(ext.max() - ent.min())
+        # pair kernel (slots 50-53): from the earliest return of the
+        # dependency wait (the previous grid's completion as this grid sees
+        # it) to the last exit, and the teardown's phases
+        dep = buf[ok, 5, 53]
+        td0, td1, td2 = buf[ok, 5, 50], buf[ok, 5, 51], buf[ok, 5, 52]
+        has = (dep > 0) & (td0 > 0) & (td1 > 0) & (td2 > 0)
+        if has.any():
+            rel = dep[has].min()
+            out["ns_release_skew"] = float(np.median(dep[has]) - rel)
+            out["ns_release_to_last_teardown"] = float(td0[has].max() - rel)
+            out["ns_release_to_last_exit"] = float(ext.max() - rel)
+            out["ns_store_read_wait"] = float(np.median(td1[has] - td0[has]))
+            out["ns_final_cluster_sync"] = float(
+                np.median(td2[has] - td1[has]))
+            out["ns_dealloc_to_exit"] = float(np.median(ext[has] - td2[has]))
+            # each warp's arrival at the teardown (role 9 slots 40-50, SM
+            # cycles) relative to thread 0's, the latest warp per CTA
+            t0 = buf[ok, 4, 50]
+            arr = buf[ok, 9, 40:51]
+            sel = (t0 > 0) & (arr > 0).all(axis=1)
+            if sel.any():
+                rel_w = arr[sel] - t0[sel][:, None]
+                out["cyc_teardown_arrival_by_warp"] = [
+                    float(v) for v in np.median(rel_w, axis=0)]
+                out["cyc_teardown_latest_warp"] = float(
+                    np.median(rel_w.max(axis=1)))
         clk = buf[ok, 4, 63] - buf[ok, 4, 61]
         out["sm_mhz"] = float(np.median(clk / np.maximum(ext - ent, 1)) * 1e3)
         # SM cycles from entry to the first copy, and from the end of the
@@ -154,6 +180,8 @@ def main(argv=None) -> None:
                     help="no synchronize before the traced call: it starts "
                          "while the previous calls drain, as in a stream of "
                          "calls (the stamps of the last call win)")
+    ap.add_argument("--raw", default=None,
+                    help="also save the raw stamp buffer (.npy) here")
     args = ap.parse_args(argv)
 
     import torch
@@ -190,6 +218,8 @@ def main(argv=None) -> None:
     call(args.calls)
     torch.cuda.synchronize()
     lib.nvfp4_dual_gemm_trace_read(buf.ctypes.data, buf.nbytes)
+    if args.raw:
+        np.save(args.raw, buf)
     print({"problem": [m, n, k], "flags": args.flags,
            "plan": api.plan(m, n, k, args.flags), **summarise(buf)})
 
