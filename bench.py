@@ -22,8 +22,11 @@ K back-to-back calls, each between two CUDA events on the launching stream
 with a barrier and a synchronize on both sides; the region's median is the
 shape's time (max over ranks).  Inputs rotate over enough independent sets
 that more than 2 x the 126 MB L2 is touched between two uses of a set.
-Beside it, per shape: the same calls captured in a CUDA graph, and end to
-end through the host-buffer API (pinned host inputs and output).
+Beside it, per shape: the same calls captured in a CUDA graph, end to end
+through the host-buffer API (pinned host inputs and output), and cold
+single calls (`cold_us_per_call`: each call after a 256 MB write that
+evicts L2, timed alone with its launch latency, median of `--cold-reps`),
+the way a harness that clears L2 before every call times it.
 
 Multi-GPU (torchrun, one process per GPU): C2/C3/C4 run the full shape on
 every rank (weak scaling); C5's N = 28672 is split over the ranks (strong
@@ -409,6 +412,37 @@ def time_eager(step_fn, steps, warmup, world, repeats):
     return statistics.median(times), times, clk.summary()
 
 
+COLD_TIMED = ("per shape: `cold_reps` single calls, each after a 256 MB "
+              "device write that evicts L2 (2 x its 126 MB), CUDA events "
+              "around that one call on the launching stream; median call "
+              "(the way a harness that clears L2 between calls times it)")
+_FLUSH = []
+
+
+def time_cold(step_fn, reps, world):
+    """`reps` single calls, each preceded by a write of a buffer twice the
+    L2 size and bracketed by its own CUDA events; returns the median ms of
+    one call, max over ranks (the launch latency of the call is inside)."""
+    if not _FLUSH:
+        _FLUSH.append(torch.empty(256 << 20, dtype=torch.uint8,
+                                  device="cuda"))
+    buf = _FLUSH[0]
+    step_fn(0)
+    torch.cuda.synchronize()
+    evs = []
+    for i in range(reps):
+        buf.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        step_fn(i)
+        e.record()
+        evs.append((s, e))
+    torch.cuda.synchronize()
+    ms = statistics.median(s.elapsed_time(e) for s, e in evs)
+    return max(gather_ranks(ms, world))
+
+
 def time_graph(step_fn, steps, warmup, world, repeats=1):
     """Warm up eagerly, capture `steps` calls in one CUDA graph, replay it
     `repeats` times, each replay a timed region; returns (median ms per
@@ -562,6 +596,10 @@ def run_ours(args, world, rank):
                "l2": f"{ns} rotating input sets of "
                      f"{algo_bytes(m, n, k) / 1e6:.1f} MB (> 2 x 126 MB L2 "
                      "between reuses)"}
+        if args.cold_reps > 0:
+            ent["cold_us_per_call"] = round(
+                time_cold(step, args.cold_reps, world) * 1e3, 3)
+            launches += args.cold_reps + 1
         # the same calls captured in a CUDA graph (caller workspace, so the
         # capture allocates nothing), with and without STATIC_WEIGHTS
         if not args.no_graph:
@@ -617,6 +655,8 @@ def run_ours(args, world, rank):
         "repeats": args.repeats,
         "ms_per_step": sum(s["us_per_call"] for s in shapes) / 1e3,
         "us_per_call": {s["workload"]: s["us_per_call"] for s in shapes},
+        "cold_us_per_call": {s["workload"]: s.get("cold_us_per_call")
+                             for s in shapes},
         "higher_is_better": True,
         "scaling": "weak",
         "scaling_by_workload": {k: ("strong" if WORKLOADS[k].get("strong")
@@ -637,6 +677,7 @@ def run_ours(args, world, rank):
             "api": "custom_kernel(data) -> torch binding _C -> C ABI "
                    "nvfp4_dual_gemm_run, default flags",
             "timed": EAGER_TIMED,
+            "cold": COLD_TIMED,
             "l2": "per shape, rotating input sets touching > 2 x 126 MB "
                   "between reuses of a set"},
         "shapes": shapes,
@@ -649,7 +690,8 @@ def run_ours(args, world, rank):
                        "nvfp4_dual_gemm_run_host), geomean over the shapes"},
         "gpu_launches": launches,
         "gpu_launches_note": "dual GEMM kernel launches in the eager timed "
-                             "regions that give `value` (one per call)",
+                             "regions that give `value` (one per call) and "
+                             "in the cold single-call timings",
         "clocks": merge_clocks(clocks),
     }
     if cpu:
@@ -716,6 +758,9 @@ def run_reference(args, world):
                          if (m, n, k) in build_ref.SAFE_SHAPES else
                          "cuda_nvfp4_dual_gemm_generic (its launcher "
                          "template, instantiated for this shape)")}
+        if args.cold_reps > 0:
+            ent["cold_us_per_call"] = round(
+                time_cold(step, args.cold_reps, 1) * 1e3, 3)
         if args.e2e_steps > 0:
             d0 = sets[0]
             dev_in, host_in, c_host = _host_copies(d0)
@@ -746,6 +791,8 @@ def run_reference(args, world):
         "steps": args.steps, "warmup": args.warmup, "repeats": args.repeats,
         "ms_per_step": sum(s.get("us_per_call", 0.0) for s in shapes) / 1e3,
         "us_per_call": {s["workload"]: s.get("us_per_call") for s in shapes},
+        "cold_us_per_call": {s["workload"]: s.get("cold_us_per_call")
+                             for s in shapes},
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "nvfp4 (e2m1 x e4m3/16, fp32 accumulate, fp16 out)",
         "data": "synthetic: seeded randn -> NVFP4 by torch ops on the GPU "
@@ -757,7 +804,7 @@ def run_reference(args, world):
                    "parallelism": ("rank 0 alone, on one rank's shapes "
                                    f"(C5 N / {world})" if world > 1 else
                                    "single GPU"),
-                   "timed": EAGER_TIMED},
+                   "timed": EAGER_TIMED, "cold": COLD_TIMED},
         "reference_kind": ("the reference's CUDA kernel compiled from its "
                            "sources by oracle/build_ref.py, called as its "
                            "custom_kernel calls it (submission.py:1153-1157)"
@@ -1081,6 +1128,9 @@ def main():
                     help="end-to-end steps per shape (0: skip)")
     ap.add_argument("--no-graph", action="store_true",
                     help="skip the CUDA-graph timings beside the eager ones")
+    ap.add_argument("--cold-reps", type=int, default=30,
+                    help="single calls after an L2 flush per shape, timed "
+                         "one by one (0: skip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--plumbing", choices=sorted(PLUMBING),
                     help="time one of the kernels beside the dual GEMM "
