@@ -3279,6 +3279,28 @@ int run_host_impl(const void* A, const void* B1, const void* B2,
   uint8_t* st = static_cast<uint8_t*>(staging);
   const size_t row_b = static_cast<size_t>(K) / 2;
   const size_t atom_row = static_cast<size_t>(K / 64) * 512;  // per 128 rows
+  if (nslab == 1) {
+    // Nothing to overlap: upload, kernel and download in order on the
+    // caller's stream, without the copy streams' event hand-offs (a few us
+    // each on a call that the PCIe transfers already bound).
+    const size_t n_sf = static_cast<size_t>(blocked_bytes(N, K));
+    rc = copy_up(st + lay.a, A, M * row_b, s0);
+    if (!rc) rc = copy_up(st + lay.sfa, SFA, blocked_bytes(M, K), s0);
+    if (!rc) rc = copy_up(st + lay.b1, B1, N * row_b, s0);
+    if (!rc) rc = copy_up(st + lay.b2, B2, N * row_b, s0);
+    if (!rc) rc = copy_up(st + lay.sfb1, SFB1, n_sf, s0);
+    if (!rc) rc = copy_up(st + lay.sfb2, SFB2, n_sf, s0);
+    __half* cs = reinterpret_cast<__half*>(st + lay.c);
+    if (!rc)
+      rc = run_impl(st + lay.a, st + lay.b1, st + lay.b2, st + lay.sfa,
+                    st + lay.sfb1, st + lay.sfb2, cs, M, N, K, 1, flags,
+                    nullptr, 0, true, s0);
+    if (!rc &&
+        (e = cudaMemcpyAsync(C, cs, static_cast<size_t>(M) * N * sizeof(__half),
+                             cudaMemcpyDeviceToHost, s0)))
+      rc = cuda_fail(e, "download");
+    return rc;
+  }
   // Uploads start once everything before this call on the caller's stream
   // (an earlier call still reading the staging buffer) is done.
   if ((e = cudaEventRecord(p.start, s0)) ||
