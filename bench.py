@@ -443,6 +443,33 @@ def time_cold(step_fn, reps, world):
     return max(gather_ranks(ms, world))
 
 
+def time_allgather(d, key, world, rank, reps):
+    """The optional all-gather of the N-sharded C (NCCL, after the kernels,
+    not part of `value`): shard.gather_columns of this rank's [M, N/w] slice
+    into the full [M, N], `reps` calls between events, median per call, max
+    over ranks; bus bandwidth as NCCL counts it for an all-gather."""
+    from nvfp4_dual_gemm_b200 import shard
+
+    wl = WORKLOADS[key]
+    spec = shard.shard_spec(wl["N"], wl["K"], world, rank)
+    c_local = d[9].squeeze(-1)
+    shard.gather_columns(c_local, spec)  # warm-up (NCCL channels)
+    times = []
+    for _ in range(reps):
+        times.append(_region(lambda: shard.gather_columns(c_local, spec),
+                             world))
+    ms = max(gather_ranks(statistics.median(times), world))
+    full = c_local.numel() * c_local.element_size() * world
+    return {"us": round(ms * 1e3, 1),
+            "bytes_out_per_rank": full,
+            "busbw_gbs": round(full * (world - 1) / world / (ms * 1e-3) / 1e9,
+                               1),
+            "what": "nvfp4_dual_gemm_b200.shard.gather_columns: NCCL "
+                    "all_gather of the [M, N/w] fp16 slices + column "
+                    "assembly into [M, N]; reported separately, not in "
+                    "value"}
+
+
 def time_graph(step_fn, steps, warmup, world, repeats=1):
     """Warm up eagerly, capture `steps` calls in one CUDA graph, replay it
     `repeats` times, each replay a timed region; returns (median ms per
@@ -600,6 +627,9 @@ def run_ours(args, world, rank):
             ent["cold_us_per_call"] = round(
                 time_cold(step, args.cold_reps, world) * 1e3, 3)
             launches += args.cold_reps + 1
+        if WORKLOADS[key].get("strong") and world > 1:
+            ent["allgather"] = time_allgather(sets[0], key, world, rank,
+                                              max(3, args.steps // 2))
         # the same calls captured in a CUDA graph (caller workspace, so the
         # capture allocates nothing), with and without STATIC_WEIGHTS
         if not args.no_graph:
