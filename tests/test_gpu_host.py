@@ -49,7 +49,8 @@ def test_host_entry_matches_oracle(m, n, k, slabs):
     assert_close(got, O.reference_output(p), f"host entry {m}x{n}x{k}/{slabs}")
 
 
-def test_host_entry_pageable_memory_and_repeat_calls():
+@pytest.mark.parametrize("slabs", [1, 3])  # 1: everything on the caller's stream
+def test_host_entry_pageable_memory_and_repeat_calls(slabs):
     m, n, k = 256, 768, 1536
     p = O.make_problem(m, n, k, seed=5)
     q = O.make_problem(m, n, k, seed=6)
@@ -64,7 +65,7 @@ def test_host_entry_pageable_memory_and_repeat_calls():
             h["c"].fill_(float("nan"))
             dg.dual_gemm_host(h["a"], h["b1"], h["b2"], h["sfa_blocked"],
                               h["sfb1_blocked"], h["sfb2_blocked"], h["c"],
-                              slabs=3, staging=staging)
+                              slabs=slabs, staging=staging)
         torch.cuda.current_stream().synchronize()
         assert_close(hp["c"].numpy(), want_p, f"pageable call {rep}")
         assert_close(hq["c"].numpy(), want_q, f"pinned call {rep}")
