@@ -338,9 +338,9 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 // e4m3(amax / 6) (round to nearest even, saturating at 448) and sets w0/w1
 // to the eight bytes of e2m1 codes of q = RN(v / scale) rounded to the e2m1
 // grid (nearest, ties to the even code, saturating at 6, sign kept), all-zero
-// codes when the scale is 0.  The activation quantiser and the NVFP4-output
-// epilogue both use it, so the fused output equals quantising the fp16
-// result.
+// codes when the scale is 0.  The forms below (the compare form for 16-bit
+// values, encode_rcp16) give the same codes, so the fused NVFP4 output
+// equals quantising the fp16 result, whichever form each side uses.
 //
 // No division: the e2m1 code of q only depends on how q compares with the
 // grid midpoints t in {0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5}, and
@@ -394,6 +394,10 @@ __device__ __forceinline__ uint8_t quant_block16(const float* v, uint32_t& w0,
 // between 2^-11 and 2240) is exact in fp16 and in bf16, and for a 16-bit v,
 // v >= T <=> v > the 16-bit value below T; so comparing 16-bit keys with
 // packed 2-wide compares gives exactly the codes of the fp32 form above.
+// The NVFP4-output epilogue uses this compare form (which keeps the GEMM
+// kernels' register allocation as it is); the activation quantiser uses
+// quant_block16_x2 below, which gives the same codes with fewer
+// instructions and hands blocks holding a NaN to this form.
 template <typename H2>
 struct Half2Ops;
 template <>
@@ -405,6 +409,7 @@ struct Half2Ops<__half2> {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(u)));
   }
   static __device__ __forceinline__ float hi(uint32_t u) { return lo(u >> 16); }
+  static constexpr uint32_t kInfKey = 0x7C00u;  // |v| bits of +inf
 };
 template <>
 struct Half2Ops<__nv_bfloat162> {
@@ -417,6 +422,7 @@ struct Half2Ops<__nv_bfloat162> {
   static __device__ __forceinline__ float hi(uint32_t u) {
     return __uint_as_float(u & 0xFFFF0000u);
   }
+  static constexpr uint32_t kInfKey = 0x7F80u;
 };
 
 template <typename H2>
@@ -425,9 +431,9 @@ __device__ __forceinline__ H2 as_h2(uint32_t u) {
 }
 
 template <typename H2>
-__device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
-                                                    uint32_t& w0,
-                                                    uint32_t& w1) {
+__device__ __forceinline__ uint8_t quant_block16_x2_cmp(const uint32_t (&p)[8],
+                                                        uint32_t& w0,
+                                                        uint32_t& w1) {
   using Ops = Half2Ops<H2>;
   uint32_t a[8];  // |v| pairs: the keys
 #pragma unroll
@@ -471,6 +477,124 @@ __device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
     }
   }
   return static_cast<uint8_t>(sb);
+}
+
+// Eight values x (fp32 bit patterns, x[0] first) -> four bytes of e2m1
+// codes (element 2i in the low nibble of byte i) of q = x * rh + RN(x * rl),
+// rounded once (packed fma), by the hardware conversion (round to nearest
+// even, saturating at 6, sign kept).
+__device__ __forceinline__ uint32_t e2m1_scaled8(const uint32_t (&x)[8],
+                                                 float rh, float rl) {
+  uint32_t r;
+  asm("{\n\t"
+      ".reg .b64 V, P, RH, RL;\n\t"
+      ".reg .b32 q0, q1, q2, q3, q4, q5, q6, q7;\n\t"
+      ".reg .b8 c0, c1, c2, c3;\n\t"
+      "mov.b64 RH, {%9, %9};\n\t"
+      "mov.b64 RL, {%10, %10};\n\t"
+      "mov.b64 V, {%1, %2};\n\t"
+      "mul.rn.f32x2 P, V, RL;\n\t"
+      "fma.rn.f32x2 V, V, RH, P;\n\t"
+      "mov.b64 {q0, q1}, V;\n\t"
+      "mov.b64 V, {%3, %4};\n\t"
+      "mul.rn.f32x2 P, V, RL;\n\t"
+      "fma.rn.f32x2 V, V, RH, P;\n\t"
+      "mov.b64 {q2, q3}, V;\n\t"
+      "mov.b64 V, {%5, %6};\n\t"
+      "mul.rn.f32x2 P, V, RL;\n\t"
+      "fma.rn.f32x2 V, V, RH, P;\n\t"
+      "mov.b64 {q4, q5}, V;\n\t"
+      "mov.b64 V, {%7, %8};\n\t"
+      "mul.rn.f32x2 P, V, RL;\n\t"
+      "fma.rn.f32x2 V, V, RH, P;\n\t"
+      "mov.b64 {q6, q7}, V;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c0, q1, q0;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c1, q3, q2;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c2, q5, q4;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 c3, q7, q6;\n\t"
+      "mov.b32 %0, {c0, c1, c2, c3};\n\t"
+      "}"
+      : "=r"(r)
+      : "r"(x[0]), "r"(x[1]), "r"(x[2]), "r"(x[3]), "r"(x[4]), "r"(x[5]),
+        "r"(x[6]), "r"(x[7]), "f"(rh), "f"(rl));
+  return r;
+}
+
+// One block's scale byte e4m3(amax / 6) and the e2m1 codes of its sixteen
+// values x (fp32 bit patterns) under it, with v / s replaced by
+// v * rh + RN(v * rl), rounded once, where rh = 1/s rounded toward zero and
+// rl = RN((1 - s * rh) * rh) >= 0 (the residual 1 - s * rh is exact in one
+// fma), and q rounded to e2m1 by the hardware conversion.  rh + rl is 1/s
+// to about 2^-46 relative, so q is v / s to about 2^-45 relative:
+//  * v / s exactly on a midpoint t (v = t * s) lands exactly on t and takes
+//    the same tie rule;
+//  * otherwise v / s lies at least ~2^-29 relative away from every fp32
+//    rounding boundary t +- ulp(t) / 2 (v = (t +- ulp(t) / 2) * s would need
+//    25 significant bits), so RN(q) and RN(v / s) fall on the same side of
+//    t, or are both t.
+// rl >= 0 keeps the sign of -0 (x * rl = -0); values whose quotient
+// overflows saturate at 6 either way.  For 16-bit v, tests/test_oracle.py
+// simulates this arithmetic for every finite value under every positive
+// e4m3 s on the CPU, and a GPU test runs all of those pairs through the
+// kernel; fp32 v are tested on and around every midpoint and boundary.
+// (A single rounded reciprocal, q = RN(v * RN(1/s)), is not enough: ties
+// at 1.25, 2.5 and 5 under scales of mantissa 1.875 round the wrong way.)
+__device__ __forceinline__ uint8_t encode_rcp16(float amax,
+                                                const uint32_t (&x)[16],
+                                                uint32_t& w0, uint32_t& w1) {
+  const __nv_fp8_storage_t sb =
+      __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+  const float sd =
+      __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
+  w0 = 0;
+  w1 = 0;
+  if (sd > 0.f) {
+    const float rh = __frcp_rz(sd);
+    const float rl = __fmul_rn(__fmaf_rn(-sd, rh, 1.0f), rh);
+    const uint32_t(&xa)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x);
+    const uint32_t(&xb)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x + 8);
+    w0 = e2m1_scaled8(xa, rh, rl);
+    w1 = e2m1_scaled8(xb, rh, rl);
+  }
+  return static_cast<uint8_t>(sb);
+}
+
+// The activation quantiser's 16-bit block form: amax as the largest |v| key
+// (16-bit keys order like |v|), then encode_rcp16.  A block holding a NaN
+// (key above +inf's) goes to the compare form.
+template <typename H2>
+__device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
+                                                    uint32_t& w0,
+                                                    uint32_t& w1) {
+  using Ops = Half2Ops<H2>;
+  uint32_t km = p[0] & 0x7FFF7FFFu;
+#pragma unroll
+  for (int i = 1; i < 8; ++i) km = __vmaxu2(km, p[i] & 0x7FFF7FFFu);
+  const uint32_t key = max(km & 0xFFFFu, km >> 16);
+  if (key > Ops::kInfKey) return quant_block16_x2_cmp<H2>(p, w0, w1);
+  uint32_t x[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    x[2 * i] = __float_as_uint(Ops::lo(p[i]));
+    x[2 * i + 1] = __float_as_uint(Ops::hi(p[i]));
+  }
+  return encode_rcp16(Ops::lo(key), x, w0, w1);
+}
+
+// The activation quantiser's fp32 block form: amax as the largest |v| bit
+// pattern, then encode_rcp16; a block holding a NaN goes to quant_block16.
+__device__ __forceinline__ uint8_t quant_block16_rcp(const float (&v)[16],
+                                                     uint32_t& w0,
+                                                     uint32_t& w1) {
+  uint32_t x[16];
+  uint32_t km = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    x[i] = __float_as_uint(v[i]);
+    km = max(km, x[i] & 0x7FFFFFFFu);
+  }
+  if (km > 0x7F800000u) return quant_block16(v, w0, w1);
+  return encode_rcp16(__uint_as_float(km), x, w0, w1);
 }
 
 // Where the epilogue of one tile row writes its outputs: fp16 C, or NVFP4
@@ -597,7 +721,7 @@ __device__ __noinline__ void quant_store16(uint8_t* q, uint8_t* sf, int col,
                                           uint32_t h6, uint32_t h7) {
   const uint32_t h[8] = {h0, h1, h2, h3, h4, h5, h6, h7};
   uint32_t w0, w1;
-  const uint8_t sb = quant_block16_x2<__half2>(h, w0, w1);
+  const uint8_t sb = quant_block16_x2_cmp<__half2>(h, w0, w1);
   if (row_ok) *reinterpret_cast<uint2*>(q) = make_uint2(w0, w1);
   if (sf_ok) sf[(col / 64) * kSfAtomBytes + (col / 16) % 4] = sb;
 }
@@ -2142,7 +2266,7 @@ struct In16<float> {
   }
 };
 // One 16-element block of a row: its raw loaded form and its encoder (fp32
-// values through quant_block16; fp16 / bf16 kept as packed pairs for
+// values through quant_block16_rcp; fp16 / bf16 kept as packed pairs for
 // quant_block16_x2).
 template <typename T>
 struct Block16 {
@@ -2164,7 +2288,7 @@ struct Block16<float> {
   float v[16];
   __device__ __forceinline__ void load(const float* p) { In16<float>::load(p, v); }
   __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1) const {
-    return quant_block16(v, w0, w1);
+    return quant_block16_rcp(v, w0, w1);
   }
 };
 

@@ -41,3 +41,24 @@ def assert_close(got: np.ndarray, ref: np.ndarray, what: str = "") -> None:
         raise AssertionError(
             f"{what}: {n_bad} of {got.size} outputs outside rtol=atol=1e-3; "
             f"worst at {worst}: got {g} ref {r}")
+
+
+def near_midpoint_fp32(s, rng):
+    """fp32 values on, and a few ulps around, every e2m1 midpoint and grid
+    point times s, around every fp32 rounding boundary (t +- ulp(t)/2) * s,
+    and random ones up to 6.4 s, with both signs; plus zeros and tiny and
+    huge values."""
+    mids = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    grid = np.array([0.5, 1, 1.5, 2, 3, 4, 6], np.float32)
+    t = np.concatenate([mids, grid])
+    ulp = np.spacing(t)
+    centres = np.concatenate([t, t + ulp / 2, t - ulp / 2]).astype(
+        np.float64) * float(s)
+    centres = centres.astype(np.float32)
+    steps = np.arange(-3, 4, dtype=np.int64)
+    near = (centres.view(np.int32)[:, None] + steps[None, :]).astype(
+        np.int32).view(np.float32).ravel()
+    rand = (rng.random(64) * 6.4 * s).astype(np.float32)
+    v = np.concatenate([near, rand, [0.0, 1e-40, 1e-30, 3e38]]).astype(
+        np.float32)
+    return np.concatenate([v, -v])

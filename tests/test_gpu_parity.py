@@ -12,7 +12,8 @@ import torch
 import nvfp4_dual_gemm_b200 as dg
 from nvfp4_dual_gemm_b200 import _lib
 from oracle import nvfp4_oracle as O
-from tests.helpers import assert_close, data_tuple, to_device
+from tests.helpers import (assert_close, data_tuple, near_midpoint_fp32,
+                           to_device)
 
 pytestmark = pytest.mark.gpu
 
@@ -435,6 +436,128 @@ def test_activation_quantizer_dtypes_and_pitch(dtype, rows, k, pitch):
     torch.cuda.synchronize()
     assert none is None
     assert np.array_equal(gblk2.cpu().numpy(), gblk.cpu().numpy())
+
+
+def _finite_16bit_values(dtype):
+    """Every finite value of a 16-bit float type, as float32 (both zeros)."""
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.int16)
+    v = torch.from_numpy(bits).view(getattr(torch, dtype)).float().numpy()
+    return v[np.isfinite(v)]
+
+
+def _every_value_under_every_scale(dtype):
+    """Blocks of 16 that put every finite 16-bit v with s/16 <= |v| <= amax
+    (and +-0, and a few tiny negatives that round to -0) under every
+    positive e4m3 scale s: each block opens with an amax whose scale is s,
+    the largest 16-bit value with that scale.  Returns [rows, 1024] float32
+    values (exact in the 16-bit type); zero blocks pad the last row."""
+    vals = _finite_16bit_values(dtype)
+    pos = np.sort(vals[vals > 0])
+    with np.errstate(invalid="ignore", over="ignore"):
+        pos_sc = O.e4m3_encode(pos / np.float32(6.0))
+    blocks = []
+    for code in range(1, 0x7F):
+        amaxes = pos[pos_sc == code]
+        assert len(amaxes), f"no {dtype} amax has e4m3 scale {code:#x}"
+        amax = amaxes[-1]
+        s = O.e4m3_decode(np.uint8(code))
+        mag = np.abs(vals)
+        sel = vals[((mag >= s / 16) & (mag <= amax)) | (mag == 0)]
+        tiny = -pos[(pos < s / 8)][-4:]
+        members = np.concatenate([sel, tiny]).astype(np.float32)
+        pad = (-len(members)) % 15
+        members = np.concatenate([members, np.zeros(pad, np.float32)])
+        body = members.reshape(-1, 15)
+        head = np.full((body.shape[0], 1), amax, np.float32)
+        blocks.append(np.concatenate([head, body], axis=1))
+    x = np.concatenate(blocks).reshape(-1)
+    x = np.concatenate([x, np.zeros((-len(x)) % 1024, np.float32)])
+    return x.reshape(-1, 1024)
+
+
+def _check_quantised_rows(x, gc, gsf, gblk):
+    codes, sf = O.quantize(x)
+    gcodes = gc.cpu().numpy()
+    if not np.array_equal(gcodes, codes):
+        bad = np.argwhere(gcodes != codes)
+        first = bad[:8]
+        raise AssertionError(
+            f"{len(bad)} code bytes differ, first at {first.tolist()}: "
+            f"values {[x[r, 2 * c:2 * c + 2].tolist() for r, c in first]} "
+            f"gpu {[hex(gcodes[tuple(b)]) for b in first]} oracle "
+            f"{[hex(codes[tuple(b)]) for b in first]}")
+    assert np.array_equal(gsf.view(torch.uint8).cpu().numpy(), sf)
+    assert np.array_equal(gblk.cpu().numpy(), O.to_blocked(sf))
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16"])
+def test_activation_quantizer_every_value_under_every_scale(dtype):
+    # The 16-bit encoder replaces v / s by a two-term reciprocal product and
+    # the hardware e2m1 conversion; over every finite 16-bit v and every
+    # e4m3 scale it can meet (all midpoint ties v = t * s, -0, subnormal
+    # scales and values, saturation at 6 included) its codes and scales are
+    # bit-exact against the oracle's fp32 division.
+    x = _every_value_under_every_scale(dtype)
+    xt = torch.from_numpy(x).to(getattr(torch, dtype)).cuda()
+    assert np.array_equal(xt.float().cpu().numpy(), x)
+    gc, gsf, gblk = dg.quantize_nvfp4(xt)
+    torch.cuda.synchronize()
+    _check_quantised_rows(x, gc, gsf, gblk)
+
+
+def test_activation_quantizer_fp32_near_every_midpoint():
+    # fp32 rows: values on and a few ulps around every e2m1 midpoint, grid
+    # point and fp32 rounding boundary times every positive e4m3 scale s,
+    # in blocks opened by the largest fp32 amax whose scale is s (quotients
+    # up to ~6.4 saturate); plus blocks of huge and tiny values.  Bit-exact
+    # against the oracle's fp32 division.
+    rng = np.random.default_rng(23)
+    blocks = []
+    for code in range(1, 0x7F):
+        s = O.e4m3_decode(np.uint8(code)).astype(np.float32)
+        amax = np.float32(6 * s * 1.0625)
+        while O.e4m3_encode(np.float32(amax / np.float32(6))) != code:
+            amax = np.nextafter(amax, np.float32(0))
+        v = near_midpoint_fp32(s, rng)
+        v = v[np.abs(v) <= amax]
+        v = np.concatenate([v, np.zeros((-len(v)) % 15, np.float32)])
+        body = v.reshape(-1, 15)
+        blocks.append(np.concatenate(
+            [np.full((len(body), 1), amax, np.float32), body], axis=1))
+    blocks.append(np.array([[3e38, -3e38, 1e30, -1e-30, 1e-45, -0.0] +
+                            [2e38] * 10], np.float32))
+    blocks.append(np.array([[1e-40, -1e-40, 1e-45, -1e-45] + [0.0] * 12],
+                           np.float32))
+    x = np.concatenate(blocks).reshape(-1)
+    x = np.concatenate([x, np.zeros((-len(x)) % 1024, np.float32)])
+    x = x.reshape(-1, 1024)
+    gc, gsf, gblk = dg.quantize_nvfp4(torch.from_numpy(x).cuda())
+    torch.cuda.synchronize()
+    _check_quantised_rows(x, gc, gsf, gblk)
+
+
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+def test_activation_quantizer_nan_elements(dtype):
+    # A NaN element takes no part in its block's scale and encodes as a zero
+    # carrying the NaN's sign bit; the block's other elements and all other
+    # blocks are encoded as if the NaN were 0.
+    rng = np.random.default_rng(17)
+    x = rng.standard_normal((256, 1024)).astype(np.float32)
+    x[::3, 5] = np.nan
+    x[1::5, 40:43] = -np.nan
+    xt = torch.from_numpy(x).to(getattr(torch, dtype)).cuda()
+    ints = torch.int32 if dtype == "float32" else torch.int16
+    raw = xt.view(ints).cpu().numpy()
+    isnan = torch.isnan(xt).cpu().numpy()
+    clean = np.where(isnan, np.float32(0), xt.float().cpu().numpy())
+    codes, sf = O.quantize(clean)
+    want = O.unpack_codes(codes)
+    want[isnan] = np.where(raw[isnan] < 0, 8, 0)
+    gc, gsf, gblk = dg.quantize_nvfp4(xt)
+    torch.cuda.synchronize()
+    assert np.array_equal(O.unpack_codes(gc.cpu().numpy()), want)
+    assert np.array_equal(gsf.view(torch.uint8).cpu().numpy(), sf)
+    assert np.array_equal(gblk.cpu().numpy(), O.to_blocked(sf))
 
 
 @pytest.mark.parametrize("rows,k,pitch", [(300, 1024, 0), (1, 64, 0),

@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from oracle import nvfp4_oracle as O
+from tests.helpers import near_midpoint_fp32
 
 
 def test_e2m1_table_matches_ocp_values():
@@ -252,3 +253,88 @@ def test_packed_16bit_e2m1_encoding_equals_division():
                 want = O.e2m1_encode(v / sd)
             bad = np.flatnonzero(got != want)
             assert bad.size == 0, (b, kind, v[bad[:4]])
+
+
+@pytest.mark.skipif(np.finfo(np.longdouble).nmant < 63,
+                    reason="needs an 80-bit long double to model the fma")
+def test_reciprocal_product_e2m1_encoding_equals_division():
+    # The activation quantiser's form for fp16 / bf16 rows
+    # (quant_block16_x2): q = v * rh + RN(v * rl) rounded once (fma), with
+    # rh = 1/s rounded toward zero and rl = RN(RN(1 - s * rh) * rh), then
+    # e2m1 round-to-nearest-even.  The fma's single rounding is modelled in
+    # 80-bit long double (exact: the sum spans fewer than 64 bits).  Every
+    # finite fp16 and bf16 value, signed zeros included, under every
+    # positive e4m3 scale.
+    L = np.longdouble
+    bits = np.arange(65536, dtype=np.uint32)
+    bf16 = (bits << 16).view(np.float32)
+    f16 = bits.astype(np.uint16).view(np.float16).astype(np.float32)
+    for kind, vals in (("bf16", bf16), ("f16", f16)):
+        v = vals[np.isfinite(vals)]
+        vl = v.astype(L)
+        for b in range(1, 0x7F):
+            s = O.e4m3_decode(np.uint8(b)).astype(np.float32)
+            rh = np.float32(np.float32(1) / s)
+            if L(rh) * L(s) > 1:  # round toward zero
+                rh = np.nextafter(rh, np.float32(0))
+            rl = np.float32(np.float32(L(1) - L(s) * L(rh)) * rh)
+            assert rl >= 0
+            with np.errstate(over="ignore"):
+                p = (v * rl).astype(np.float32)
+                q = (vl * L(rh) + p.astype(L)).astype(np.float32)
+                want = O.e2m1_encode((v / s).astype(np.float32))
+            got = O.e2m1_encode(q)
+            bad = np.flatnonzero(got != want)
+            assert bad.size == 0, (kind, b, v[bad[:4]], q[bad[:4]])
+
+
+def _rn_f32(fr):
+    """A Fraction rounded once to the nearest float32 (ties to even),
+    overflowing to +-inf; returns a Python float holding that value."""
+    from fractions import Fraction
+    if fr == 0:
+        return 0.0
+    sign = -1.0 if fr < 0 else 1.0
+    a = abs(fr)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    if Fraction(2) ** e > a:
+        e -= 1
+    e = max(e, -126) - 23          # ulp exponent (subnormals: 2^-149)
+    scaled = a / Fraction(2) ** e
+    m, rem = divmod(scaled.numerator, scaled.denominator)
+    if 2 * rem > scaled.denominator or (2 * rem == scaled.denominator and
+                                        m & 1):
+        m += 1
+    if m * 2.0 ** e > 3.4028234663852886e38:
+        return sign * float("inf")
+    return sign * m * 2.0 ** e
+
+
+def test_reciprocal_product_e2m1_encoding_fp32():
+    # The same form for fp32 rows (quant_block16_rcp), with the fma's single
+    # rounding modelled exactly (fractions): values on and around every
+    # midpoint, grid point and fp32 rounding boundary times s, under every
+    # positive e4m3 scale, give the codes of e2m1(RN(v / s)).
+    from fractions import Fraction
+    rng = np.random.default_rng(9)
+    for b in range(1, 0x7F):
+        s = O.e4m3_decode(np.uint8(b)).astype(np.float32)
+        rh = np.float32(np.float32(1) / s)
+        if Fraction(float(rh)) * Fraction(float(s)) > 1:
+            rh = np.nextafter(rh, np.float32(0))
+        e = np.float32(_rn_f32(1 - Fraction(float(s)) * Fraction(float(rh))))
+        rl = np.float32(_rn_f32(Fraction(float(e)) * Fraction(float(rh))))
+        v = near_midpoint_fp32(s, rng)
+        q = np.array([_rn_f32(Fraction(float(x)) * Fraction(float(rh)) +
+                              Fraction(_rn_f32(Fraction(float(x)) *
+                                               Fraction(float(rl)))))
+                      for x in v], np.float32)
+        # v = +-0: v * rh has v's sign, RN(v * rl) v's sign times rl's, and
+        # their sum is -0 only when both are -0 (IEEE round to nearest)
+        neg0 = np.signbit(v) & ~np.signbit(rl)
+        q = np.where(v == 0, np.where(neg0, np.float32(-0.0), 0), q)
+        with np.errstate(over="ignore"):
+            want = O.e2m1_encode((v / s).astype(np.float32))
+        got = O.e2m1_encode(q)
+        bad = np.flatnonzero(got != want)
+        assert bad.size == 0, (b, v[bad[:4]], q[bad[:4]])
