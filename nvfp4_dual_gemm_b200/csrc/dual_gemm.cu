@@ -539,23 +539,29 @@ __device__ __forceinline__ uint32_t e2m1_scaled8(const uint32_t (&x)[8],
 // kernel; fp32 v are tested on and around every midpoint and boundary.
 // (A single rounded reciprocal, q = RN(v * RN(1/s)), is not enough: ties
 // at 1.25, 2.5 and 5 under scales of mantissa 1.875 round the wrong way.)
-__device__ __forceinline__ uint8_t encode_rcp16(float amax,
-                                                const uint32_t (&x)[16],
-                                                uint32_t& w0, uint32_t& w1) {
-  const __nv_fp8_storage_t sb =
-      __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+// (rh, rl) depend on the scale byte alone, so the kernel reads them from a
+// 128-entry table in shared memory (rcp_pair fills it); a zero scale has
+// (0, 0) and its codes are cleared by a select.
+__device__ __forceinline__ float2 rcp_pair(uint32_t sb) {
   const float sd =
       __half2float(__half(__nv_cvt_fp8_to_halfraw(sb, __NV_E4M3)));
-  w0 = 0;
-  w1 = 0;
-  if (sd > 0.f) {
-    const float rh = __frcp_rz(sd);
-    const float rl = __fmul_rn(__fmaf_rn(-sd, rh, 1.0f), rh);
-    const uint32_t(&xa)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x);
-    const uint32_t(&xb)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x + 8);
-    w0 = e2m1_scaled8(xa, rh, rl);
-    w1 = e2m1_scaled8(xb, rh, rl);
-  }
+  if (!(sd > 0.f)) return make_float2(0.f, 0.f);
+  const float rh = __frcp_rz(sd);
+  return make_float2(rh, __fmul_rn(__fmaf_rn(-sd, rh, 1.0f), rh));
+}
+__device__ __forceinline__ uint8_t encode_rcp16(float amax,
+                                                const uint32_t (&x)[16],
+                                                uint32_t& w0, uint32_t& w1,
+                                                const float2* rtab) {
+  const __nv_fp8_storage_t sb =
+      __nv_cvt_float_to_fp8(amax / 6.0f, __NV_SATFINITE, __NV_E4M3);
+  const float2 r = rtab[sb & 0x7F];  // amax >= 0: the sign bit is clear
+  const uint32_t(&xa)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x);
+  const uint32_t(&xb)[8] = *reinterpret_cast<const uint32_t(*)[8]>(x + 8);
+  const uint32_t a = e2m1_scaled8(xa, r.x, r.y);
+  const uint32_t b = e2m1_scaled8(xb, r.x, r.y);
+  w0 = sb != 0 ? a : 0u;
+  w1 = sb != 0 ? b : 0u;
   return static_cast<uint8_t>(sb);
 }
 
@@ -565,7 +571,8 @@ __device__ __forceinline__ uint8_t encode_rcp16(float amax,
 template <typename H2>
 __device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
                                                     uint32_t& w0,
-                                                    uint32_t& w1) {
+                                                    uint32_t& w1,
+                                                    const float2* rtab) {
   using Ops = Half2Ops<H2>;
   uint32_t km = p[0] & 0x7FFF7FFFu;
 #pragma unroll
@@ -578,14 +585,15 @@ __device__ __forceinline__ uint8_t quant_block16_x2(const uint32_t (&p)[8],
     x[2 * i] = __float_as_uint(Ops::lo(p[i]));
     x[2 * i + 1] = __float_as_uint(Ops::hi(p[i]));
   }
-  return encode_rcp16(Ops::lo(key), x, w0, w1);
+  return encode_rcp16(Ops::lo(key), x, w0, w1, rtab);
 }
 
 // The activation quantiser's fp32 block form: amax as the largest |v| bit
 // pattern, then encode_rcp16; a block holding a NaN goes to quant_block16.
 __device__ __forceinline__ uint8_t quant_block16_rcp(const float (&v)[16],
                                                      uint32_t& w0,
-                                                     uint32_t& w1) {
+                                                     uint32_t& w1,
+                                                     const float2* rtab) {
   uint32_t x[16];
   uint32_t km = 0;
 #pragma unroll
@@ -594,7 +602,7 @@ __device__ __forceinline__ uint8_t quant_block16_rcp(const float (&v)[16],
     km = max(km, x[i] & 0x7FFFFFFFu);
   }
   if (km > 0x7F800000u) return quant_block16(v, w0, w1);
-  return encode_rcp16(__uint_as_float(km), x, w0, w1);
+  return encode_rcp16(__uint_as_float(km), x, w0, w1, rtab);
 }
 
 // Where the epilogue of one tile row writes its outputs: fp16 C, or NVFP4
@@ -2277,20 +2285,64 @@ struct Block16 {
     raw[0] = a.x; raw[1] = a.y; raw[2] = a.z; raw[3] = a.w;
     raw[4] = b.x; raw[5] = b.y; raw[6] = b.z; raw[7] = b.w;
   }
-  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1) const {
+  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1,
+                                            const float2* rtab) const {
     using H2 = typename std::conditional<std::is_same<T, __half>::value,
                                          __half2, __nv_bfloat162>::type;
-    return quant_block16_x2<H2>(raw, w0, w1);
+    return quant_block16_x2<H2>(raw, w0, w1, rtab);
   }
 };
 template <>
 struct Block16<float> {
   float v[16];
   __device__ __forceinline__ void load(const float* p) { In16<float>::load(p, v); }
-  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1) const {
-    return quant_block16_rcp(v, w0, w1);
+  __device__ __forceinline__ uint8_t encode(uint32_t& w0, uint32_t& w1,
+                                            const float2* rtab) const {
+    return quant_block16_rcp(v, w0, w1, rtab);
   }
 };
+
+// One unit of the activation quantiser: the 1024-element run at c0 - 16 lane
+// of row r (rows up to the next multiple of 128 included: their scales are
+// written as zero).
+template <typename T>
+__device__ __forceinline__ void quantize_unit(
+    const T* __restrict__ X, int rows, int K, long long ldx,
+    uint8_t* __restrict__ codes, uint8_t* __restrict__ sf_plain,
+    uint8_t* __restrict__ sf_blocked, int groups, int lane, int r, int c0,
+    const float2* rtab) {
+  Block16<T> blk[2];
+  bool act[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    act[h] = c0 + 512 * h < K;
+    if (act[h] && r < rows) blk[h].load(X + (size_t)r * ldx + c0 + 512 * h);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int c = c0 + 512 * h;
+    uint32_t sb = 0;
+    if (act[h] && r < rows) {
+      uint32_t w0, w1;
+      sb = blk[h].encode(w0, w1, rtab);
+      *reinterpret_cast<uint2*>(codes + (size_t)r * (K / 2) + c / 2) =
+          make_uint2(w0, w1);
+    }
+    const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 1);
+    const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 2);
+    const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 3);
+    if ((lane & 3) == 0 && act[h]) {
+      const uint32_t word = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
+      const int g = c / 64;
+      if (sf_plain != nullptr && r < rows)
+        *reinterpret_cast<uint32_t*>(sf_plain + (size_t)r * (K / 16) +
+                                     (size_t)g * 4) = word;
+      *reinterpret_cast<uint32_t*>(
+          sf_blocked + ((size_t)(r / 128) * groups + g) * kSfAtomBytes +
+          (r % 32) * 16 + ((r % 128) / 32) * 4) = word;
+    }
+  }
+}
 
 template <typename T>
 __global__ void __launch_bounds__(256)
@@ -2298,44 +2350,44 @@ __global__ void __launch_bounds__(256)
                          uint8_t* __restrict__ codes,
                          uint8_t* __restrict__ sf_plain,
                          uint8_t* __restrict__ sf_blocked) {
+  __shared__ float2 rtab[128];  // (rh, rl) of each e4m3 scale byte
+  if (threadIdx.x < 128) rtab[threadIdx.x] = rcp_pair(threadIdx.x);
+  __syncthreads();
   const int groups = K / 64;
   const int chunks = (K + 1023) / 1024;  // 1024-element runs per row
-  const long long units = (long long)((rows + 127) / 128) * 128 * chunks;
   const int lane = threadIdx.x & 31;
-  for (long long u = (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-       u < units; u += (long long)gridDim.x * (blockDim.x / 32)) {
-    const int r = static_cast<int>(u / chunks);
-    const int c0 = static_cast<int>(u - (long long)r * chunks) * 1024 + 16 * lane;
-    Block16<T> blk[2];
-    bool act[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      act[h] = c0 + 512 * h < K;
-      if (act[h] && r < rows) blk[h].load(X + (size_t)r * ldx + c0 + 512 * h);
+  // unit u = row r, run ch (u = r * chunks + ch); each warp starts at its
+  // global warp index and strides by the grid's warp count
+  const long long u0 =
+      (long long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const long long stride = (long long)gridDim.x * (blockDim.x / 32);
+  if (sizeof(T) == 2) {
+    // 16-bit rows: (r, ch) advanced by (dr, dch) per step, one 64-bit
+    // division per warp instead of one per unit (8192 x 7168 bf16, eager:
+    // 31.4 instead of 33.1 us; the fp32 rows measured slower this way)
+    const long long rows_pad = (rows + 127) / 128 * 128ll;
+    long long r = u0 / chunks;
+    int ch = static_cast<int>(u0 - r * chunks);
+    const long long dr = stride / chunks;
+    const int dch = static_cast<int>(stride - dr * chunks);
+    for (; r < rows_pad; r += dr, ch += dch) {
+      if (ch >= chunks) {
+        ch -= chunks;
+        if (++r >= rows_pad) break;
+      }
+      quantize_unit<T>(X, rows, K, ldx, codes, sf_plain, sf_blocked, groups,
+                       lane, static_cast<int>(r), ch * 1024 + 16 * lane,
+                       rtab);
     }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int c = c0 + 512 * h;
-      uint32_t sb = 0;
-      if (act[h] && r < rows) {
-        uint32_t w0, w1;
-        sb = blk[h].encode(w0, w1);
-        *reinterpret_cast<uint2*>(codes + (size_t)r * (K / 2) + c / 2) =
-            make_uint2(w0, w1);
-      }
-      const uint32_t s1 = __shfl_down_sync(0xffffffffu, sb, 1);
-      const uint32_t s2 = __shfl_down_sync(0xffffffffu, sb, 2);
-      const uint32_t s3 = __shfl_down_sync(0xffffffffu, sb, 3);
-      if ((lane & 3) == 0 && act[h]) {
-        const uint32_t word = sb | (s1 << 8) | (s2 << 16) | (s3 << 24);
-        const int g = c / 64;
-        if (sf_plain != nullptr && r < rows)
-          *reinterpret_cast<uint32_t*>(sf_plain + (size_t)r * (K / 16) +
-                                       (size_t)g * 4) = word;
-        *reinterpret_cast<uint32_t*>(
-            sf_blocked + ((size_t)(r / 128) * groups + g) * kSfAtomBytes +
-            (r % 32) * 16 + ((r % 128) / 32) * 4) = word;
-      }
+  } else {
+    const long long units = (long long)((rows + 127) / 128) * 128 * chunks;
+    for (long long u = u0; u < units; u += stride) {
+      const int r = static_cast<int>(u / chunks);
+      quantize_unit<T>(X, rows, K, ldx, codes, sf_plain, sf_blocked, groups,
+                       lane, r,
+                       static_cast<int>(u - (long long)r * chunks) * 1024 +
+                           16 * lane,
+                       rtab);
     }
   }
 }
