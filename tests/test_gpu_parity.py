@@ -536,6 +536,23 @@ def test_activation_quantizer_fp32_near_every_midpoint():
     _check_quantised_rows(x, gc, gsf, gblk)
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_activation_quantizer_many_units_per_warp(dtype):
+    # 2001 ragged rows of K = 7104 (seven 1024-element runs, the last one
+    # partial) inside a wider pitch: 14,336 units for at most 9,472 warps, so
+    # warps step through several (row, run) pairs and the run index wraps
+    # into the next row; bit-exact against the oracle.
+    rng = np.random.default_rng(41)
+    rows, k, pitch = 2001, 7104, 7168
+    x = (rng.standard_normal((rows, pitch)) *
+         rng.choice([1e-3, 1.0, 40.0], size=(rows, 1))).astype(np.float32)
+    xt = torch.from_numpy(x).to(getattr(torch, dtype)).cuda()[:, :k]
+    x32 = xt.float().cpu().numpy()
+    gc, gsf, gblk = dg.quantize_nvfp4(xt)
+    torch.cuda.synchronize()
+    _check_quantised_rows(x32, gc, gsf, gblk)
+
+
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
 def test_activation_quantizer_nan_elements(dtype):
     # A NaN element takes no part in its block's scale and encodes as a zero
