@@ -2419,8 +2419,15 @@ __global__ void __launch_bounds__(256)
 // consecutive 4-byte words of a row), the blocked side as whole 512-byte
 // atoms (the 32 atoms of a row block and 32 consecutive groups are
 // contiguous), so both sides are coalesced.  Padding rows of the blocked
-// buffer are written as zero.
+// buffer are written as zero.  The shared tile is held in the blocked order,
+// tile[group][word] with row r at word 4 (r % 32) + r / 32 and a row pitch
+// of 129 words: the plain side (consecutive threads: consecutive groups of
+// one row) and the blocked side (consecutive words of one atom) both touch
+// 32 different banks per warp.  (With tile[row][group], rows r, r + 32,
+// r + 64, r + 96 of one atom word run fell on one bank.)
 constexpr int kCvtGroups = 32;
+constexpr int kCvtPitch = 129;
+__device__ __forceinline__ int cvt_word(int r) { return 4 * (r & 31) + (r >> 5); }
 // words each of the 256 threads moves: a fixed count, so that every load of a
 // thread is issued before the first one is used
 constexpr int kCvtIters = 128 * kCvtGroups / 256;
@@ -2429,7 +2436,7 @@ __global__ void __launch_bounds__(256)
     scales_to_blocked_kernel(const uint8_t* __restrict__ plain, int rows,
                              int groups, long long ld,
                              uint8_t* __restrict__ blocked) {
-  __shared__ uint32_t tile[128][kCvtGroups + 1];
+  __shared__ uint32_t tile[kCvtGroups * kCvtPitch];
   const int rb = blockIdx.y;
   const int g0 = blockIdx.x * kCvtGroups;
   const int ng = min(kCvtGroups, groups - g0);
@@ -2447,22 +2454,21 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int j = 0; j < kCvtIters; ++j) {
     const int i = threadIdx.x + j * 256;
-    if (i < 128 * ng) tile[i / ng][i % ng] = v[j];
+    const int r = i / ng, gg = i - r * ng;
+    if (i < 128 * ng) tile[gg * kCvtPitch + cvt_word(r)] = v[j];
   }
   __syncthreads();
   uint32_t* out = reinterpret_cast<uint32_t*>(blocked) +
                   ((size_t)rb * groups + g0) * (kSfAtomBytes / 4);
-  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
-    const int gg = i >> 7, w = i & 127;  // word w of atom gg: row (w/4)+32(w%4)
-    out[i] = tile[(w >> 2) + 32 * (w & 3)][gg];
-  }
+  for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x)
+    out[i] = tile[(i >> 7) * kCvtPitch + (i & 127)];  // word i % 128 of atom i / 128
 }
 
 __global__ void __launch_bounds__(256)
     scales_from_blocked_kernel(const uint8_t* __restrict__ blocked, int rows,
                                int groups, long long ld,
                                uint8_t* __restrict__ plain) {
-  __shared__ uint32_t tile[128][kCvtGroups + 1];
+  __shared__ uint32_t tile[kCvtGroups * kCvtPitch];
   const int rb = blockIdx.y;
   const int g0 = blockIdx.x * kCvtGroups;
   const int ng = min(kCvtGroups, groups - g0);
@@ -2477,8 +2483,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int j = 0; j < kCvtIters; ++j) {
     const int i = threadIdx.x + j * 256;
-    const int gg = i >> 7, w = i & 127;
-    if (i < 128 * ng) tile[(w >> 2) + 32 * (w & 3)][gg] = v[j];
+    if (i < 128 * ng) tile[(i >> 7) * kCvtPitch + (i & 127)] = v[j];
   }
   __syncthreads();
   for (int i = threadIdx.x; i < 128 * ng; i += blockDim.x) {
@@ -2486,7 +2491,7 @@ __global__ void __launch_bounds__(256)
     const int row = rb * 128 + r;
     if (row < rows)
       *reinterpret_cast<uint32_t*>(plain + (size_t)row * ld + 4 * (g0 + gg)) =
-          tile[r][gg];
+          tile[gg * kCvtPitch + cvt_word(r)];
   }
 }
 
