@@ -212,7 +212,8 @@ def _bf16(x):
 
 
 def test_packed_16bit_e2m1_encoding_equals_division():
-    # The CUDA quantiser's form for fp16 / bf16 data (quant_block16_x2):
+    # The compare form for fp16 / bf16 data (quant_block16_x2_cmp: the
+    # NVFP4-output epilogue, and blocks holding a NaN in the quantiser):
     # the midpoint products t * s rounded to the 16-bit type (exact: at most
     # 7 significant bits, within range) and compared with |v| as 16-bit
     # values, the >= midpoints as > the 16-bit value just below.  Every fp16
