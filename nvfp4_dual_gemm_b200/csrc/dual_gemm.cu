@@ -2321,9 +2321,9 @@ struct Block16<float> {
   }
 };
 
-// One unit of the activation quantiser: the 1024-element run at c0 - 16 lane
-// of row r (rows up to the next multiple of 128 included: their scales are
-// written as zero).
+// One unit of the activation quantiser: the 1024-element run of row r that
+// starts at element c0 - 16 lane (rows up to the next multiple of 128
+// included: their scales are written as zero).
 template <typename T>
 __device__ __forceinline__ void quantize_unit(
     const T* __restrict__ X, int rows, int K, long long ldx,
@@ -2386,7 +2386,7 @@ __global__ void __launch_bounds__(256)
     // 16-bit rows: (r, ch) advanced by (dr, dch) per step, one 64-bit
     // division per warp instead of one per unit (8192 x 7168 bf16, eager:
     // 31.4 instead of 33.1 us; the fp32 rows measured slower this way)
-    const long long rows_pad = (rows + 127) / 128 * 128ll;
+    const long long rows_pad = ((long long)rows + 127) / 128 * 128;
     long long r = u0 / chunks;
     int ch = static_cast<int>(u0 - r * chunks);
     const long long dr = stride / chunks;
@@ -2401,7 +2401,7 @@ __global__ void __launch_bounds__(256)
                        rtab);
     }
   } else {
-    const long long units = (long long)((rows + 127) / 128) * 128 * chunks;
+    const long long units = ((long long)rows + 127) / 128 * 128 * chunks;
     for (long long u = u0; u < units; u += stride) {
       const int r = static_cast<int>(u / chunks);
       quantize_unit<T>(X, rows, K, ldx, codes, sf_plain, sf_blocked, groups,
@@ -3844,7 +3844,7 @@ int nvfp4_quantize_rows(const void* X, int dtype, int rows, int K,
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const long long units =
-      (long long)((rows + 127) / 128) * 128 * ((K + 1023) / 1024);
+      ((long long)rows + 127) / 128 * 128 * ((K + 1023) / 1024);
   const int threads = 256;
   const long long want = (units + threads / 32 - 1) / (threads / 32);
   const int blocks = (int)std::min<long long>(want, (long long)sms * 8);
